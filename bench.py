@@ -1,0 +1,419 @@
+"""Benchmark: greedy batch-1 decode of the Qwen2.5-0.5B-architecture int4 model (config 0).
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl enx|reference]
+
+A step is one decode token: the whole decoder (24 layers of int4 projections, f16-KV GQA
+attention), the tied int8 head and the sampler, for one sequence, at positions 32..95 (a
+32-id prompt decoded out to 64 tokens, as config 0 specifies; longer runs restart the
+sequence every 64 tokens, the re-prefill being outside the timed events).  Weights are seeded
+random-init (normal(0, 0.02), norm gains 1), quantised with the reference's scheme; the prompt
+is uniform random ids.  Each step streams all 351 MB of weights, more than the 126 MB L2, so
+consecutive steps cannot reuse cached weights.
+
+value: device-fed loop (enx_decode_loop: the sampled id feeds the next step on the GPU), CUDA
+events on the context stream, max over ranks.  e2e: the public per-token API
+(Session.decode_step -> enx_decode_step), which copies each step's inputs host->device from
+pinned memory and reads the id back, timed with events around the same steps.
+
+N > 1: one independent replica per GPU (independent sequences are data-parallel; the path has no
+exchange step), weak scaling.  --impl reference times the CPU restatement of the reference's
+path (oracle/, the reference itself is TypeScript/WebGPU and cannot run here) on rank 0.
+"""
+
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import statistics
+import subprocess
+import sys
+import threading
+import time
+from pathlib import Path
+
+import numpy as np
+
+ROOT = Path(__file__).resolve().parent
+sys.path.insert(0, str(ROOT))
+
+from enargeia_b200.checkpoint import QWEN2_0_5B, build_model_file  # noqa: E402
+
+PROMPT = 32
+GEN = 64            # config 0 decodes 64 tokens per sequence
+SEED = 20251201     # model seed
+METRIC = "decode tok/s (greedy, batch 1, Qwen2.5-0.5B int4 + int8 head, ctx 32..96)"
+MODEL_DIR = Path(os.environ.get("ENX_MODEL_DIR", "/tmp/enx_models"))
+
+
+def model_path() -> Path:
+    return MODEL_DIR / f"qwen2.5-0.5b-random-s{SEED}-q4q8.enargeia"
+
+
+def algorithmic_bytes():
+    """Bytes one decode step must move at the reference layout: every weight range once
+    (packed + scales + zeros + norms + biases), plus the per-step KV reads."""
+    from enargeia_b200.format import read_enargeia
+
+    f = read_enargeia(model_path())
+    weights = sum(t.nbytes for t in f.tensors.values())
+    head = f.quant("model.embed_tokens.weight")
+    return f, weights, head.nbytes
+
+
+# ---------------------------------------------------------------------------------------------
+# clocks
+
+
+class ClockSampler:
+    def __init__(self, device: int):
+        self.device = device
+        self.proc = None
+        self.lines = []
+        self.t = None
+
+    def __enter__(self):
+        q = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+             "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+             "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+        try:
+            self.proc = subprocess.Popen(["nvidia-smi", f"--query-gpu={q}", "--format=csv,noheader,nounits",
+                                          "-lms", "100", "-i", str(self.device)], stdout=subprocess.PIPE,
+                                         stderr=subprocess.DEVNULL, text=True)
+            self.t = threading.Thread(target=self._read, daemon=True)
+            self.t.start()
+        except FileNotFoundError:
+            self.proc = None
+        time.sleep(0.3)
+        return self
+
+    def _read(self):
+        for line in self.proc.stdout:
+            self.lines.append(line.strip())
+
+    def __exit__(self, *exc):
+        time.sleep(0.25)
+        if self.proc:
+            self.proc.terminate()
+            try:
+                self.proc.wait(timeout=5)
+            except subprocess.TimeoutExpired:
+                self.proc.kill()
+        if self.t:
+            self.t.join(timeout=2)
+
+    def summary(self):
+        rows = []
+        for ln in self.lines:
+            parts = [p.strip() for p in ln.split(",")]
+            if len(parts) < 9:
+                continue
+            try:
+                rows.append((float(parts[1]), float(parts[2]), parts[5:9]))
+            except ValueError:
+                continue
+        if not rows:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["unsampled"], "samples": 0}
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        reasons = sorted({names[i] for _, _, flags in rows for i, f in enumerate(flags) if f.lower() == "active"})
+        loaded = [r[0] for r in rows if r[0] > 0.5 * r[1]] or [r[0] for r in rows]
+        return {"sm_mhz": statistics.median(loaded), "sm_max_mhz": max(r[1] for r in rows), "reasons": reasons,
+                "samples": len(rows)}
+
+
+# ---------------------------------------------------------------------------------------------
+# GPU arm
+
+
+def run_enx(args, rank, world, local_rank):
+    import torch
+    import torch.distributed as dist
+
+    from enargeia_b200 import build, kernels as K
+    from enargeia_b200.session import GREEDY, Model, Session
+
+    build.build()
+    torch.cuda.set_device(local_rank)
+    dev = torch.device("cuda", local_rank)
+    if local_rank == 0:
+        build_model_file(QWEN2_0_5B, SEED, model_path())
+    if world > 1:
+        dist.barrier()
+    else:
+        build_model_file(QWEN2_0_5B, SEED, model_path())
+    f, weight_bytes, head_bytes = algorithmic_bytes()
+    cfg = QWEN2_0_5B
+
+    ctx = PROMPT + GEN + 1
+    m = Model(cfg, local_rank).load(model_path()).kv_alloc(ctx, 1)
+    stream = torch.cuda.ExternalStream(m.stream_handle(), device=dev)
+    prompt = [int(v) for v in np.random.default_rng(1000 + rank).integers(0, cfg.vocab, PROMPT)]
+    greedy = [GREEDY]
+
+    def restart():
+        m.reset(0)
+        m.prefill(0, prompt)
+        return m.sample_prefill(0, GREEDY, 0.5)
+
+    def segments(total):
+        while total > 0:
+            n = min(GEN - 1, total)
+            yield n
+            total -= n
+
+    # warm-up: W device-fed steps and W public-API steps (graphs captured, clocks up)
+    first = restart()
+    m.decode_loop([first], greedy, np.full(max(args.warmup, 1), 0.5, np.float32), max(args.warmup, 1))
+    first = restart()
+    s = Session(m, GREEDY)
+    tok = first
+    for _ in range(max(args.warmup, 1)):
+        tok = s.decode_step(tok)
+    torch.cuda.synchronize()
+
+    def barrier():
+        if world > 1:
+            dist.barrier()
+        torch.cuda.synchronize()
+
+    def max_over_ranks(x):
+        if world == 1:
+            return x
+        t = torch.tensor([x], dtype=torch.float64, device=dev)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        return float(t.item())
+
+    # --- value: device-fed loop -----------------------------------------------------------
+    loop_ids = []
+    ms_total = 0.0
+    with ClockSampler(local_rank) as clocks:
+        barrier()
+        for n in segments(args.steps):
+            first = restart()
+            torch.cuda.synchronize()
+            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            e0.record(stream)
+            m.decode_loop([first], greedy, np.full(n, 0.5, np.float32), n, sync=False)
+            e1.record(stream)
+            m.synchronize()
+            ms_total += e0.elapsed_time(e1)
+            loop_ids.append([first] + list(m.loop_ids(n)[:, 0]))
+        barrier()
+    launches_per_step = m.step_launches()
+    ms_total = max_over_ranks(ms_total)
+    value = world * args.steps / (ms_total / 1e3)
+
+    # --- e2e: public per-token API ---------------------------------------------------------
+    e2e_ms = 0.0
+    api_ids = []
+    barrier()
+    for n in segments(args.steps):
+        first = restart()
+        sess = Session(m, GREEDY)
+        torch.cuda.synchronize()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        ids = [first]
+        e0.record(stream)
+        tok = first
+        for _ in range(n):
+            tok = sess.decode_step(tok)
+            ids.append(tok)
+        e1.record(stream)
+        torch.cuda.synchronize()
+        e2e_ms += e0.elapsed_time(e1)
+        api_ids.append(ids)
+    barrier()
+    e2e_ms = max_over_ranks(e2e_ms)
+    e2e_value = world * args.steps / (e2e_ms / 1e3)
+    consistent = api_ids == loop_ids
+
+    # --- roofline: the tied int8 head, the largest kernel of the step ------------------------
+    tv = m.tensor_view("model.embed_tokens.weight")
+    x = torch.randn(cfg.hidden, device=dev)
+    logits = torch.empty(cfg.vocab, device=dev)
+    flush = torch.empty(256 << 20, dtype=torch.uint8, device=dev)  # 256 MB > 126 MB L2
+    import ctypes as C
+
+    from enargeia_b200._lib import EmbeddingDims, call
+
+    d = EmbeddingDims(1, cfg.hidden, 0, cfg.vocab, 64, cfg.hidden // 64, 0, 0, 0, 0, 0, 0)
+    head_ms = []
+    cur = torch.cuda.current_stream()
+    for i in range(args.warmup + 20):
+        flush.zero_()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record(cur)
+        call("enx_lm_head_q8", C.c_void_p(x.data_ptr()), C.c_void_p(tv["packed"]), C.c_void_p(tv["scales"]),
+             C.c_void_p(tv["zeros"]), C.c_void_p(logits.data_ptr()), C.byref(d), C.c_void_p(cur.cuda_stream))
+        e1.record(cur)
+        torch.cuda.synchronize()
+        if i >= args.warmup:
+            head_ms.append(e0.elapsed_time(e1))
+    head_algo = head_bytes + cfg.hidden * 4 + cfg.vocab * 4
+    head_avg = sum(head_ms) / len(head_ms)
+    peaks = {}
+    try:
+        peaks = json.loads((ROOT / "MEASURED_PEAKS.json").read_text())
+    except (OSError, ValueError):
+        pass
+    hbm = float(peaks.get("hbm_gbs", 6650.0))
+    peak_src = "measured" if "hbm_gbs" in peaks else "fallback"
+    achieved = head_algo / (head_avg / 1e3) / 1e9
+    step_bytes = weight_bytes  # plus KV reads, added below at the mean position
+    mean_pos = PROMPT + GEN / 2
+    kv_bytes = cfg.layers * 2 * int(mean_pos) * cfg.kv_dim * 2
+    step_achieved = (step_bytes + kv_bytes) / (ms_total / args.steps / 1e3) / 1e9
+
+    traffic = None
+    tf = ROOT / "profiles" / "lm_head_q8_traffic.json"
+    if tf.exists():
+        traffic = json.loads(tf.read_text()).get("dram_bytes_per_launch")
+
+    out = {
+        "metric": METRIC,
+        "value": round(value, 2),
+        "unit": "tok/s",
+        "n_gpus": world,
+        "steps": args.steps,
+        "warmup": args.warmup,
+        "ms_per_step": round(ms_total / args.steps, 5),
+        "higher_is_better": True,
+        "scaling": "weak",
+        "vs_baseline": None,
+        "dtype": "int4/int8 weights x f32 activations, f32 accumulate, f16 KV",
+        "data": "synthetic: seeded random-init weights normal(0,0.02) quantised int4 + int8 head; uniform random prompt ids",
+        "config": {"workload": "config 0: greedy batch-1 decode, 24 layers, hidden 896, 14q/2kv x 64, FFN 4864, "
+                               "vocab 151936, prompt 32 -> 64 new tokens, f16 KV",
+                   "batch_per_gpu": 1, "parallelism": f"replicas x{world} (independent sequences)",
+                   "l2": "inputs larger than L2: 351 MB of weights streamed per step vs 126 MB L2",
+                   "step_bytes": step_bytes + kv_bytes},
+        "e2e": {"value": round(e2e_value, 2), "unit": "tok/s", "h2d_bytes_per_step": 116, "d2h_bytes_per_step": 4,
+                "api": "Session.decode_step -> enx_decode_step (pinned step block in, 4-byte id out)"},
+        "roofline": {"kernel": "k_head<8,1> (final RMSNorm + tied int8 LM head, 151936x896)", "bound": "hbm",
+                     "achieved": round(achieved, 1), "peak": hbm, "unit": "GB/s",
+                     "frac": round(achieved / hbm, 4), "traffic": traffic,
+                     "algorithmic_bytes_per_launch": head_algo, "launch_us": round(head_avg * 1e3, 2),
+                     "peak_source": f"{peak_src} MEASURED_PEAKS.json hbm_gbs (burst copy)"},
+        "step_roofline": {"bound": "hbm", "bytes_per_step": step_bytes + kv_bytes,
+                          "achieved": round(step_achieved, 1), "peak": hbm, "unit": "GB/s",
+                          "frac": round(step_achieved / hbm, 4)},
+        "gpu_launches": launches_per_step * args.steps,
+        "launches_per_step": launches_per_step,
+        "ids_consistent_loop_vs_api": consistent,
+        "clocks": clocks.summary(),
+    }
+    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+        out["cpu_baseline"] = cpu_baseline(f, prompt, budget_s=args.cpu_budget)
+    if rank == 0:
+        print(json.dumps(out), flush=True)
+    m.close()
+
+
+# ---------------------------------------------------------------------------------------------
+# CPU legs (the oracle: a restatement of the reference's CPU path; the reference itself is
+# TypeScript and cannot run on this box)
+
+
+def cpu_baseline(f, prompt, budget_s=15.0, threads=None):
+    from oracle import oracle as O
+
+    O.build()
+    if threads:
+        O.set_threads(threads)
+    cores = O.max_threads()
+    om = O.OracleModel(f, QWEN2_0_5B, PROMPT + GEN + 1)
+    logits = om.prefill(prompt)
+    tok = O.argmax(logits)
+    n = 0
+    t0 = time.perf_counter()
+    while n < GEN - 1 and (n < 2 or time.perf_counter() - t0 < budget_s):
+        logits = om.decode(tok)
+        tok = O.argmax(logits)
+        n += 1
+    dt = time.perf_counter() - t0
+    return {"value": round(n / dt, 4), "unit": "tok/s", "cores": cores, "kind": "port",
+            "sample": f"{n} greedy decode steps of config 0 after a 32-id prefill (oracle/enx_oracle.cpp, "
+                      f"f64 accumulate, OpenMP over output rows), {dt:.1f} s"}
+
+
+def run_reference(args, rank, world):
+    if rank != 0:
+        return
+    from oracle import oracle as O
+
+    O.build()
+    build_model_file(QWEN2_0_5B, SEED, model_path())
+    from enargeia_b200.format import read_enargeia
+
+    f = read_enargeia(model_path())
+    cores = O.max_threads()
+    prompt = [int(v) for v in np.random.default_rng(1000).integers(0, QWEN2_0_5B.vocab, PROMPT)]
+    om = O.OracleModel(f, QWEN2_0_5B, PROMPT + GEN + 1)
+
+    def restart():
+        om.reset()
+        return O.argmax(om.prefill(prompt))
+
+    tok = restart()
+    for _ in range(args.warmup):
+        tok = O.argmax(om.decode(tok))
+    total = 0.0
+    done = 0
+    while done < args.steps:
+        n = min(GEN - 1, args.steps - done)
+        tok = restart()
+        t0 = time.perf_counter()
+        for _ in range(n):
+            tok = O.argmax(om.decode(tok))
+        total += time.perf_counter() - t0
+        done += n
+    value = args.steps / total
+    print(json.dumps({
+        "impl": "reference", "metric": METRIC, "value": round(value, 4), "unit": "tok/s", "n_gpus": world,
+        "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(total / args.steps * 1e3, 3),
+        "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f64 accumulate / f32 store",
+        "data": "synthetic: same seeded random-init model and prompt as the enx arm",
+        "config": {"workload": "config 0: greedy batch-1 decode (CPU restatement of the reference path)"},
+        "cpu_baseline": {"value": round(value, 4), "unit": "tok/s", "cores": cores, "kind": "port",
+                         "sample": f"{args.steps} decode steps, host threads {cores}; the reference's own path is "
+                                   "TypeScript/WebGPU (no node, browser or graphics stack on this box)"},
+        "e2e": {"value": round(value, 4), "unit": "tok/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+    }), flush=True)
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=2016)
+    ap.add_argument("--warmup", type=int, default=8)
+    ap.add_argument("--impl", choices=["enx", "reference"], default="enx")
+    ap.add_argument("--cpu-budget", type=float, default=15.0)
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    args = ap.parse_args()
+    if args.warmup < 3:
+        raise SystemExit("--warmup must be at least 3")
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local_rank = int(os.environ.get("LOCAL_RANK", "0"))
+    if args.impl == "reference":
+        if args.steps > 256:
+            args.steps = 64  # the CPU leg times a bounded sample (about 0.3-1 s per step)
+        run_reference(args, rank, world)
+        return
+    if world > 1:
+        import torch
+        import torch.distributed as dist
+
+        torch.cuda.set_device(local_rank)
+        dist.init_process_group("nccl", device_id=torch.device("cuda", local_rank))
+    try:
+        run_enx(args, rank, world, local_rank)
+    finally:
+        if world > 1:
+            import torch.distributed as dist
+
+            dist.destroy_process_group()
+
+
+if __name__ == "__main__":
+    main()

@@ -1,0 +1,1005 @@
+// libenx C ABI: raw kernel entry points, the .enargeia loader, and the model context
+// (weights + f16 KV caches + the captured decode step).  Declarations and the reference
+// interfaces each function replaces are in include/enx.h.
+
+#include <cmath>
+#include <cstdio>
+#include <cstring>
+#include <fstream>
+#include <map>
+#include <memory>
+#include <string>
+#include <vector>
+
+#include "enx_internal.cuh"
+#include "k_decode.cuh"
+#include "k_small.cuh"
+#include "json_lite.h"
+
+// ---------------------------------------------------------------------------------------------
+// error state
+
+namespace enx {
+
+static thread_local std::string g_last_error;
+
+void set_error(const std::string& msg) { g_last_error = msg; }
+
+enx_status fail(enx_status code, const std::string& msg) {
+    g_last_error = msg;
+    return code;
+}
+
+enx_status cuda_fail(cudaError_t err, const char* what) {
+    g_last_error = std::string(what) + ": " + cudaGetErrorName(err) + " (" + cudaGetErrorString(err) + ")";
+    return ENX_ERR_CUDA;
+}
+
+}  // namespace enx
+
+using namespace enx;
+
+extern "C" const char* enx_last_error(void) { return g_last_error.c_str(); }
+extern "C" const char* enx_version(void) { return "enx 0.1 sm_100a"; }
+
+#define CHECK_ARG(cond, msg) \
+    do {                     \
+        if (!(cond)) return fail(ENX_ERR_INVALID, msg); \
+    } while (0)
+
+// ---------------------------------------------------------------------------------------------
+// raw kernels
+
+extern "C" enx_status enx_matmul_q4(const float* x, const uint32_t* packed, const float* scales,
+                                    const uint32_t* zeros, const float* bias, float* out,
+                                    const enx_matmul_q4_dims* d, void* stream) {
+    CHECK_ARG(d && x && packed && scales && zeros && out, "enx_matmul_q4: null pointer");
+    CHECK_ARG(d->block_size == 64, "enx_matmul_q4: block_size must be 64");
+    CHECK_ARG(d->k % 64 == 0 && d->k > 0, "enx_matmul_q4: k must be a positive multiple of 64");
+    CHECK_ARG(d->blocks_per_row == d->k / 64, "enx_matmul_q4: blocks_per_row != k/64");
+    CHECK_ARG(!d->use_bias || bias, "enx_matmul_q4: use_bias set without a bias");
+    if (d->m == 0 || d->n == 0) return ENX_OK;
+    QW w{packed, scales, zeros, d->n, d->k};
+    ENX_CUDA(launch_matmul(4, x, w, d->use_bias ? bias : nullptr, out, d->m, d->out_stride, d->out_offset,
+                           as_stream(stream), false));
+    return ENX_OK;
+}
+
+extern "C" enx_status enx_lm_head_q8(const float* x, const uint32_t* packed, const float* scales,
+                                     const uint32_t* zeros, float* out, const enx_embedding_dims* d,
+                                     void* stream) {
+    CHECK_ARG(d && x && packed && scales && zeros && out, "enx_lm_head_q8: null pointer");
+    CHECK_ARG(d->seq == 1, "enx_lm_head_q8: seq must be 1 (decode-shaped head)");
+    CHECK_ARG(d->block_size == 64 && d->hidden % 64 == 0 && d->blocks_per_row == d->hidden / 64,
+              "enx_lm_head_q8: hidden must be a multiple of 64 with block_size 64");
+    if (d->row_count == 0) return ENX_OK;
+    QW w{packed, scales, zeros, d->row_count, d->hidden};
+    ENX_CUDA(launch_matmul(8, x, w, nullptr, out, 1, d->row_count, d->out_offset, as_stream(stream), false));
+    return ENX_OK;
+}
+
+extern "C" enx_status enx_embed_gather_q8(const uint32_t* ids, const uint32_t* packed,
+                                          const float* scales, const uint32_t* zeros, float* out,
+                                          const enx_embedding_dims* d, void* stream) {
+    CHECK_ARG(d && ids && packed && scales && zeros && out, "enx_embed_gather_q8: null pointer");
+    CHECK_ARG(d->block_size == 64 && d->hidden % 64 == 0, "enx_embed_gather_q8: bad hidden/block");
+    if (d->seq == 0) return ENX_OK;
+    QW w{packed, scales, zeros, d->row_count, d->hidden};
+    ENX_CUDA(launch_embed(ids, w, 8, out, d->seq, d->row_begin, d->row_count, d->hidden, as_stream(stream), false));
+    return ENX_OK;
+}
+
+extern "C" enx_status enx_sample(float* logits, const uint32_t* history, uint32_t* out,
+                                 const enx_sample_dims* d, void* workspace, void* stream) {
+    (void)workspace;
+    CHECK_ARG(d && logits && out, "enx_sample: null pointer");
+    CHECK_ARG(d->history_length == 0 || history, "enx_sample: history_length > 0 without history");
+    CHECK_ARG(d->vocab > 0, "enx_sample: empty vocabulary");
+    if (d->vocab > sample_max_vocab())
+        return fail(ENX_ERR_RANGE, "enx_sample: vocabulary of " + std::to_string(d->vocab) +
+                                       " exceeds the on-chip limit of " + std::to_string(sample_max_vocab()));
+    SampleRow r{d->temperature, d->top_p, d->repetition_penalty, d->random};
+    ENX_CUDA(launch_sample(logits, d->vocab, 1, history, d->history_length, nullptr, nullptr, false, r, out,
+                           as_stream(stream), false));
+    return ENX_OK;
+}
+
+extern "C" enx_status enx_sample_batched(float* logits, uint32_t vocab, uint32_t batch,
+                                         const uint32_t* history, uint32_t history_stride,
+                                         const uint32_t* history_length,
+                                         const enx_sampling_row* rows, uint32_t* out, void* stream) {
+    CHECK_ARG(logits && rows && out, "enx_sample_batched: null pointer");
+    CHECK_ARG(vocab > 0, "enx_sample_batched: empty vocabulary");
+    if (vocab > sample_max_vocab()) return fail(ENX_ERR_RANGE, "enx_sample_batched: vocabulary too large");
+    if (batch == 0) return ENX_OK;
+    static_assert(sizeof(enx_sampling_row) == sizeof(SampleRow), "row layout");
+    ENX_CUDA(launch_sample(logits, vocab, batch, history, history_stride, history_length,
+                           reinterpret_cast<const SampleRow*>(rows), false, SampleRow{}, out, as_stream(stream),
+                           false));
+    return ENX_OK;
+}
+
+static uint32_t splits_for(uint32_t positions) { return (positions + kAttnChunk - 1) / kAttnChunk; }
+
+extern "C" size_t enx_attn_decode_workspace_bytes(uint32_t max_context, uint32_t heads, uint32_t head_dim) {
+    return (size_t)splits_for(max_context) * heads * (head_dim + 2) * sizeof(float);
+}
+
+extern "C" size_t enx_attn_prefill_workspace_bytes(uint32_t queries, uint32_t keys, uint32_t heads,
+                                                   uint32_t head_dim) {
+    return (size_t)queries * splits_for(keys) * heads * (head_dim + 2) * sizeof(float);
+}
+
+static enx_status attn_common(const float* q, const uint16_t* kc, const uint16_t* vc, float* out,
+                              uint32_t ntok, uint32_t begin, uint32_t heads, uint32_t kv_heads,
+                              uint32_t hd, void* ws, cudaStream_t st, const char* who) {
+    std::string w = who;
+    CHECK_ARG(q && kc && vc && out && ws, (w + ": null pointer").c_str());
+    CHECK_ARG(kv_heads > 0 && heads % kv_heads == 0, (w + ": heads must be a multiple of kv_heads").c_str());
+    CHECK_ARG(hd % 2 == 0 && hd <= 64 && hd > 0, (w + ": head_dim must be even and <= 64").c_str());
+    if (ntok == 0) return ENX_OK;
+    StepArgs S{};
+    S.hidden = heads * hd;
+    S.heads = heads;
+    S.kv_heads = kv_heads;
+    S.head_dim = hd;
+    S.q = const_cast<float*>(q);
+    S.attn_part = static_cast<float*>(ws);
+    S.splits = splits_for(begin + ntok);
+    S.pos = nullptr;
+    S.pos_base = begin;
+    S.seq_fixed = 0;
+    S.kcache = const_cast<uint16_t*>(kc);
+    S.vcache = const_cast<uint16_t*>(vc);
+    S.layers = 1;
+    S.max_context = begin + ntok;
+    ENX_CUDA(launch_attn(S, 0, ntok, st));
+    ENX_CUDA(launch_attn_merge(S, out, ntok, st));
+    return ENX_OK;
+}
+
+extern "C" enx_status enx_attn_decode(const float* q, const uint16_t* k_cache, const uint16_t* v_cache,
+                                      float* out, const enx_attn_decode_dims* d, void* workspace,
+                                      void* stream) {
+    CHECK_ARG(d, "enx_attn_decode: null dims");
+    CHECK_ARG(d->cache_stride == d->kv_heads * d->head_dim, "enx_attn_decode: cache_stride must be kv_heads*head_dim");
+    return attn_common(q, k_cache, v_cache, out, 1, d->position, d->heads, d->kv_heads, d->head_dim, workspace,
+                       as_stream(stream), "enx_attn_decode");
+}
+
+extern "C" enx_status enx_attn_prefill(const float* q, const uint16_t* k_cache, const uint16_t* v_cache,
+                                       float* out, uint32_t queries, uint32_t begin, uint32_t heads,
+                                       uint32_t kv_heads, uint32_t head_dim, void* workspace,
+                                       void* stream) {
+    return attn_common(q, k_cache, v_cache, out, queries, begin, heads, kv_heads, head_dim, workspace,
+                       as_stream(stream), "enx_attn_prefill");
+}
+
+extern "C" enx_status enx_rmsnorm(const float* x, const float* w, float* out, uint32_t seq,
+                                  uint32_t features, float eps, void* stream) {
+    CHECK_ARG(x && w && out, "enx_rmsnorm: null pointer");
+    ENX_CUDA(launch_rmsnorm(x, w, out, seq, features, eps, as_stream(stream)));
+    return ENX_OK;
+}
+
+extern "C" enx_status enx_rope(const float* x, float* out, const float* ct, const float* sn, uint32_t seq,
+                               uint32_t heads, uint32_t hd, uint32_t pos0, uint32_t out_offset, void* stream) {
+    CHECK_ARG(x && out && ct && sn, "enx_rope: null pointer");
+    CHECK_ARG(hd % 2 == 0, "enx_rope: head_dim must be even");
+    ENX_CUDA(launch_rope(x, out, ct, sn, seq, heads, hd, pos0, out_offset, as_stream(stream)));
+    return ENX_OK;
+}
+
+extern "C" enx_status enx_cache_pack(const float* src, uint16_t* dst, uint32_t count, uint32_t dst_offset,
+                                     void* stream) {
+    CHECK_ARG(src && dst, "enx_cache_pack: null pointer");
+    ENX_CUDA(launch_cache_pack(src, dst, count, dst_offset, as_stream(stream)));
+    return ENX_OK;
+}
+
+extern "C" enx_status enx_silu_mul(const float* g, const float* u, float* out, uint32_t n, void* stream) {
+    CHECK_ARG(g && u && out, "enx_silu_mul: null pointer");
+    ENX_CUDA(launch_silu_mul(g, u, out, n, as_stream(stream)));
+    return ENX_OK;
+}
+
+extern "C" enx_status enx_add(const float* a, const float* b, float* out, uint32_t n, void* stream) {
+    CHECK_ARG(a && b && out, "enx_add: null pointer");
+    ENX_CUDA(launch_add(a, b, out, n, as_stream(stream)));
+    return ENX_OK;
+}
+
+// ---------------------------------------------------------------------------------------------
+// model context
+
+namespace {
+
+constexpr uint32_t kMaxStepBatch = 4;
+
+struct Tensor {
+    int bits = 0;  // 4, 8, or 32 (F32 data in `packed`)
+    uint32_t rows = 0, cols = 0;
+    void* packed = nullptr;
+    float* scales = nullptr;
+    uint32_t* zeros = nullptr;
+    size_t bytes = 0;
+};
+
+// Per-step inputs/outputs, one pinned host copy and one device copy; the captured step copies
+// the input half host->device at its start and the ids device->host at its end.
+struct StepBlock {
+    uint32_t tokens[kMaxStepBatch];
+    uint32_t pos[kMaxStepBatch];
+    uint32_t hist_len[kMaxStepBatch];
+    uint32_t pad;
+    SampleRow rows[kMaxStepBatch];
+    uint32_t out[kMaxStepBatch];
+};
+
+__global__ void k_step_prep(StepBlock* blk, uint32_t* history, uint32_t max_ctx, uint32_t batch) {
+    uint32_t b = threadIdx.x;
+    if (b < batch) history[(size_t)b * max_ctx + blk->pos[b]] = blk->tokens[b];
+}
+
+// State of a device-fed decode loop: step counter, start positions, first tokens, params.
+struct LoopState {
+    uint32_t i;
+    uint32_t base_pos[kMaxStepBatch];
+    uint32_t first[kMaxStepBatch];
+    SampleRow params[kMaxStepBatch];  // random field unused: per-step draws come from `randoms`
+};
+
+__global__ void k_loop_prep(LoopState* L, StepBlock* blk, const float* randoms, const uint32_t* ids,
+                            uint32_t* history, uint32_t max_ctx, uint32_t batch) {
+    uint32_t b = threadIdx.x;
+    if (b >= batch) return;
+    uint32_t i = L->i;
+    uint32_t tok = i == 0 ? L->first[b] : ids[(size_t)(i - 1) * batch + b];
+    uint32_t pos = L->base_pos[b] + i;
+    blk->tokens[b] = tok;
+    blk->pos[b] = pos;
+    blk->hist_len[b] = pos + 1;
+    SampleRow r = L->params[b];
+    r.random = randoms[(size_t)i * batch + b];
+    blk->rows[b] = r;
+    history[(size_t)b * max_ctx + pos] = tok;
+}
+
+__global__ void k_loop_post(LoopState* L, const StepBlock* blk, uint32_t* ids, uint32_t batch) {
+    uint32_t b = threadIdx.x;
+    uint32_t i = L->i;
+    if (b < batch) ids[(size_t)i * batch + b] = blk->out[b];
+    __syncthreads();
+    if (b == 0) L->i = i + 1;
+}
+
+}  // namespace
+
+struct enx_ctx {
+    enx_model_config cfg{};
+    int device = 0;
+    cudaStream_t stream = nullptr;
+    std::map<std::string, Tensor> tensors;
+    void* arena = nullptr;
+    size_t arena_bytes = 0;
+    bool loaded = false;
+    std::vector<LayerArgs> layers;
+    HeadArgs head{};
+    // KV and per-sequence state
+    uint32_t max_ctx = 0, batch = 0;
+    uint16_t* kcache = nullptr;
+    uint16_t* vcache = nullptr;
+    float* rope_cos = nullptr;
+    float* rope_sin = nullptr;
+    uint32_t* history = nullptr;  // [batch][max_ctx]
+    std::vector<uint32_t> filled;
+    // decode step buffers
+    float *x = nullptr, *q = nullptr, *gated = nullptr, *logits = nullptr, *normed = nullptr,
+          *attn_part = nullptr;
+    StepBlock* d_step = nullptr;
+    StepBlock* h_step = nullptr;
+    cudaGraphExec_t graph[kMaxStepBatch + 1] = {};
+    uint32_t graph_launches[kMaxStepBatch + 1] = {};
+    cudaGraphExec_t loop_graph[kMaxStepBatch + 1] = {};
+    uint32_t loop_launches[kMaxStepBatch + 1] = {};
+    LoopState* d_loop = nullptr;
+    LoopState* h_loop = nullptr;
+    float* d_loop_rand = nullptr;
+    uint32_t* d_loop_ids = nullptr;
+    uint32_t* h_loop_ids = nullptr;
+    uint32_t loop_cap = 0, loop_count = 0;
+    uint32_t last_launches = 0;
+    // prefill buffers (chunk-sized)
+    uint32_t pf_chunk = 0;
+    float *pf_x = nullptr, *pf_n = nullptr, *pf_q = nullptr, *pf_q2 = nullptr, *pf_k = nullptr,
+          *pf_k2 = nullptr, *pf_v = nullptr, *pf_att = nullptr, *pf_t = nullptr, *pf_g = nullptr,
+          *pf_u = nullptr, *pf_part = nullptr;
+    uint32_t* pf_ids = nullptr;
+};
+
+namespace {
+
+template <typename T>
+enx_status dalloc(T** p, size_t count, const char* what) {
+    if (count == 0) count = 1;
+    cudaError_t e = cudaMalloc(reinterpret_cast<void**>(p), count * sizeof(T));
+    if (e != cudaSuccess) return fail(ENX_ERR_NOMEM, std::string("cudaMalloc(") + what + "): " + cudaGetErrorString(e));
+    return ENX_OK;
+}
+
+template <typename T>
+void dfree(T*& p) {
+    if (p) cudaFree(p);
+    p = nullptr;
+}
+
+struct DeviceGuard {
+    int prev = -1;
+    explicit DeviceGuard(int dev) {
+        cudaGetDevice(&prev);
+        if (prev != dev) cudaSetDevice(dev);
+    }
+    ~DeviceGuard() {
+        int cur = -1;
+        cudaGetDevice(&cur);
+        if (prev >= 0 && cur != prev) cudaSetDevice(prev);
+    }
+};
+
+void free_graphs(enx_ctx* c) {
+    for (auto& g : c->graph) {
+        if (g) cudaGraphExecDestroy(g);
+        g = nullptr;
+    }
+    for (auto& g : c->loop_graph) {
+        if (g) cudaGraphExecDestroy(g);
+        g = nullptr;
+    }
+}
+
+void free_prefill(enx_ctx* c) {
+    dfree(c->pf_x); dfree(c->pf_n); dfree(c->pf_q); dfree(c->pf_q2); dfree(c->pf_k); dfree(c->pf_k2);
+    dfree(c->pf_v); dfree(c->pf_att); dfree(c->pf_t); dfree(c->pf_g); dfree(c->pf_u); dfree(c->pf_part);
+    dfree(c->pf_ids);
+    c->pf_chunk = 0;
+}
+
+void free_kv(enx_ctx* c) {
+    free_graphs(c);
+    free_prefill(c);
+    dfree(c->kcache); dfree(c->vcache); dfree(c->rope_cos); dfree(c->rope_sin); dfree(c->history);
+    dfree(c->x); dfree(c->q); dfree(c->gated); dfree(c->logits); dfree(c->normed); dfree(c->attn_part);
+    dfree(c->d_step);
+    if (c->h_step) cudaFreeHost(c->h_step);
+    c->h_step = nullptr;
+    dfree(c->d_loop); dfree(c->d_loop_rand); dfree(c->d_loop_ids);
+    if (c->h_loop) cudaFreeHost(c->h_loop);
+    if (c->h_loop_ids) cudaFreeHost(c->h_loop_ids);
+    c->h_loop = nullptr;
+    c->h_loop_ids = nullptr;
+    c->loop_cap = c->loop_count = 0;
+    c->max_ctx = c->batch = 0;
+    c->filled.clear();
+}
+
+const Tensor* find(enx_ctx* c, const std::string& name, int bits, uint32_t rows, uint32_t cols,
+                   std::string& err) {
+    auto it = c->tensors.find(name);
+    if (it == c->tensors.end()) { err = "missing tensor " + name; return nullptr; }
+    const Tensor& t = it->second;
+    if ((bits == 32) != (t.bits == 32) || (bits != 32 && bits != 0 && t.bits != bits)) {
+        err = name + ": unexpected dtype";
+        return nullptr;
+    }
+    if (t.rows != rows || t.cols != cols) {
+        err = name + ": shape [" + std::to_string(t.rows) + ", " + std::to_string(t.cols) + "] expected [" +
+              std::to_string(rows) + ", " + std::to_string(cols) + "]";
+        return nullptr;
+    }
+    return &t;
+}
+
+QW qw(const Tensor* t) {
+    return QW{static_cast<const uint32_t*>(t->packed), t->scales, t->zeros, t->rows, t->cols};
+}
+
+enx_status bind_model(enx_ctx* c) {
+    const enx_model_config& C = c->cfg;
+    const uint32_t H = C.hidden, kv = C.kv_heads * C.head_dim, I = C.intermediate;
+    std::string err;
+    c->layers.assign(C.layers, LayerArgs{});
+    for (uint32_t l = 0; l < C.layers; ++l) {
+        std::string p = "model.layers." + std::to_string(l) + ".";
+        LayerArgs& L = c->layers[l];
+        L.layer = l;
+        const Tensor* t;
+#define NEED(var, name, bits, r, cl)                                 \
+    t = find(c, p + name, bits, r, cl, err);                        \
+    if (!t) return fail(ENX_ERR_FORMAT, err);                        \
+    var = t;
+        const Tensor *tin, *tpost, *tq, *tk, *tv, *to, *tg, *tu, *td, *bq, *bk, *bv;
+        NEED(tin, "input_layernorm.weight", 32, H, 1);
+        NEED(tpost, "post_attention_layernorm.weight", 32, H, 1);
+        NEED(tq, "self_attn.q_proj.weight", 4, H, H);
+        NEED(tk, "self_attn.k_proj.weight", 4, kv, H);
+        NEED(tv, "self_attn.v_proj.weight", 4, kv, H);
+        NEED(to, "self_attn.o_proj.weight", 4, H, H);
+        NEED(tg, "mlp.gate_proj.weight", 4, I, H);
+        NEED(tu, "mlp.up_proj.weight", 4, I, H);
+        NEED(td, "mlp.down_proj.weight", 4, H, I);
+        NEED(bq, "self_attn.q_proj.bias", 32, H, 1);
+        NEED(bk, "self_attn.k_proj.bias", 32, kv, 1);
+        NEED(bv, "self_attn.v_proj.bias", 32, kv, 1);
+#undef NEED
+        L.norm_in = static_cast<const float*>(tin->packed);
+        L.norm_post = static_cast<const float*>(tpost->packed);
+        L.wq = qw(tq); L.wk = qw(tk); L.wv = qw(tv); L.wo = qw(to); L.wg = qw(tg); L.wu = qw(tu); L.wd = qw(td);
+        L.bq = static_cast<const float*>(bq->packed);
+        L.bk = static_cast<const float*>(bk->packed);
+        L.bv = static_cast<const float*>(bv->packed);
+    }
+    const Tensor* e = find(c, "model.embed_tokens.weight", 0, C.vocab, H, err);
+    if (!e) return fail(ENX_ERR_FORMAT, err);
+    if (e->bits != 4 && e->bits != 8) return fail(ENX_ERR_FORMAT, "embedding must be Q4 or Q8");
+    const Tensor* fn = find(c, "model.norm.weight", 32, H, 1, err);
+    if (!fn) return fail(ENX_ERR_FORMAT, err);
+    c->head.embed = qw(e);
+    c->head.bits = e->bits;
+    c->head.norm = static_cast<const float*>(fn->packed);
+    return ENX_OK;
+}
+
+}  // namespace
+
+extern "C" enx_status enx_create(const enx_model_config* cfg, int device, enx_ctx** out) {
+    CHECK_ARG(cfg && out, "enx_create: null pointer");
+    const enx_model_config& C = *cfg;
+    CHECK_ARG(C.layers > 0 && C.hidden > 0 && C.heads > 0 && C.kv_heads > 0 && C.vocab > 0, "enx_create: empty config");
+    CHECK_ARG(C.heads % C.kv_heads == 0, "enx_create: heads must be a multiple of kv_heads");
+    CHECK_ARG(C.heads * C.head_dim == C.hidden, "enx_create: heads*head_dim must equal hidden");
+    CHECK_ARG(C.head_dim % 2 == 0 && C.head_dim <= 64, "enx_create: head_dim must be even and <= 64");
+    CHECK_ARG(C.hidden % 64 == 0 && C.intermediate % 64 == 0, "enx_create: hidden/intermediate must be multiples of 64");
+    CHECK_ARG(C.vocab <= sample_max_vocab(), "enx_create: vocabulary exceeds the sampler's on-chip limit");
+    int n = 0;
+    ENX_CUDA(cudaGetDeviceCount(&n));
+    if (device < 0 || device >= n) return fail(ENX_ERR_INVALID, "enx_create: no CUDA device " + std::to_string(device));
+    DeviceGuard g(device);
+    std::unique_ptr<enx_ctx> c(new enx_ctx());
+    c->cfg = C;
+    c->device = device;
+    ENX_CUDA(cudaStreamCreateWithFlags(&c->stream, cudaStreamNonBlocking));
+    *out = c.release();
+    return ENX_OK;
+}
+
+extern "C" enx_status enx_destroy(enx_ctx* c) {
+    if (!c) return ENX_OK;
+    {
+        DeviceGuard g(c->device);
+        if (c->stream) cudaStreamSynchronize(c->stream);
+        free_kv(c);
+        if (c->arena) cudaFree(c->arena);
+        if (c->stream) cudaStreamDestroy(c->stream);
+    }
+    delete c;
+    return ENX_OK;
+}
+
+extern "C" enx_status enx_load_enargeia_memory(enx_ctx* c, const void* data, size_t size) {
+    CHECK_ARG(c && data, "enx_load_enargeia: null pointer");
+    const uint8_t* raw = static_cast<const uint8_t*>(data);
+    if (size < 16) return fail(ENX_ERR_FORMAT, "need at least 16 bytes to read the header length");
+    if (std::memcmp(raw, "ENARGEIA", 8) != 0) return fail(ENX_ERR_FORMAT, "not a .enargeia file: bad magic");
+    uint32_t version, hlen;
+    std::memcpy(&version, raw + 8, 4);
+    std::memcpy(&hlen, raw + 12, 4);
+    if (version != 1) return fail(ENX_ERR_FORMAT, "unsupported .enargeia version " + std::to_string(version) + ", expected 1");
+    if (hlen > 64u * 1024 * 1024 || 16 + (size_t)hlen > size) return fail(ENX_ERR_FORMAT, "header length out of range");
+    size_t data_off = 16 + (size_t)hlen;
+    data_off += (256 - data_off % 256) % 256;
+    json::Value root;
+    std::string perr;
+    if (!json::parse(std::string(reinterpret_cast<const char*>(raw + 16), hlen), root, perr))
+        return fail(ENX_ERR_FORMAT, "header JSON: " + perr);
+    const json::Value* tensors = root.get("tensors");
+    if (!tensors || !tensors->is_object()) return fail(ENX_ERR_FORMAT, "header has no tensors object");
+
+    struct Range { size_t b, e; };
+    struct Plan { Tensor t; Range r[3]; int nr; };
+    std::map<std::string, Plan> plan;
+    size_t total = 0;
+    auto range = [&](const json::Value* v, Range& r) -> bool {
+        if (!v || !v->is_array() || v->arr.size() != 2) return false;
+        r.b = (size_t)v->arr[0].num;
+        r.e = (size_t)v->arr[1].num;
+        return r.e >= r.b && data_off + r.e <= size && r.b % 256 == 0;
+    };
+    for (auto& kvp : tensors->obj) {
+        const std::string& name = kvp.first;
+        const json::Value& e = kvp.second;
+        const json::Value* dt = e.get("dtype");
+        const json::Value* sh = e.get("shape");
+        const json::Value* of = e.get("offsets");
+        if (!dt || !sh || !of || !sh->is_array()) return fail(ENX_ERR_FORMAT, name + ": incomplete entry");
+        Plan p{};
+        if (dt->str == "Q4" || dt->str == "Q8") {
+            if (sh->arr.size() != 2) return fail(ENX_ERR_FORMAT, name + ": quantised tensor must be 2-D");
+            p.t.bits = dt->str == "Q4" ? 4 : 8;
+            p.t.rows = (uint32_t)sh->arr[0].num;
+            p.t.cols = (uint32_t)sh->arr[1].num;
+            const json::Value* bs = e.get("blockSize");
+            if (bs && (uint32_t)bs->num != 64) return fail(ENX_ERR_FORMAT, name + ": block size must be 64");
+            if (p.t.cols % 64) return fail(ENX_ERR_FORMAT, name + ": reduction axis not a multiple of 64");
+            if (!range(of->get("packed"), p.r[0]) || !range(of->get("scales"), p.r[1]) || !range(of->get("zeros"), p.r[2]))
+                return fail(ENX_ERR_FORMAT, name + ": bad byte range");
+            size_t elems = (size_t)p.t.rows * p.t.cols, blocks = elems / 64, per = 32 / p.t.bits;
+            if (p.r[0].e - p.r[0].b != elems / per * 4 || p.r[1].e - p.r[1].b != blocks * 4 ||
+                p.r[2].e - p.r[2].b != (blocks + per - 1) / per * 4)
+                return fail(ENX_ERR_FORMAT, name + ": range sizes do not match the shape");
+            p.nr = 3;
+        } else if (dt->str == "F32") {
+            p.t.bits = 32;
+            size_t n = 1;
+            for (auto& d : sh->arr) n *= (size_t)d.num;
+            p.t.rows = sh->arr.empty() ? 1 : (uint32_t)sh->arr[0].num;
+            p.t.cols = sh->arr.size() >= 2 ? (uint32_t)(n / p.t.rows) : 1;
+            if (!range(of->get("data"), p.r[0]) || p.r[0].e - p.r[0].b != n * 4)
+                return fail(ENX_ERR_FORMAT, name + ": bad data range");
+            p.nr = 1;
+        } else {
+            return fail(ENX_ERR_FORMAT, name + ": dtype " + dt->str + " unsupported on this path");
+        }
+        for (int i = 0; i < p.nr; ++i) total += (p.r[i].e - p.r[i].b + 255) / 256 * 256 + 256;
+        plan[name] = p;
+    }
+    DeviceGuard g(c->device);
+    if (c->arena) { cudaFree(c->arena); c->arena = nullptr; }
+    c->tensors.clear();
+    c->loaded = false;
+    free_graphs(c);
+    ENX_TRY(dalloc(reinterpret_cast<uint8_t**>(&c->arena), total, "weights"));
+    c->arena_bytes = total;
+    uint8_t* cur = static_cast<uint8_t*>(c->arena);
+    // Ranges go to the device verbatim; every range starts 256-aligned and keeps 16 bytes of
+    // slack after it so 16-byte vector loads at the tail never leave the allocation.
+    for (auto& kvp : plan) {
+        Plan& p = kvp.second;
+        void* dst[3];
+        for (int i = 0; i < p.nr; ++i) {
+            size_t n = p.r[i].e - p.r[i].b;
+            ENX_CUDA(cudaMemcpyAsync(cur, raw + data_off + p.r[i].b, n, cudaMemcpyHostToDevice, c->stream));
+            dst[i] = cur;
+            cur += (n + 255) / 256 * 256 + 256;
+        }
+        p.t.packed = dst[0];
+        if (p.nr == 3) {
+            p.t.scales = static_cast<float*>(dst[1]);
+            p.t.zeros = static_cast<uint32_t*>(dst[2]);
+        }
+        p.t.bytes = 0;
+        for (int i = 0; i < p.nr; ++i) p.t.bytes += p.r[i].e - p.r[i].b;
+        c->tensors[kvp.first] = p.t;
+    }
+    ENX_CUDA(cudaStreamSynchronize(c->stream));
+    ENX_TRY(bind_model(c));
+    c->loaded = true;
+    return ENX_OK;
+}
+
+extern "C" enx_status enx_load_enargeia(enx_ctx* c, const char* path) {
+    CHECK_ARG(c && path, "enx_load_enargeia: null pointer");
+    std::ifstream f(path, std::ios::binary | std::ios::ate);
+    if (!f) return fail(ENX_ERR_FORMAT, std::string("cannot open ") + path);
+    size_t n = (size_t)f.tellg();
+    f.seekg(0);
+    void* host = nullptr;
+    // pinned staging so the upload runs at full PCIe rate
+    if (cudaMallocHost(&host, n) != cudaSuccess) return fail(ENX_ERR_NOMEM, "cudaMallocHost for the model file");
+    f.read(static_cast<char*>(host), (std::streamsize)n);
+    enx_status s = f ? enx_load_enargeia_memory(c, host, n) : fail(ENX_ERR_FORMAT, "short read");
+    cudaFreeHost(host);
+    return s;
+}
+
+extern "C" enx_status enx_kv_alloc(enx_ctx* c, uint32_t max_context, uint32_t batch) {
+    CHECK_ARG(c, "enx_kv_alloc: null context");
+    CHECK_ARG(max_context > 0 && batch > 0, "enx_kv_alloc: empty cache");
+    const enx_model_config& C = c->cfg;
+    DeviceGuard g(c->device);
+    cudaStreamSynchronize(c->stream);
+    free_kv(c);
+    const size_t kv = (size_t)C.kv_heads * C.head_dim;
+    const size_t per = (size_t)batch * C.layers * max_context * kv;
+    ENX_TRY(dalloc(&c->kcache, per, "k cache"));
+    ENX_TRY(dalloc(&c->vcache, per, "v cache"));
+    ENX_CUDA(cudaMemsetAsync(c->kcache, 0, per * 2, c->stream));
+    ENX_CUDA(cudaMemsetAsync(c->vcache, 0, per * 2, c->stream));
+    // RoPE table: f64 angle, cos and sin rounded once to f32 (src/kernels/rope.wgsl:42-46)
+    const uint32_t half = C.head_dim / 2;
+    std::vector<float> ct((size_t)max_context * half), st((size_t)max_context * half);
+    for (uint32_t p = 0; p < max_context; ++p)
+        for (uint32_t i = 0; i < half; ++i) {
+            double freq = 1.0 / std::pow((double)C.rope_theta, (2.0 * i) / (double)C.head_dim);
+            double a = (double)p * freq;
+            ct[(size_t)p * half + i] = (float)std::cos(a);
+            st[(size_t)p * half + i] = (float)std::sin(a);
+        }
+    ENX_TRY(dalloc(&c->rope_cos, ct.size(), "rope cos"));
+    ENX_TRY(dalloc(&c->rope_sin, st.size(), "rope sin"));
+    ENX_CUDA(cudaMemcpy(c->rope_cos, ct.data(), ct.size() * 4, cudaMemcpyHostToDevice));
+    ENX_CUDA(cudaMemcpy(c->rope_sin, st.data(), st.size() * 4, cudaMemcpyHostToDevice));
+    ENX_TRY(dalloc(&c->history, (size_t)batch * max_context, "history"));
+    const uint32_t B = batch < kMaxStepBatch ? batch : kMaxStepBatch;
+    ENX_TRY(dalloc(&c->x, (size_t)B * C.hidden, "x"));
+    ENX_TRY(dalloc(&c->q, (size_t)B * C.hidden, "q"));
+    ENX_TRY(dalloc(&c->gated, (size_t)B * C.intermediate, "gated"));
+    ENX_TRY(dalloc(&c->logits, (size_t)batch * C.vocab, "logits"));
+    ENX_TRY(dalloc(&c->normed, (size_t)batch * C.hidden, "normed"));
+    ENX_TRY(dalloc(&c->attn_part, (size_t)B * splits_for(max_context) * C.heads * (C.head_dim + 2), "attn partials"));
+    ENX_TRY(dalloc(&c->d_step, 1, "step block"));
+    if (cudaMallocHost(&c->h_step, sizeof(StepBlock)) != cudaSuccess) return fail(ENX_ERR_NOMEM, "pinned step block");
+    std::memset(c->h_step, 0, sizeof(StepBlock));
+    // device-fed loop: room for every step the caches can hold
+    c->loop_cap = max_context * B;
+    ENX_TRY(dalloc(&c->d_loop, 1, "loop state"));
+    ENX_TRY(dalloc(&c->d_loop_rand, c->loop_cap, "loop randoms"));
+    ENX_TRY(dalloc(&c->d_loop_ids, c->loop_cap, "loop ids"));
+    if (cudaMallocHost(&c->h_loop, sizeof(LoopState)) != cudaSuccess) return fail(ENX_ERR_NOMEM, "pinned loop state");
+    if (cudaMallocHost(&c->h_loop_ids, (size_t)c->loop_cap * 4) != cudaSuccess) return fail(ENX_ERR_NOMEM, "pinned loop ids");
+    ENX_CUDA(cudaStreamSynchronize(c->stream));
+    c->max_ctx = max_context;
+    c->batch = batch;
+    c->filled.assign(batch, 0);
+    return ENX_OK;
+}
+
+extern "C" enx_status enx_kv_reset(enx_ctx* c, uint32_t seq) {
+    CHECK_ARG(c, "enx_kv_reset: null context");
+    if (seq >= c->batch) return fail(ENX_ERR_RANGE, "enx_kv_reset: sequence " + std::to_string(seq) + " outside the cache");
+    c->filled[seq] = 0;
+    return ENX_OK;
+}
+
+extern "C" enx_status enx_kv_filled(enx_ctx* c, uint32_t seq, uint32_t* filled) {
+    CHECK_ARG(c && filled, "enx_kv_filled: null pointer");
+    if (seq >= c->batch) return fail(ENX_ERR_RANGE, "enx_kv_filled: sequence outside the cache");
+    *filled = c->filled[seq];
+    return ENX_OK;
+}
+
+static StepArgs step_args(enx_ctx* c) {
+    const enx_model_config& C = c->cfg;
+    StepArgs S{};
+    S.hidden = C.hidden;
+    S.heads = C.heads;
+    S.kv_heads = C.kv_heads;
+    S.head_dim = C.head_dim;
+    S.intermediate = C.intermediate;
+    S.eps = C.rms_norm_eps;
+    S.x = c->x;
+    S.q = c->q;
+    S.gated = c->gated;
+    S.logits = c->logits;
+    S.normed = c->normed;
+    S.attn_part = c->attn_part;
+    S.splits = splits_for(c->max_ctx);
+    S.pos = nullptr;
+    S.pos_base = 0;
+    S.seq_fixed = 0xFFFFFFFFu;
+    S.rope_cos = c->rope_cos;
+    S.rope_sin = c->rope_sin;
+    S.kcache = c->kcache;
+    S.vcache = c->vcache;
+    S.layers = C.layers;
+    S.max_context = c->max_ctx;
+    return S;
+}
+
+static enx_status ensure_prefill(enx_ctx* c, uint32_t chunk) {
+    if (c->pf_chunk >= chunk) return ENX_OK;
+    free_prefill(c);
+    const enx_model_config& C = c->cfg;
+    const size_t H = C.hidden, kv = (size_t)C.kv_heads * C.head_dim, I = C.intermediate;
+    ENX_TRY(dalloc(&c->pf_x, chunk * H, "prefill x"));
+    ENX_TRY(dalloc(&c->pf_n, chunk * H, "prefill normed"));
+    ENX_TRY(dalloc(&c->pf_q, chunk * H, "prefill q"));
+    ENX_TRY(dalloc(&c->pf_q2, chunk * H, "prefill q rope"));
+    ENX_TRY(dalloc(&c->pf_k, chunk * kv, "prefill k"));
+    ENX_TRY(dalloc(&c->pf_k2, chunk * kv, "prefill k rope"));
+    ENX_TRY(dalloc(&c->pf_v, chunk * kv, "prefill v"));
+    ENX_TRY(dalloc(&c->pf_att, chunk * H, "prefill attn"));
+    ENX_TRY(dalloc(&c->pf_t, chunk * H, "prefill tmp"));
+    ENX_TRY(dalloc(&c->pf_g, chunk * I, "prefill gate"));
+    ENX_TRY(dalloc(&c->pf_u, chunk * I, "prefill up"));
+    ENX_TRY(dalloc(&c->pf_part, (size_t)chunk * splits_for(c->max_ctx) * C.heads * (C.head_dim + 2), "prefill partials"));
+    ENX_TRY(dalloc(&c->pf_ids, chunk, "prefill ids"));
+    c->pf_chunk = chunk;
+    return ENX_OK;
+}
+
+extern "C" enx_status enx_prefill(enx_ctx* c, uint32_t seq, const uint32_t* ids, uint32_t n, uint32_t chunk) {
+    CHECK_ARG(c && ids, "enx_prefill: null pointer");
+    if (!c->loaded) return fail(ENX_ERR_STATE, "enx_prefill: no model loaded");
+    if (!c->kcache) return fail(ENX_ERR_STATE, "enx_prefill: call enx_kv_alloc first");
+    if (seq >= c->batch) return fail(ENX_ERR_RANGE, "enx_prefill: sequence outside the cache");
+    if (n < 1) return fail(ENX_ERR_RANGE, "prompt length 0 must be at least 1");
+    const uint32_t remaining = c->max_ctx - c->filled[seq];
+    if (n > remaining)
+        return fail(ENX_ERR_RANGE, "prompt of " + std::to_string(n) + " exceeds the remaining context of " +
+                                       std::to_string(remaining));
+    const enx_model_config& C = c->cfg;
+    for (uint32_t i = 0; i < n; ++i)
+        if (ids[i] >= C.vocab) return fail(ENX_ERR_INVALID, "token id " + std::to_string(ids[i]) + " outside the vocabulary");
+    if (chunk == 0 || chunk > n) chunk = n;
+    DeviceGuard g(c->device);
+    ENX_TRY(ensure_prefill(c, chunk));
+    cudaStream_t st = c->stream;
+    const uint32_t H = C.hidden, kv = C.kv_heads * C.head_dim, I = C.intermediate;
+    StepArgs S = step_args(c);
+    S.seq_fixed = seq;
+    S.q = c->pf_q2;
+    S.attn_part = c->pf_part;
+    for (uint32_t begin0 = 0; begin0 < n; begin0 += chunk) {
+        const uint32_t m = n - begin0 < chunk ? n - begin0 : chunk;
+        const uint32_t begin = c->filled[seq];
+        ENX_CUDA(cudaMemcpyAsync(c->pf_ids, ids + begin0, m * 4, cudaMemcpyHostToDevice, st));
+        ENX_CUDA(cudaMemcpyAsync(c->history + (size_t)seq * c->max_ctx + begin, c->pf_ids, m * 4,
+                                 cudaMemcpyDeviceToDevice, st));
+        ENX_CUDA(launch_embed(c->pf_ids, c->head.embed, c->head.bits, c->pf_x, m, 0, C.vocab, H, st, false));
+        S.pos_base = begin;
+        for (uint32_t l = 0; l < C.layers; ++l) {
+            const LayerArgs& L = c->layers[l];
+            ENX_CUDA(launch_rmsnorm(c->pf_x, L.norm_in, c->pf_n, m, H, C.rms_norm_eps, st));
+            ENX_CUDA(launch_matmul(4, c->pf_n, L.wq, L.bq, c->pf_q, m, H, 0, st, false));
+            ENX_CUDA(launch_matmul(4, c->pf_n, L.wk, L.bk, c->pf_k, m, kv, 0, st, false));
+            ENX_CUDA(launch_matmul(4, c->pf_n, L.wv, L.bv, c->pf_v, m, kv, 0, st, false));
+            ENX_CUDA(launch_rope(c->pf_q, c->pf_q2, c->rope_cos, c->rope_sin, m, C.heads, C.head_dim, begin, 0, st));
+            ENX_CUDA(launch_rope(c->pf_k, c->pf_k2, c->rope_cos, c->rope_sin, m, C.kv_heads, C.head_dim, begin, 0, st));
+            ENX_CUDA(launch_cache_pack(c->pf_k2, c->kcache + S.cache_offset(seq, l, begin), m * kv, 0, st));
+            ENX_CUDA(launch_cache_pack(c->pf_v, c->vcache + S.cache_offset(seq, l, begin), m * kv, 0, st));
+            ENX_CUDA(launch_attn(S, l, m, st));
+            ENX_CUDA(launch_attn_merge(S, c->pf_att, m, st));
+            ENX_CUDA(launch_matmul(4, c->pf_att, L.wo, nullptr, c->pf_t, m, H, 0, st, false));
+            ENX_CUDA(launch_add(c->pf_x, c->pf_t, c->pf_x, m * H, st));
+            ENX_CUDA(launch_rmsnorm(c->pf_x, L.norm_post, c->pf_n, m, H, C.rms_norm_eps, st));
+            ENX_CUDA(launch_matmul(4, c->pf_n, L.wg, nullptr, c->pf_g, m, I, 0, st, false));
+            ENX_CUDA(launch_matmul(4, c->pf_n, L.wu, nullptr, c->pf_u, m, I, 0, st, false));
+            ENX_CUDA(launch_silu_mul(c->pf_g, c->pf_u, c->pf_g, m * I, st));
+            ENX_CUDA(launch_matmul(4, c->pf_g, L.wd, nullptr, c->pf_t, m, H, 0, st, false));
+            ENX_CUDA(launch_add(c->pf_x, c->pf_t, c->pf_x, m * H, st));
+        }
+        c->filled[seq] += m;
+        if (begin0 + m >= n) {
+            // tail on the last chunk only: final norm of the last row, then the tied head
+            float* last = c->normed + (size_t)seq * H;
+            ENX_CUDA(launch_rmsnorm(c->pf_x + (size_t)(m - 1) * H, c->head.norm, last, 1, H, C.rms_norm_eps, st));
+            ENX_CUDA(launch_matmul(c->head.bits, last, c->head.embed, nullptr, c->logits + (size_t)seq * C.vocab, 1,
+                                   C.vocab, 0, st, false));
+        }
+    }
+    ENX_CUDA(cudaStreamSynchronize(st));
+    return ENX_OK;
+}
+
+extern "C" enx_status enx_sample_prefill(enx_ctx* c, uint32_t seq, const enx_sampling* params, float random,
+                                         uint32_t* out_id) {
+    CHECK_ARG(c && params && out_id, "enx_sample_prefill: null pointer");
+    if (!c->kcache) return fail(ENX_ERR_STATE, "enx_sample_prefill: no cache");
+    if (seq >= c->batch) return fail(ENX_ERR_RANGE, "enx_sample_prefill: sequence outside the cache");
+    if (c->filled[seq] == 0) return fail(ENX_ERR_STATE, "enx_sample_prefill: nothing prefilled");
+    DeviceGuard g(c->device);
+    SampleRow r{params->temperature, params->top_p, params->repetition_penalty, random};
+    ENX_CUDA(launch_sample(c->logits + (size_t)seq * c->cfg.vocab, c->cfg.vocab, 1,
+                           c->history + (size_t)seq * c->max_ctx, c->filled[seq], nullptr, nullptr, false, r,
+                           c->d_step->out, c->stream, false));
+    ENX_CUDA(cudaMemcpyAsync(out_id, c->d_step->out, 4, cudaMemcpyDeviceToHost, c->stream));
+    ENX_CUDA(cudaStreamSynchronize(c->stream));
+    return ENX_OK;
+}
+
+static enx_status capture_step(enx_ctx* c, uint32_t B, bool loop) {
+    cudaStream_t st = c->stream;
+    StepArgs S = step_args(c);
+    S.pos = c->d_step->pos;
+    const size_t in_bytes = offsetof(StepBlock, out);
+    ENX_CUDA(cudaStreamBeginCapture(st, cudaStreamCaptureModeThreadLocal));
+    cudaError_t e = cudaSuccess;
+    if (loop) {
+        k_loop_prep<<<1, 32, 0, st>>>(c->d_loop, c->d_step, c->d_loop_rand, c->d_loop_ids, c->history, c->max_ctx, B);
+        e = cudaGetLastError();
+    } else {
+        e = cudaMemcpyAsync(c->d_step, c->h_step, in_bytes, cudaMemcpyHostToDevice, st);
+        if (e == cudaSuccess) {
+            k_step_prep<<<1, 32, 0, st>>>(c->d_step, c->history, c->max_ctx, B);
+            e = cudaGetLastError();
+        }
+    }
+    if (e == cudaSuccess) e = launch_embed(c->d_step->tokens, c->head.embed, c->head.bits, c->x, B, 0, c->cfg.vocab,
+                                           c->cfg.hidden, st, true);
+    for (uint32_t l = 0; l < c->cfg.layers && e == cudaSuccess; ++l) e = launch_layer(B, c->layers[l], S, st);
+    if (e == cudaSuccess) e = launch_head(B, c->head.bits, c->head, S, st);
+    if (e == cudaSuccess)
+        e = launch_sample(c->logits, c->cfg.vocab, B, c->history, c->max_ctx, c->d_step->hist_len, c->d_step->rows,
+                          false, SampleRow{}, c->d_step->out, st, true);
+    if (e == cudaSuccess) {
+        if (loop) {
+            k_loop_post<<<1, 32, 0, st>>>(c->d_loop, c->d_step, c->d_loop_ids, B);
+            e = cudaGetLastError();
+        } else {
+            e = cudaMemcpyAsync(c->h_step->out, c->d_step->out, B * 4, cudaMemcpyDeviceToHost, st);
+        }
+    }
+    cudaGraph_t graph = nullptr;
+    cudaError_t e2 = cudaStreamEndCapture(st, &graph);
+    if (e != cudaSuccess) {
+        if (graph) cudaGraphDestroy(graph);
+        return cuda_fail(e, "capturing the decode step");
+    }
+    if (e2 != cudaSuccess) return cuda_fail(e2, "cudaStreamEndCapture");
+    size_t nn = 0;
+    cudaGraphGetNodes(graph, nullptr, &nn);
+    std::vector<cudaGraphNode_t> nodes(nn);
+    cudaGraphGetNodes(graph, nodes.data(), &nn);
+    uint32_t kernels = 0;
+    for (auto& nd : nodes) {
+        cudaGraphNodeType t;
+        cudaGraphNodeGetType(nd, &t);
+        if (t == cudaGraphNodeTypeKernel) ++kernels;
+    }
+    cudaGraphExec_t exec = nullptr;
+    e = cudaGraphInstantiate(&exec, graph, 0);
+    cudaGraphDestroy(graph);
+    if (e != cudaSuccess) return cuda_fail(e, "cudaGraphInstantiate(decode step)");
+    (loop ? c->loop_graph : c->graph)[B] = exec;
+    (loop ? c->loop_launches : c->graph_launches)[B] = kernels;
+    return ENX_OK;
+}
+
+extern "C" enx_status enx_decode_step(enx_ctx* c, uint32_t batch, const uint32_t* tokens,
+                                      const enx_sampling* params, uint32_t params_count,
+                                      const float* randoms, uint32_t* out_ids) {
+    CHECK_ARG(c && tokens && params && randoms && out_ids, "enx_decode_step: null pointer");
+    if (!c->loaded) return fail(ENX_ERR_STATE, "enx_decode_step: no model loaded");
+    if (!c->kcache) return fail(ENX_ERR_STATE, "enx_decode_step: call enx_kv_alloc first");
+    if (batch == 0) return ENX_OK;
+    if (batch > c->batch) return fail(ENX_ERR_RANGE, "enx_decode_step: batch exceeds the allocated sequences");
+    if (batch > kMaxStepBatch)
+        return fail(ENX_ERR_RANGE, "enx_decode_step: at most " + std::to_string(kMaxStepBatch) + " sequences per step");
+    CHECK_ARG(params_count == 1 || params_count == batch, "enx_decode_step: params_count must be 1 or batch");
+    for (uint32_t b = 0; b < batch; ++b) {
+        if (tokens[b] >= c->cfg.vocab) return fail(ENX_ERR_INVALID, "token id outside the vocabulary");
+        if (c->filled[b] >= c->max_ctx)
+            return fail(ENX_ERR_RANGE, "context exhausted: " + std::to_string(c->filled[b]) + " + 1 exceeds " +
+                                           std::to_string(c->max_ctx));
+    }
+    DeviceGuard g(c->device);
+    if (!c->graph[batch]) ENX_TRY(capture_step(c, batch, false));
+    StepBlock* h = c->h_step;
+    for (uint32_t b = 0; b < batch; ++b) {
+        const enx_sampling& p = params[params_count == 1 ? 0 : b];
+        h->tokens[b] = tokens[b];
+        h->pos[b] = c->filled[b];
+        h->hist_len[b] = c->filled[b] + 1;  // the fed token joins the history before sampling
+        h->rows[b] = SampleRow{p.temperature, p.top_p, p.repetition_penalty, randoms[b]};
+    }
+    ENX_CUDA(cudaGraphLaunch(c->graph[batch], c->stream));
+    ENX_CUDA(cudaStreamSynchronize(c->stream));
+    for (uint32_t b = 0; b < batch; ++b) {
+        out_ids[b] = h->out[b];
+        c->filled[b] += 1;
+    }
+    c->last_launches = c->graph_launches[batch];
+    return ENX_OK;
+}
+
+extern "C" enx_status enx_decode_loop(enx_ctx* c, uint32_t batch, const uint32_t* first_tokens,
+                                      const enx_sampling* params, uint32_t params_count, uint32_t steps,
+                                      const float* randoms, uint32_t* out_ids, int sync) {
+    CHECK_ARG(c && first_tokens && params && randoms, "enx_decode_loop: null pointer");
+    CHECK_ARG(!sync || out_ids, "enx_decode_loop: sync without out_ids");
+    if (!c->loaded) return fail(ENX_ERR_STATE, "enx_decode_loop: no model loaded");
+    if (!c->kcache) return fail(ENX_ERR_STATE, "enx_decode_loop: call enx_kv_alloc first");
+    if (batch == 0 || steps == 0) return ENX_OK;
+    if (batch > c->batch || batch > kMaxStepBatch) return fail(ENX_ERR_RANGE, "enx_decode_loop: batch too large");
+    CHECK_ARG(params_count == 1 || params_count == batch, "enx_decode_loop: params_count must be 1 or batch");
+    for (uint32_t b = 0; b < batch; ++b) {
+        if (first_tokens[b] >= c->cfg.vocab) return fail(ENX_ERR_INVALID, "token id outside the vocabulary");
+        if ((uint64_t)c->filled[b] + steps > c->max_ctx)
+            return fail(ENX_ERR_RANGE, "context exhausted: " + std::to_string(c->filled[b]) + " + " +
+                                           std::to_string(steps) + " exceeds " + std::to_string(c->max_ctx));
+    }
+    DeviceGuard g(c->device);
+    if (!c->loop_graph[batch]) ENX_TRY(capture_step(c, batch, true));
+    ENX_CUDA(cudaStreamSynchronize(c->stream));  // the pinned loop state may still be in flight
+    LoopState* L = c->h_loop;
+    L->i = 0;
+    for (uint32_t b = 0; b < batch; ++b) {
+        const enx_sampling& p = params[params_count == 1 ? 0 : b];
+        L->base_pos[b] = c->filled[b];
+        L->first[b] = first_tokens[b];
+        L->params[b] = SampleRow{p.temperature, p.top_p, p.repetition_penalty, 0.f};
+    }
+    ENX_CUDA(cudaMemcpyAsync(c->d_loop, L, sizeof(LoopState), cudaMemcpyHostToDevice, c->stream));
+    ENX_CUDA(cudaMemcpyAsync(c->d_loop_rand, randoms, (size_t)steps * batch * 4, cudaMemcpyHostToDevice, c->stream));
+    for (uint32_t i = 0; i < steps; ++i) ENX_CUDA(cudaGraphLaunch(c->loop_graph[batch], c->stream));
+    ENX_CUDA(cudaMemcpyAsync(c->h_loop_ids, c->d_loop_ids, (size_t)steps * batch * 4, cudaMemcpyDeviceToHost,
+                             c->stream));
+    for (uint32_t b = 0; b < batch; ++b) c->filled[b] += steps;
+    c->loop_count = steps * batch;
+    c->last_launches = c->loop_launches[batch];
+    if (sync) {
+        ENX_CUDA(cudaStreamSynchronize(c->stream));
+        std::memcpy(out_ids, c->h_loop_ids, (size_t)steps * batch * 4);
+    }
+    return ENX_OK;
+}
+
+extern "C" enx_status enx_synchronize(enx_ctx* c) {
+    CHECK_ARG(c, "enx_synchronize: null context");
+    DeviceGuard g(c->device);
+    ENX_CUDA(cudaStreamSynchronize(c->stream));
+    return ENX_OK;
+}
+
+extern "C" enx_status enx_loop_ids(enx_ctx* c, uint32_t* out_ids, uint32_t count) {
+    CHECK_ARG(c && out_ids, "enx_loop_ids: null pointer");
+    if (count > c->loop_count) return fail(ENX_ERR_RANGE, "enx_loop_ids: more ids than the last loop produced");
+    std::memcpy(out_ids, c->h_loop_ids, (size_t)count * 4);
+    return ENX_OK;
+}
+
+extern "C" enx_status enx_logits(enx_ctx* c, uint32_t seq, float* out) {
+    CHECK_ARG(c && out, "enx_logits: null pointer");
+    if (!c->logits || seq >= c->batch) return fail(ENX_ERR_RANGE, "enx_logits: sequence outside the cache");
+    DeviceGuard g(c->device);
+    ENX_CUDA(cudaMemcpyAsync(out, c->logits + (size_t)seq * c->cfg.vocab, (size_t)c->cfg.vocab * 4,
+                             cudaMemcpyDeviceToHost, c->stream));
+    ENX_CUDA(cudaStreamSynchronize(c->stream));
+    return ENX_OK;
+}
+
+extern "C" enx_status enx_hidden(enx_ctx* c, uint32_t seq, float* out) {
+    CHECK_ARG(c && out, "enx_hidden: null pointer");
+    if (!c->normed || seq >= c->batch) return fail(ENX_ERR_RANGE, "enx_hidden: sequence outside the cache");
+    DeviceGuard g(c->device);
+    ENX_CUDA(cudaMemcpyAsync(out, c->normed + (size_t)seq * c->cfg.hidden, (size_t)c->cfg.hidden * 4,
+                             cudaMemcpyDeviceToHost, c->stream));
+    ENX_CUDA(cudaStreamSynchronize(c->stream));
+    return ENX_OK;
+}
+
+extern "C" enx_status enx_kv_view(enx_ctx* c, uint32_t seq, uint32_t layer, const uint16_t** k, const uint16_t** v) {
+    CHECK_ARG(c && k && v, "enx_kv_view: null pointer");
+    if (!c->kcache || seq >= c->batch || layer >= c->cfg.layers) return fail(ENX_ERR_RANGE, "enx_kv_view: out of range");
+    StepArgs S = step_args(c);
+    *k = c->kcache + S.cache_offset(seq, layer, 0);
+    *v = c->vcache + S.cache_offset(seq, layer, 0);
+    return ENX_OK;
+}
+
+extern "C" enx_status enx_tensor_view(enx_ctx* c, const char* name, int32_t* bits, uint32_t* rows, uint32_t* cols,
+                                      const void** packed, const float** scales, const uint32_t** zeros) {
+    CHECK_ARG(c && name && bits && rows && cols && packed && scales && zeros, "enx_tensor_view: null pointer");
+    auto it = c->tensors.find(name);
+    if (it == c->tensors.end()) return fail(ENX_ERR_INVALID, std::string("no tensor ") + name);
+    const Tensor& t = it->second;
+    *bits = t.bits;
+    *rows = t.rows;
+    *cols = t.cols;
+    *packed = t.packed;
+    *scales = t.scales;
+    *zeros = t.zeros;
+    return ENX_OK;
+}
+
+extern "C" enx_status enx_stream(enx_ctx* c, void** stream) {
+    CHECK_ARG(c && stream, "enx_stream: null pointer");
+    *stream = c->stream;
+    return ENX_OK;
+}
+
+extern "C" enx_status enx_step_launches(enx_ctx* c, uint32_t* launches) {
+    CHECK_ARG(c && launches, "enx_step_launches: null pointer");
+    *launches = c->last_launches;
+    return ENX_OK;
+}

@@ -1,0 +1,67 @@
+// Argument blocks and launchers of the decode kernels (k_decode.cu).
+#pragma once
+
+#include "k_matvec.cuh"
+
+namespace enx {
+
+constexpr uint32_t kAttnChunk = 64;  // positions per decode-attention split
+
+// Buffers and geometry of one decode step (shared by every layer of the step).
+struct StepArgs {
+    uint32_t hidden, heads, kv_heads, head_dim, intermediate;
+    float eps;
+    float* x;              // [MT][hidden] residual stream
+    float* q;              // [MT][hidden] rotated queries
+    float* gated;          // [MT][intermediate]
+    float* logits;         // [MT][vocab]
+    float* normed;         // [MT][hidden] final-norm output
+    float* attn_part;      // [MT][splits][heads][head_dim + 2]
+    uint32_t splits;       // max splits = ceil(max_context / kAttnChunk)
+    const uint32_t* pos;   // [MT] position written this step (device), or null: pos_base + t
+    uint32_t pos_base;
+    uint32_t seq_fixed;    // sequence of every token, or kAnySeq: token t is sequence t
+    const float* rope_cos; // [max_context][head_dim/2]
+    const float* rope_sin;
+    uint16_t* kcache;      // f16 bits, [seq][layer][max_context][kv_heads*head_dim]
+    uint16_t* vcache;
+    uint32_t layers, max_context;
+
+    __host__ __device__ uint32_t pos_of(uint32_t t) const { return pos ? pos[t] : pos_base + t; }
+    __host__ __device__ uint32_t seq_of(uint32_t t) const { return seq_fixed == 0xFFFFFFFFu ? t : seq_fixed; }
+    __host__ __device__ size_t cache_offset(uint32_t seq, uint32_t layer, uint32_t p) const {
+        return (((size_t)seq * layers + layer) * max_context + p) * (size_t)(kv_heads * head_dim);
+    }
+};
+
+struct LayerArgs {
+    uint32_t layer;
+    const float* norm_in;
+    const float* norm_post;
+    QW wq, wk, wv, wo, wg, wu, wd;
+    const float* bq;
+    const float* bk;
+    const float* bv;
+};
+
+struct HeadArgs {
+    QW embed;
+    int bits;
+    const float* norm;
+};
+
+int num_sms();
+cudaError_t launch_embed(const uint32_t* ids, const QW& table, int bits, float* out, uint32_t seq,
+                         uint32_t row_begin, uint32_t row_count, uint32_t out_stride,
+                         cudaStream_t st, bool pdl);
+cudaError_t launch_matmul(int bits, const float* x, const QW& w, const float* bias, float* out,
+                          uint32_t m, uint32_t out_stride, uint32_t out_offset, cudaStream_t st,
+                          bool pdl);
+cudaError_t launch_layer(uint32_t mt, const LayerArgs& L, const StepArgs& S, cudaStream_t st);
+cudaError_t launch_head(uint32_t mt, int bits, const HeadArgs& Hd, const StepArgs& S, cudaStream_t st);
+// Split-history attention of `ntok` queries (S.q rows) over the cache, then the merge into
+// out[ntok][hidden].  Used by prefill and by the raw enx_attn_* entry points.
+cudaError_t launch_attn(const StepArgs& S, uint32_t layer, uint32_t ntok, cudaStream_t st);
+cudaError_t launch_attn_merge(const StepArgs& S, float* out, uint32_t ntok, cudaStream_t st);
+
+}  // namespace enx

@@ -1,0 +1,271 @@
+/*
+ * enx.h — C ABI of the B200 decode hot path (libenx.so).
+ *
+ * Replaces, for CUDA hosts, the WebGPU kernels and graph of the reference engine
+ * (src/kernels/*.wgsl, src/model/graph_decode.ts, src/model/graph.ts, src/runtime/session.ts).
+ * Plain pointers and sizes only.  Device pointers are CUDA global-memory addresses; `stream`
+ * is a cudaStream_t passed as void* (NULL = the legacy default stream).
+ *
+ * Conventions, mirroring src/kernels/kernel.ts:20-112:
+ *   - every kernel entry point takes its inputs, then its output, then a dims struct whose
+ *     layout is byte-identical to the reference's uniform block for that kernel;
+ *   - kernels never allocate: outputs and workspaces are caller-owned (the reference's
+ *     BufferPool is the only scratch owner, src/gpu/pool.ts:1-12);
+ *   - every call returns an enx_status; enx_last_error() gives the message of the last
+ *     failure on the calling thread (the reference throws RangeError / EnargeiaError instead).
+ *
+ * Two levels:
+ *   1. raw kernels (enx_matmul_q4, enx_lm_head_q8, enx_embed_gather_q8, enx_sample,
+ *      enx_attn_decode, enx_rmsnorm, enx_rope, enx_cache_pack, enx_silu_mul, enx_add), each the
+ *      drop-in for one WGSL dispatch;
+ *   2. a model context (enx_create ... enx_destroy) holding the weights, KV caches and the
+ *      captured decode step, the drop-in for WeightStore + KVCache + DecodeGraph/ForwardGraph.
+ */
+#ifndef ENX_H
+#define ENX_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#if defined(__GNUC__)
+#define ENX_API __attribute__((visibility("default")))
+#else
+#define ENX_API
+#endif
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+typedef int32_t enx_status;
+#define ENX_OK 0
+#define ENX_ERR_INVALID 1   /* bad argument, size or pointer (kernel.ts:70-75 bind mismatch) */
+#define ENX_ERR_CUDA 2      /* a CUDA runtime error; the message names the call */
+#define ENX_ERR_RANGE 3     /* RangeError: grid limits, context exhausted, prompt too long */
+#define ENX_ERR_FORMAT 4    /* EnargeiaError: malformed or unsupported .enargeia */
+#define ENX_ERR_TIMEOUT 5   /* a bounded device-side wait gave up (no GPU hang) */
+#define ENX_ERR_NOMEM 6
+#define ENX_ERR_STATE 7     /* call order: e.g. decode before load */
+
+/* Last error message of the calling thread ("" when none). */
+ENX_API const char* enx_last_error(void);
+/* Library version string, and the compute capability it was built for ("sm_100a"). */
+ENX_API const char* enx_version(void);
+
+/* ------------------------------------------------------------------------------------------
+ * Raw kernels.  Dims structs are the reference's uniform blocks, byte for byte.
+ * ---------------------------------------------------------------------------------------- */
+
+/* matmulQ4Dims, 48 bytes (src/kernels/matmul_q4.ts:151-165). */
+typedef struct {
+    uint32_t m, n, k, use_bias;
+    uint32_t block_size, blocks_per_row, out_stride, out_offset;
+    uint32_t grid_width, pad0, pad1, pad2;
+} enx_matmul_q4_dims;
+
+/* out[row*out_stride + out_offset + col] = sum_i x[row*k + i] * (q - z) * s + bias[col]
+ * Replaces matmul_q4_decode (m == 1, src/kernels/matmul_q4_decode.wgsl:56-101) and
+ * matmul_q4_prefill (m > 1, src/kernels/matmul_q4_prefill.wgsl:77-162).  Bindings in the
+ * reference's order: x, packed, scales, zeros, bias, out, dims.  `bias` may be NULL when
+ * use_bias is 0.  Requires k % 64 == 0 and block_size == 64. */
+ENX_API enx_status enx_matmul_q4(const float* x, const uint32_t* packed, const float* scales,
+                         const uint32_t* zeros, const float* bias, float* out,
+                         const enx_matmul_q4_dims* dims, void* stream);
+
+/* embeddingDims, 48 bytes (src/kernels/embedding_variants.ts:398-412). */
+typedef struct {
+    uint32_t seq, hidden, row_begin, row_count;
+    uint32_t block_size, blocks_per_row, out_stride, out_offset;
+    uint32_t grid_width, pad0, pad1, pad2;
+} enx_embedding_dims;
+
+/* Tied LM head over the int8 table: out[col + out_offset] = sum_k x[k] * W[col, k] for
+ * col < row_count (lm_head_q8, src/kernels/embedding_variants.ts:326-370).  seq must be 1.
+ * Bindings: x, packed, scales, zeros, out, dims. */
+ENX_API enx_status enx_lm_head_q8(const float* x, const uint32_t* packed, const float* scales,
+                          const uint32_t* zeros, float* out, const enx_embedding_dims* dims,
+                          void* stream);
+
+/* out[s, :] = dequant(table[ids[s] - row_begin, :]) for ids inside [row_begin, row_begin +
+ * row_count) (embed_gather_q8, src/kernels/embedding_variants.ts:291-317).  Bindings: ids,
+ * packed, scales, zeros, out, dims. */
+ENX_API enx_status enx_embed_gather_q8(const uint32_t* ids, const uint32_t* packed, const float* scales,
+                               const uint32_t* zeros, float* out, const enx_embedding_dims* dims,
+                               void* stream);
+
+/* sampleDims, 32 bytes (src/kernels/sample.ts:35-50). */
+typedef struct {
+    uint32_t vocab, history_length;
+    float temperature, top_p, repetition_penalty, random;
+    uint32_t pad0, pad1;
+} enx_sample_dims;
+
+/* The sampler of src/kernels/sample.wgsl:143-332: in-place repetition penalty on `logits`,
+ * then greedy argmax (temperature <= 0) or temperature / top-p / seeded draw; writes one id to
+ * out[0].  Bindings: logits (read_write), history, out, dims.  Probabilities, bisection masses
+ * and the running draw total are computed in double (the oracle's exact-arithmetic rule).
+ * `workspace` is unused and may be NULL (the kernel keeps its state in shared memory); the
+ * argument exists so the call shape matches the batched entry point. */
+ENX_API enx_status enx_sample(float* logits, const uint32_t* history, uint32_t* out,
+                      const enx_sample_dims* dims, void* workspace, void* stream);
+
+/* Batched form: rows b = 0..batch-1 of logits [batch][vocab] with their own histories
+ * (history + b*history_stride, history_length[b]) and params; out[b].  All pointers device. */
+typedef struct {
+    float temperature, top_p, repetition_penalty, random;
+} enx_sampling_row;
+
+ENX_API enx_status enx_sample_batched(float* logits, uint32_t vocab, uint32_t batch,
+                              const uint32_t* history, uint32_t history_stride,
+                              const uint32_t* history_length, const enx_sampling_row* rows,
+                              uint32_t* out, void* stream);
+
+/* attnDecodeDims, 32 bytes (src/kernels/attn_decode.ts:23-32). */
+typedef struct {
+    uint32_t position, heads, kv_heads, head_dim;
+    uint32_t score_stride, cache_stride, pad0, pad1;
+} enx_attn_decode_dims;
+
+/* Decode attention of one query over the f16 cache, fused: attn_scores_decode_f16 +
+ * softmax + attn_apply_decode_parallel_f16 (src/kernels/cache_variants.ts:147-179,
+ * src/kernels/softmax.wgsl:30-81, src/kernels/cache_variants.ts:353-399).
+ * q f32[heads*head_dim]; k_cache/v_cache f16 bits [position+1][cache_stride]; out
+ * f32[heads*head_dim].  `workspace` holds split partials: enx_attn_decode_workspace_bytes(). */
+ENX_API enx_status enx_attn_decode(const float* q, const uint16_t* k_cache, const uint16_t* v_cache,
+                           float* out, const enx_attn_decode_dims* dims, void* workspace,
+                           void* stream);
+ENX_API size_t enx_attn_decode_workspace_bytes(uint32_t max_context, uint32_t heads, uint32_t head_dim);
+
+/* Prefill attention of a chunk: queries i = 0..queries-1 at absolute positions begin+i attend
+ * cached keys 0..begin+i (attn_scores_f16 / softmax / attn_apply_f16,
+ * src/kernels/cache_variants.ts:81-144).  q f32[queries][heads*hd]; out likewise. */
+ENX_API enx_status enx_attn_prefill(const float* q, const uint16_t* k_cache, const uint16_t* v_cache,
+                            float* out, uint32_t queries, uint32_t begin, uint32_t heads,
+                            uint32_t kv_heads, uint32_t head_dim, void* workspace, void* stream);
+ENX_API size_t enx_attn_prefill_workspace_bytes(uint32_t queries, uint32_t keys, uint32_t heads,
+                                        uint32_t head_dim);
+
+/* RMSNorm rows (src/kernels/rmsnorm.wgsl:27-63): out = x * rsqrt(mean(x^2) + eps) * w. */
+ENX_API enx_status enx_rmsnorm(const float* x, const float* weight, float* out, uint32_t seq,
+                       uint32_t features, float eps, void* stream);
+
+/* Half-rotation RoPE (src/kernels/rope.wgsl:28-53) from a cos/sin table
+ * ([max_pos][head_dim/2] each, f32); out[out_offset + ...].  Rows s at position
+ * position_offset + s. */
+ENX_API enx_status enx_rope(const float* x, float* out, const float* cos_table, const float* sin_table,
+                    uint32_t seq, uint32_t heads, uint32_t head_dim, uint32_t position_offset,
+                    uint32_t out_offset, void* stream);
+
+/* f32 -> f16 (round to nearest even) pack into a cache at element offset dst_offset
+ * (cache_pack_f16, src/kernels/cache_variants.ts:269-301, cachePackDims). */
+ENX_API enx_status enx_cache_pack(const float* src, uint16_t* dst, uint32_t count, uint32_t dst_offset,
+                          void* stream);
+ENX_API enx_status enx_silu_mul(const float* gate, const float* up, float* out, uint32_t count,
+                        void* stream);
+ENX_API enx_status enx_add(const float* a, const float* b, float* out, uint32_t count, void* stream);
+
+/* ------------------------------------------------------------------------------------------
+ * Model context: WeightStore + KVCache + DecodeGraph + ForwardGraph + Session's step.
+ * One context is used from one host thread and owns one CUDA stream.
+ * ---------------------------------------------------------------------------------------- */
+
+/* ModelConfig (src/model/graph.ts:57-67). */
+typedef struct {
+    uint32_t layers, hidden, heads, kv_heads, head_dim, intermediate, vocab;
+    float rms_norm_eps, rope_theta;
+} enx_model_config;
+
+/* SamplingParams (src/kernels/sample.ts:24-33). */
+typedef struct {
+    float temperature, top_p, repetition_penalty;
+} enx_sampling;
+
+typedef struct enx_ctx enx_ctx;
+
+/* Create a context on CUDA device `device`. */
+ENX_API enx_status enx_create(const enx_model_config* cfg, int device, enx_ctx** out);
+ENX_API enx_status enx_destroy(enx_ctx* ctx);
+
+/* Load every tensor of a .enargeia file (WeightStore.loadQuantized, src/model/weights.ts:
+ * 299-471): the file is parsed here (magic, version, JSON header, 256-aligned ranges,
+ * src/model/enargeia.ts:112-240) and each range is copied to the device verbatim. */
+ENX_API enx_status enx_load_enargeia(enx_ctx* ctx, const char* path);
+/* Same, from a host buffer holding the whole file. */
+ENX_API enx_status enx_load_enargeia_memory(enx_ctx* ctx, const void* data, size_t size);
+
+/* Preallocate f16 KV caches for `batch` sequences of `max_context` positions each
+ * (KVCache constructor, src/runtime/kvcache.ts:59-88).  Also sizes the decode scratch. */
+ENX_API enx_status enx_kv_alloc(enx_ctx* ctx, uint32_t max_context, uint32_t batch);
+/* Forget sequence `seq` without freeing (KVCache.reset, src/runtime/kvcache.ts:135-137). */
+ENX_API enx_status enx_kv_reset(enx_ctx* ctx, uint32_t seq);
+/* Positions filled in sequence `seq` (KVCache.filled). */
+ENX_API enx_status enx_kv_filled(enx_ctx* ctx, uint32_t seq, uint32_t* filled);
+
+/* Chunked prefill of `n` ids into sequence `seq` (Session.runPrefill + ForwardGraph.
+ * encodeChunks, src/runtime/session.ts:326-344, src/model/graph.ts:610-621).  The ids become
+ * the sequence's history; the logits of the last prompt position are kept on the device for
+ * enx_sample_prefill / enx_logits.  ENX_ERR_RANGE if the prompt exceeds the remaining context. */
+ENX_API enx_status enx_prefill(enx_ctx* ctx, uint32_t seq, const uint32_t* ids, uint32_t n,
+                       uint32_t chunk);
+
+/* Session.sampleFromPrefill (src/runtime/session.ts:472-495): sample the first token from the
+ * prefill logits with `params` and draw `random`; the id is written to *out_id (host). */
+ENX_API enx_status enx_sample_prefill(enx_ctx* ctx, uint32_t seq, const enx_sampling* params,
+                              float random, uint32_t* out_id);
+
+/* One decode step for sequences 0..batch-1 (Session.decodeStep, src/runtime/session.ts:
+ * 347-375): append tokens[b] at each sequence's next position, run the whole decoder and the
+ * sampler, write the next ids to out_ids[b].  tokens/params/randoms/out_ids are HOST arrays
+ * of `batch` entries; params may hold one entry (shared) when params_count == 1.  The fed token
+ * joins the sequence's history before sampling, as in the reference. */
+ENX_API enx_status enx_decode_step(enx_ctx* ctx, uint32_t batch, const uint32_t* tokens,
+                           const enx_sampling* params, uint32_t params_count,
+                           const float* randoms, uint32_t* out_ids);
+
+/* Decode `steps` tokens for sequences 0..batch-1 with no host round trip between steps (the
+ * loop of Session.generate, src/runtime/session.ts:440-452, kept on the device): step 0 feeds
+ * first_tokens[b], step i feeds the id sampled at step i-1; step i of sequence b draws
+ * randoms[i*batch + b].  Each step is one launch of the captured decode graph.  With sync != 0
+ * the call waits and writes steps*batch ids to out_ids (host); with sync == 0 it only enqueues
+ * on the context stream, and enx_synchronize + enx_loop_ids fetch the ids later (out_ids may
+ * then be NULL).  ENX_ERR_RANGE if a sequence would run past its context. */
+ENX_API enx_status enx_decode_loop(enx_ctx* ctx, uint32_t batch, const uint32_t* first_tokens,
+                                   const enx_sampling* params, uint32_t params_count,
+                                   uint32_t steps, const float* randoms, uint32_t* out_ids,
+                                   int sync);
+/* Wait for all work queued on the context's stream. */
+ENX_API enx_status enx_synchronize(enx_ctx* ctx);
+/* Ids of the last enx_decode_loop (count = steps*batch), after enx_synchronize. */
+ENX_API enx_status enx_loop_ids(enx_ctx* ctx, uint32_t* out_ids, uint32_t count);
+
+/* Logits of the last step of sequence `seq` (Session.logitsAfter's readback,
+ * src/runtime/session.ts:385-401), copied to host `out` (vocab floats).  Valid after
+ * enx_prefill or enx_decode_step; a sampled step with a repetition penalty has modified them in
+ * place, as in the reference. */
+ENX_API enx_status enx_logits(enx_ctx* ctx, uint32_t seq, float* out);
+
+/* Final-norm hidden state of the last step of sequence `seq` (hidden floats, host). */
+ENX_API enx_status enx_hidden(enx_ctx* ctx, uint32_t seq, float* out);
+
+/* Device view of one layer's cache of sequence `seq` (f16 bits, [max_context][kv_heads*hd]),
+ * for parity checks. */
+ENX_API enx_status enx_kv_view(enx_ctx* ctx, uint32_t seq, uint32_t layer, const uint16_t** k,
+                       const uint16_t** v);
+
+/* Device pointers of one loaded tensor (packed/scales/zeros for Q4/Q8, data in `packed` for
+ * F32).  Shapes are returned in rows/cols (cols = 1 for 1-D). */
+ENX_API enx_status enx_tensor_view(enx_ctx* ctx, const char* name, int32_t* dtype_bits, uint32_t* rows,
+                           uint32_t* cols, const void** packed, const float** scales,
+                           const uint32_t** zeros);
+
+/* The CUDA stream the context runs on (cudaStream_t as void*). */
+ENX_API enx_status enx_stream(enx_ctx* ctx, void** stream);
+
+/* Kernel launches issued by the last enx_decode_step (the captured step's node count). */
+ENX_API enx_status enx_step_launches(enx_ctx* ctx, uint32_t* launches);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* ENX_H */
