@@ -81,6 +81,7 @@ SIGNATURES = {
     "enx_sample": (C.c_int32, [P, P, P, C.POINTER(SampleDims), P, P]),
     "enx_sample_batched": (C.c_int32, [P, U32, U32, P, U32, P, P, P, P]),
     "enx_attn_decode": (C.c_int32, [P, P, P, P, C.POINTER(AttnDecodeDims), P, P]),
+    "enx_attn_decode_noalloc": (C.c_int32, [P, P, P, P, C.POINTER(AttnDecodeDims), P]),
     "enx_attn_decode_workspace_bytes": (C.c_size_t, [U32, U32, U32]),
     "enx_attn_prefill": (C.c_int32, [P, P, P, P, U32, U32, U32, U32, U32, P, P]),
     "enx_attn_prefill_workspace_bytes": (C.c_size_t, [U32, U32, U32, U32]),

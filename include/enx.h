@@ -134,6 +134,18 @@ typedef struct {
 ENX_API enx_status enx_attn_decode(const float* q, const uint16_t* k_cache, const uint16_t* v_cache,
                            float* out, const enx_attn_decode_dims* dims, void* workspace,
                            void* stream);
+/* Same computation as enx_attn_decode, for callers that cannot allocate device memory (for
+ * example code running where cudaMalloc's implicit synchronisation is not allowed, or hosts that
+ * only hand over fixed buffers).  No counterpart in the reference: its WebGPU path always has a
+ * buffer pool.  The split partials live in one library-owned device array (about 528 KB, held on
+ * every GPU that loads the library until exit); limits: position < 4096, heads <= 32,
+ * head_dim <= 64, else ENX_ERR_RANGE.  The first call on each device looks up that array's
+ * device address (cudaGetSymbolAddress, with the device current): make that first call before
+ * any stream capture.  All calls share the array, so calls that overlap on the GPU (other
+ * streams, other threads) race; serialise them.  Allocates nothing. */
+ENX_API enx_status enx_attn_decode_noalloc(const float* q, const uint16_t* k_cache,
+                                           const uint16_t* v_cache, float* out,
+                                           const enx_attn_decode_dims* dims, void* stream);
 ENX_API size_t enx_attn_decode_workspace_bytes(uint32_t max_context, uint32_t heads, uint32_t head_dim);
 
 /* Prefill attention of a chunk: queries i = 0..queries-1 at absolute positions begin+i attend
