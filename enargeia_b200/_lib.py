@@ -108,6 +108,8 @@ SIGNATURES = {
     "enx_kv_view": (C.c_int32, [P, U32, U32, C.POINTER(P), C.POINTER(P)]),
     "enx_tensor_view": (C.c_int32, [P, C.c_char_p, C.POINTER(C.c_int32), C.POINTER(U32), C.POINTER(U32),
                                     C.POINTER(P), C.POINTER(P), C.POINTER(P)]),
+    "enx_set_tracing": (C.c_int32, [P, C.c_int]),
+    "enx_trace": (C.c_int32, [P, P, U32, C.POINTER(U32)]),
     "enx_stream": (C.c_int32, [P, C.POINTER(P)]),
     "enx_step_launches": (C.c_int32, [P, C.POINTER(U32)]),
 }

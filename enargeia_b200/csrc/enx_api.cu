@@ -4,6 +4,7 @@
 
 #include <cmath>
 #include <cstdio>
+#include <cstdlib>
 #include <cstring>
 #include <fstream>
 #include <map>
@@ -13,6 +14,7 @@
 
 #include "enx_internal.cuh"
 #include "k_decode.cuh"
+#include "k_mega.cuh"
 #include "k_small.cuh"
 #include "json_lite.h"
 
@@ -234,6 +236,7 @@ struct StepBlock {
     uint32_t pad;
     SampleRow rows[kMaxStepBatch];
     uint32_t out[kMaxStepBatch];
+    uint32_t err;  // sticky device error of the persistent kernel (read back with `out`)
 };
 
 __global__ void k_step_prep(StepBlock* blk, uint32_t* history, uint32_t max_ctx, uint32_t batch) {
@@ -308,6 +311,11 @@ struct enx_ctx {
     uint32_t* d_loop_ids = nullptr;
     uint32_t* h_loop_ids = nullptr;
     uint32_t loop_cap = 0, loop_count = 0;
+    unsigned long long* d_bar = nullptr;  // grid-barrier counter of the persistent step kernel
+    unsigned long long* d_trace = nullptr;  // stage stamps when tracing is on
+    uint32_t trace_len = 0;
+    bool graph_mega[kMaxStepBatch + 1] = {};
+    bool loop_mega[kMaxStepBatch + 1] = {};
     uint32_t last_launches = 0;
     // prefill buffers (chunk-sized)
     uint32_t pf_chunk = 0;
@@ -372,7 +380,7 @@ void free_kv(enx_ctx* c) {
     dfree(c->d_step);
     if (c->h_step) cudaFreeHost(c->h_step);
     c->h_step = nullptr;
-    dfree(c->d_loop); dfree(c->d_loop_rand); dfree(c->d_loop_ids);
+    dfree(c->d_loop); dfree(c->d_loop_rand); dfree(c->d_loop_ids); dfree(c->d_bar);
     if (c->h_loop) cudaFreeHost(c->h_loop);
     if (c->h_loop_ids) cudaFreeHost(c->h_loop_ids);
     c->h_loop = nullptr;
@@ -478,6 +486,7 @@ extern "C" enx_status enx_destroy(enx_ctx* c) {
         DeviceGuard g(c->device);
         if (c->stream) cudaStreamSynchronize(c->stream);
         free_kv(c);
+        dfree(c->d_trace);
         if (c->arena) cudaFree(c->arena);
         if (c->stream) cudaStreamDestroy(c->stream);
     }
@@ -641,6 +650,8 @@ extern "C" enx_status enx_kv_alloc(enx_ctx* c, uint32_t max_context, uint32_t ba
     std::memset(c->h_step, 0, sizeof(StepBlock));
     // device-fed loop: room for every step the caches can hold
     c->loop_cap = max_context * B;
+    ENX_TRY(dalloc(&c->d_bar, 1, "barrier counter"));
+    ENX_CUDA(cudaMemsetAsync(c->d_step, 0, sizeof(StepBlock), c->stream));
     ENX_TRY(dalloc(&c->d_loop, 1, "loop state"));
     ENX_TRY(dalloc(&c->d_loop_rand, c->loop_cap, "loop randoms"));
     ENX_TRY(dalloc(&c->d_loop_ids, c->loop_cap, "loop ids"));
@@ -797,6 +808,44 @@ extern "C" enx_status enx_sample_prefill(enx_ctx* c, uint32_t seq, const enx_sam
     return ENX_OK;
 }
 
+// The persistent step kernel runs when it fits: 1, 2 or 4 tokens, attention scores for every
+// cached position fit its shared-memory area (it recomputes attention in every CTA), and
+// ENX_DECODE_PATH is not "kernels".  Otherwise the five-launches-per-layer path runs.
+static bool mega_eligible(enx_ctx* c, uint32_t B, const StepArgs& S, MegaArgs& A, MegaGeometry& geo) {
+    const char* env = std::getenv("ENX_DECODE_PATH");
+    if (env && std::string(env) == "kernels") return false;
+    const enx_model_config& C = c->cfg;
+    if ((B != 1 && B != 2 && B != 4) || C.layers > kMaxLayers || C.head_dim % 8 != 0 || C.head_dim > 64 ||
+        C.heads / C.kv_heads > 8 || C.hidden > 1024)
+        return false;
+    std::memset(&A, 0, sizeof(A));
+    A.hidden = C.hidden;
+    A.heads = C.heads;
+    A.kv_heads = C.kv_heads;
+    A.head_dim = C.head_dim;
+    A.intermediate = C.intermediate;
+    A.vocab = C.vocab;
+    A.layers = C.layers;
+    A.eps = C.rms_norm_eps;
+    A.attn_scale = 1.0f / std::sqrt((float)C.head_dim);
+    for (uint32_t l = 0; l < C.layers; ++l) A.layer[l] = c->layers[l];
+    A.head = c->head.embed;
+    A.head_bits = c->head.bits;
+    A.final_norm = c->head.norm;
+    A.S = S;
+    A.tokens = c->d_step->tokens;
+    A.bar = c->d_bar;
+    A.err = &c->d_step->err;
+    A.head_chunk = 32;
+    A.trace = c->d_trace;
+    geo = mega_geometry(B, A);
+    if (geo.nslots < 2 || c->max_ctx > geo.max_positions) return false;
+    A.nslots = geo.nslots;
+    A.slot_bytes = geo.slot_bytes;
+    A.x4_floats = geo.x4_floats;
+    return true;
+}
+
 static enx_status capture_step(enx_ctx* c, uint32_t B, bool loop) {
     cudaStream_t st = c->stream;
     StepArgs S = step_args(c);
@@ -814,10 +863,22 @@ static enx_status capture_step(enx_ctx* c, uint32_t B, bool loop) {
             e = cudaGetLastError();
         }
     }
-    if (e == cudaSuccess) e = launch_embed(c->d_step->tokens, c->head.embed, c->head.bits, c->x, B, 0, c->cfg.vocab,
-                                           c->cfg.hidden, st, true);
-    for (uint32_t l = 0; l < c->cfg.layers && e == cudaSuccess; ++l) e = launch_layer(B, c->layers[l], S, st);
-    if (e == cudaSuccess) e = launch_head(B, c->head.bits, c->head, S, st);
+    bool mega = false;
+    if (e == cudaSuccess) {
+        MegaArgs A;
+        MegaGeometry geo{};
+        mega = mega_eligible(c, B, S, A, geo);
+        if (mega) {
+            e = cudaMemsetAsync(c->d_bar, 0, sizeof(unsigned long long), st);
+            if (e == cudaSuccess) e = launch_mega(B, A, geo, st);
+        } else {
+            e = launch_embed(c->d_step->tokens, c->head.embed, c->head.bits, c->x, B, 0, c->cfg.vocab, c->cfg.hidden,
+                             st, true);
+            for (uint32_t l = 0; l < c->cfg.layers && e == cudaSuccess; ++l) e = launch_layer(B, c->layers[l], S, st);
+            if (e == cudaSuccess) e = launch_head(B, c->head.bits, c->head, S, st);
+        }
+    }
+    (loop ? c->loop_mega : c->graph_mega)[B] = mega;
     if (e == cudaSuccess)
         e = launch_sample(c->logits, c->cfg.vocab, B, c->history, c->max_ctx, c->d_step->hist_len, c->d_step->rows,
                           false, SampleRow{}, c->d_step->out, st, true);
@@ -826,7 +887,9 @@ static enx_status capture_step(enx_ctx* c, uint32_t B, bool loop) {
             k_loop_post<<<1, 32, 0, st>>>(c->d_loop, c->d_step, c->d_loop_ids, B);
             e = cudaGetLastError();
         } else {
-            e = cudaMemcpyAsync(c->h_step->out, c->d_step->out, B * 4, cudaMemcpyDeviceToHost, st);
+            // the ids and the sticky error word travel back together
+            e = cudaMemcpyAsync(c->h_step->out, c->d_step->out, sizeof(StepBlock) - offsetof(StepBlock, out),
+                                cudaMemcpyDeviceToHost, st);
         }
     }
     cudaGraph_t graph = nullptr;
@@ -884,6 +947,13 @@ extern "C" enx_status enx_decode_step(enx_ctx* c, uint32_t batch, const uint32_t
     }
     ENX_CUDA(cudaGraphLaunch(c->graph[batch], c->stream));
     ENX_CUDA(cudaStreamSynchronize(c->stream));
+    if (h->err) {
+        const uint32_t code = h->err;
+        h->err = 0;
+        cudaMemsetAsync(&c->d_step->err, 0, 4, c->stream);
+        return fail(ENX_ERR_TIMEOUT, std::string("decode step: a bounded device wait gave up (") +
+                                         (code == 1 ? "grid barrier" : "weight copy") + ")");
+    }
     for (uint32_t b = 0; b < batch; ++b) {
         out_ids[b] = h->out[b];
         c->filled[b] += 1;
@@ -891,6 +961,8 @@ extern "C" enx_status enx_decode_step(enx_ctx* c, uint32_t batch, const uint32_t
     c->last_launches = c->graph_launches[batch];
     return ENX_OK;
 }
+
+static enx_status device_error(enx_ctx* c);
 
 extern "C" enx_status enx_decode_loop(enx_ctx* c, uint32_t batch, const uint32_t* first_tokens,
                                       const enx_sampling* params, uint32_t params_count, uint32_t steps,
@@ -929,16 +1001,27 @@ extern "C" enx_status enx_decode_loop(enx_ctx* c, uint32_t batch, const uint32_t
     c->last_launches = c->loop_launches[batch];
     if (sync) {
         ENX_CUDA(cudaStreamSynchronize(c->stream));
+        ENX_TRY(device_error(c));
         std::memcpy(out_ids, c->h_loop_ids, (size_t)steps * batch * 4);
     }
     return ENX_OK;
+}
+
+// Reads (and clears) the sticky device error word after the stream has drained.
+static enx_status device_error(enx_ctx* c) {
+    uint32_t code = 0;
+    ENX_CUDA(cudaMemcpy(&code, &c->d_step->err, 4, cudaMemcpyDeviceToHost));
+    if (!code) return ENX_OK;
+    ENX_CUDA(cudaMemset(&c->d_step->err, 0, 4));
+    return fail(ENX_ERR_TIMEOUT, std::string("decode step: a bounded device wait gave up (") +
+                                     (code == 1 ? "grid barrier" : "weight copy") + ")");
 }
 
 extern "C" enx_status enx_synchronize(enx_ctx* c) {
     CHECK_ARG(c, "enx_synchronize: null context");
     DeviceGuard g(c->device);
     ENX_CUDA(cudaStreamSynchronize(c->stream));
-    return ENX_OK;
+    return c->d_step ? device_error(c) : ENX_OK;
 }
 
 extern "C" enx_status enx_loop_ids(enx_ctx* c, uint32_t* out_ids, uint32_t count) {
@@ -989,6 +1072,32 @@ extern "C" enx_status enx_tensor_view(enx_ctx* c, const char* name, int32_t* bit
     *packed = t.packed;
     *scales = t.scales;
     *zeros = t.zeros;
+    return ENX_OK;
+}
+
+extern "C" enx_status enx_set_tracing(enx_ctx* c, int on) {
+    CHECK_ARG(c, "enx_set_tracing: null context");
+    DeviceGuard g(c->device);
+    cudaStreamSynchronize(c->stream);
+    free_graphs(c);
+    dfree(c->d_trace);
+    c->trace_len = 0;
+    if (on) {
+        c->trace_len = 3 * (4 * c->cfg.layers + 1);
+        ENX_TRY(dalloc(&c->d_trace, c->trace_len, "trace"));
+        ENX_CUDA(cudaMemset(c->d_trace, 0, (size_t)c->trace_len * 8));
+    }
+    return ENX_OK;
+}
+
+extern "C" enx_status enx_trace(enx_ctx* c, uint64_t* out, uint32_t capacity, uint32_t* count) {
+    CHECK_ARG(c && out && count, "enx_trace: null pointer");
+    if (!c->d_trace) return fail(ENX_ERR_STATE, "enx_trace: tracing is off");
+    DeviceGuard g(c->device);
+    const uint32_t n = capacity < c->trace_len ? capacity : c->trace_len;
+    ENX_CUDA(cudaStreamSynchronize(c->stream));
+    ENX_CUDA(cudaMemcpy(out, c->d_trace, (size_t)n * 8, cudaMemcpyDeviceToHost));
+    *count = n;
     return ENX_OK;
 }
 

@@ -270,6 +270,16 @@ ENX_API enx_status enx_tensor_view(enx_ctx* ctx, const char* name, int32_t* dtyp
                            uint32_t* cols, const void** packed, const float** scales,
                            const uint32_t** zeros);
 
+/* Stage telemetry (Session.setInstrumented + the per-kernel timestamp queries of
+ * src/runtime/session.ts:162-308).  With tracing on, the persistent decode kernel stamps the
+ * device clock (ns) three times per stage: when the stage starts (its barrier released), when its
+ * weights have landed in shared memory, and when its compute is done; stages are 4 per layer
+ * (qkv, attention+o, gate/up, down) then the head.  enx_trace copies the stamps of the last step
+ * (3 * (4*layers + 1) values; unused slots are 0).  Turning tracing on or off re-captures the
+ * decode graphs on the next step. */
+ENX_API enx_status enx_set_tracing(enx_ctx* ctx, int on);
+ENX_API enx_status enx_trace(enx_ctx* ctx, uint64_t* out, uint32_t capacity, uint32_t* count);
+
 /* The CUDA stream the context runs on (cudaStream_t as void*). */
 ENX_API enx_status enx_stream(enx_ctx* ctx, void** stream);
 
