@@ -124,12 +124,12 @@ extern "C" enx_status enx_sample_batched(float* logits, uint32_t vocab, uint32_t
 static uint32_t splits_for(uint32_t positions) { return (positions + kAttnChunk - 1) / kAttnChunk; }
 
 extern "C" size_t enx_attn_decode_workspace_bytes(uint32_t max_context, uint32_t heads, uint32_t head_dim) {
-    return (size_t)splits_for(max_context) * heads * (head_dim + 2) * sizeof(float);
+    return (size_t)splits_for(max_context) * kAttnChunk * heads * sizeof(float);
 }
 
 extern "C" size_t enx_attn_prefill_workspace_bytes(uint32_t queries, uint32_t keys, uint32_t heads,
                                                    uint32_t head_dim) {
-    return (size_t)queries * splits_for(keys) * heads * (head_dim + 2) * sizeof(float);
+    return (size_t)queries * splits_for(keys) * kAttnChunk * heads * sizeof(float);
 }
 
 static enx_status attn_common(const float* q, const uint16_t* kc, const uint16_t* vc, float* out,
@@ -139,6 +139,7 @@ static enx_status attn_common(const float* q, const uint16_t* kc, const uint16_t
     CHECK_ARG(q && kc && vc && out && ws, (w + ": null pointer").c_str());
     CHECK_ARG(kv_heads > 0 && heads % kv_heads == 0, (w + ": heads must be a multiple of kv_heads").c_str());
     CHECK_ARG(hd % 2 == 0 && hd <= 64 && hd > 0, (w + ": head_dim must be even and <= 64").c_str());
+    CHECK_ARG(heads / kv_heads <= 8, (w + ": at most 8 query heads per kv head").c_str());
     if (ntok == 0) return ENX_OK;
     StepArgs S{};
     S.hidden = heads * hd;
@@ -146,8 +147,8 @@ static enx_status attn_common(const float* q, const uint16_t* kc, const uint16_t
     S.kv_heads = kv_heads;
     S.head_dim = hd;
     S.q = const_cast<float*>(q);
-    S.attn_part = static_cast<float*>(ws);
-    S.splits = splits_for(begin + ntok);
+    S.scores = static_cast<float*>(ws);
+    S.score_stride = splits_for(begin + ntok) * kAttnChunk;
     S.pos = nullptr;
     S.pos_base = begin;
     S.seq_fixed = 0;
@@ -155,8 +156,7 @@ static enx_status attn_common(const float* q, const uint16_t* kc, const uint16_t
     S.vcache = const_cast<uint16_t*>(vc);
     S.layers = 1;
     S.max_context = begin + ntok;
-    ENX_CUDA(launch_attn(S, 0, ntok, st));
-    ENX_CUDA(launch_attn_merge(S, out, ntok, st));
+    ENX_CUDA(launch_attn(S, 0, ntok, out, st, false));
     return ENX_OK;
 }
 
@@ -292,13 +292,13 @@ struct enx_ctx {
     uint32_t max_ctx = 0, batch = 0;
     uint16_t* kcache = nullptr;
     uint16_t* vcache = nullptr;
-    float* rope_cos = nullptr;
-    float* rope_sin = nullptr;
+    double* rope_cos = nullptr;
+    double* rope_sin = nullptr;
     uint32_t* history = nullptr;  // [batch][max_ctx]
     std::vector<uint32_t> filled;
     // decode step buffers
     float *x = nullptr, *q = nullptr, *gated = nullptr, *logits = nullptr, *normed = nullptr,
-          *attn_part = nullptr;
+          *scores = nullptr, *attn_out = nullptr;
     StepBlock* d_step = nullptr;
     StepBlock* h_step = nullptr;
     cudaGraphExec_t graph[kMaxStepBatch + 1] = {};
@@ -376,7 +376,7 @@ void free_kv(enx_ctx* c) {
     free_graphs(c);
     free_prefill(c);
     dfree(c->kcache); dfree(c->vcache); dfree(c->rope_cos); dfree(c->rope_sin); dfree(c->history);
-    dfree(c->x); dfree(c->q); dfree(c->gated); dfree(c->logits); dfree(c->normed); dfree(c->attn_part);
+    dfree(c->x); dfree(c->q); dfree(c->gated); dfree(c->logits); dfree(c->normed); dfree(c->scores); dfree(c->attn_out);
     dfree(c->d_step);
     if (c->h_step) cudaFreeHost(c->h_step);
     c->h_step = nullptr;
@@ -466,6 +466,7 @@ extern "C" enx_status enx_create(const enx_model_config* cfg, int device, enx_ct
     CHECK_ARG(C.heads % C.kv_heads == 0, "enx_create: heads must be a multiple of kv_heads");
     CHECK_ARG(C.heads * C.head_dim == C.hidden, "enx_create: heads*head_dim must equal hidden");
     CHECK_ARG(C.head_dim % 2 == 0 && C.head_dim <= 64, "enx_create: head_dim must be even and <= 64");
+    CHECK_ARG(C.heads / C.kv_heads <= 8, "enx_create: at most 8 query heads per kv head");
     CHECK_ARG(C.hidden % 64 == 0 && C.intermediate % 64 == 0, "enx_create: hidden/intermediate must be multiples of 64");
     CHECK_ARG(C.vocab <= sample_max_vocab(), "enx_create: vocabulary exceeds the sampler's on-chip limit");
     int n = 0;
@@ -625,18 +626,18 @@ extern "C" enx_status enx_kv_alloc(enx_ctx* c, uint32_t max_context, uint32_t ba
     ENX_CUDA(cudaMemsetAsync(c->vcache, 0, per * 2, c->stream));
     // RoPE table: f64 angle, cos and sin rounded once to f32 (src/kernels/rope.wgsl:42-46)
     const uint32_t half = C.head_dim / 2;
-    std::vector<float> ct((size_t)max_context * half), st((size_t)max_context * half);
+    std::vector<double> ct((size_t)max_context * half), st((size_t)max_context * half);
     for (uint32_t p = 0; p < max_context; ++p)
         for (uint32_t i = 0; i < half; ++i) {
             double freq = 1.0 / std::pow((double)C.rope_theta, (2.0 * i) / (double)C.head_dim);
             double a = (double)p * freq;
-            ct[(size_t)p * half + i] = (float)std::cos(a);
-            st[(size_t)p * half + i] = (float)std::sin(a);
+            ct[(size_t)p * half + i] = std::cos(a);
+            st[(size_t)p * half + i] = std::sin(a);
         }
     ENX_TRY(dalloc(&c->rope_cos, ct.size(), "rope cos"));
     ENX_TRY(dalloc(&c->rope_sin, st.size(), "rope sin"));
-    ENX_CUDA(cudaMemcpy(c->rope_cos, ct.data(), ct.size() * 4, cudaMemcpyHostToDevice));
-    ENX_CUDA(cudaMemcpy(c->rope_sin, st.data(), st.size() * 4, cudaMemcpyHostToDevice));
+    ENX_CUDA(cudaMemcpy(c->rope_cos, ct.data(), ct.size() * 8, cudaMemcpyHostToDevice));
+    ENX_CUDA(cudaMemcpy(c->rope_sin, st.data(), st.size() * 8, cudaMemcpyHostToDevice));
     ENX_TRY(dalloc(&c->history, (size_t)batch * max_context, "history"));
     const uint32_t B = batch < kMaxStepBatch ? batch : kMaxStepBatch;
     ENX_TRY(dalloc(&c->x, (size_t)B * C.hidden, "x"));
@@ -644,7 +645,8 @@ extern "C" enx_status enx_kv_alloc(enx_ctx* c, uint32_t max_context, uint32_t ba
     ENX_TRY(dalloc(&c->gated, (size_t)B * C.intermediate, "gated"));
     ENX_TRY(dalloc(&c->logits, (size_t)batch * C.vocab, "logits"));
     ENX_TRY(dalloc(&c->normed, (size_t)batch * C.hidden, "normed"));
-    ENX_TRY(dalloc(&c->attn_part, (size_t)B * splits_for(max_context) * C.heads * (C.head_dim + 2), "attn partials"));
+    ENX_TRY(dalloc(&c->scores, (size_t)B * splits_for(max_context) * kAttnChunk * C.heads, "attention scores"));
+    ENX_TRY(dalloc(&c->attn_out, (size_t)B * C.hidden, "attention output"));
     ENX_TRY(dalloc(&c->d_step, 1, "step block"));
     if (cudaMallocHost(&c->h_step, sizeof(StepBlock)) != cudaSuccess) return fail(ENX_ERR_NOMEM, "pinned step block");
     std::memset(c->h_step, 0, sizeof(StepBlock));
@@ -692,8 +694,9 @@ static StepArgs step_args(enx_ctx* c) {
     S.gated = c->gated;
     S.logits = c->logits;
     S.normed = c->normed;
-    S.attn_part = c->attn_part;
-    S.splits = splits_for(c->max_ctx);
+    S.scores = c->scores;
+    S.attn_out = c->attn_out;
+    S.score_stride = splits_for(c->max_ctx) * kAttnChunk;
     S.pos = nullptr;
     S.pos_base = 0;
     S.seq_fixed = 0xFFFFFFFFu;
@@ -722,7 +725,7 @@ static enx_status ensure_prefill(enx_ctx* c, uint32_t chunk) {
     ENX_TRY(dalloc(&c->pf_t, chunk * H, "prefill tmp"));
     ENX_TRY(dalloc(&c->pf_g, chunk * I, "prefill gate"));
     ENX_TRY(dalloc(&c->pf_u, chunk * I, "prefill up"));
-    ENX_TRY(dalloc(&c->pf_part, (size_t)chunk * splits_for(c->max_ctx) * C.heads * (C.head_dim + 2), "prefill partials"));
+    ENX_TRY(dalloc(&c->pf_part, (size_t)chunk * splits_for(c->max_ctx) * kAttnChunk * C.heads, "prefill scores"));
     ENX_TRY(dalloc(&c->pf_ids, chunk, "prefill ids"));
     c->pf_chunk = chunk;
     return ENX_OK;
@@ -749,7 +752,7 @@ extern "C" enx_status enx_prefill(enx_ctx* c, uint32_t seq, const uint32_t* ids,
     StepArgs S = step_args(c);
     S.seq_fixed = seq;
     S.q = c->pf_q2;
-    S.attn_part = c->pf_part;
+    S.scores = c->pf_part;
     for (uint32_t begin0 = 0; begin0 < n; begin0 += chunk) {
         const uint32_t m = n - begin0 < chunk ? n - begin0 : chunk;
         const uint32_t begin = c->filled[seq];
@@ -764,12 +767,11 @@ extern "C" enx_status enx_prefill(enx_ctx* c, uint32_t seq, const uint32_t* ids,
             ENX_CUDA(launch_matmul(4, c->pf_n, L.wq, L.bq, c->pf_q, m, H, 0, st, false));
             ENX_CUDA(launch_matmul(4, c->pf_n, L.wk, L.bk, c->pf_k, m, kv, 0, st, false));
             ENX_CUDA(launch_matmul(4, c->pf_n, L.wv, L.bv, c->pf_v, m, kv, 0, st, false));
-            ENX_CUDA(launch_rope(c->pf_q, c->pf_q2, c->rope_cos, c->rope_sin, m, C.heads, C.head_dim, begin, 0, st));
-            ENX_CUDA(launch_rope(c->pf_k, c->pf_k2, c->rope_cos, c->rope_sin, m, C.kv_heads, C.head_dim, begin, 0, st));
+            ENX_CUDA(launch_rope_d(c->pf_q, c->pf_q2, c->rope_cos, c->rope_sin, m, C.heads, C.head_dim, begin, 0, st));
+            ENX_CUDA(launch_rope_d(c->pf_k, c->pf_k2, c->rope_cos, c->rope_sin, m, C.kv_heads, C.head_dim, begin, 0, st));
             ENX_CUDA(launch_cache_pack(c->pf_k2, c->kcache + S.cache_offset(seq, l, begin), m * kv, 0, st));
             ENX_CUDA(launch_cache_pack(c->pf_v, c->vcache + S.cache_offset(seq, l, begin), m * kv, 0, st));
-            ENX_CUDA(launch_attn(S, l, m, st));
-            ENX_CUDA(launch_attn_merge(S, c->pf_att, m, st));
+            ENX_CUDA(launch_attn(S, l, m, c->pf_att, st, false));
             ENX_CUDA(launch_matmul(4, c->pf_att, L.wo, nullptr, c->pf_t, m, H, 0, st, false));
             ENX_CUDA(launch_add(c->pf_x, c->pf_t, c->pf_x, m * H, st));
             ENX_CUDA(launch_rmsnorm(c->pf_x, L.norm_post, c->pf_n, m, H, C.rms_norm_eps, st));

@@ -5,7 +5,7 @@
 
 namespace enx {
 
-constexpr uint32_t kAttnChunk = 64;  // positions per decode-attention split
+constexpr uint32_t kAttnChunk = 64;  // positions per attention-score split
 
 // Buffers and geometry of one decode step (shared by every layer of the step).
 struct StepArgs {
@@ -16,13 +16,14 @@ struct StepArgs {
     float* gated;          // [MT][intermediate]
     float* logits;         // [MT][vocab]
     float* normed;         // [MT][hidden] final-norm output
-    float* attn_part;      // [MT][splits][heads][head_dim + 2]
-    uint32_t splits;       // max splits = ceil(max_context / kAttnChunk)
+    float* scores;         // [MT][heads][score_stride] attention scores (workspace)
+    float* attn_out;       // [MT][hidden] attention output
+    uint32_t score_stride; // >= positions attended (a multiple of kAttnChunk)
     const uint32_t* pos;   // [MT] position written this step (device), or null: pos_base + t
     uint32_t pos_base;
-    uint32_t seq_fixed;    // sequence of every token, or kAnySeq: token t is sequence t
-    const float* rope_cos; // [max_context][head_dim/2]
-    const float* rope_sin;
+    uint32_t seq_fixed;    // sequence of every token, or 0xFFFFFFFF: token t is sequence t
+    const double* rope_cos;  // [max_context][head_dim/2], f64 (the reference's rotation precision)
+    const double* rope_sin;
     uint16_t* kcache;      // f16 bits, [seq][layer][max_context][kv_heads*head_dim]
     uint16_t* vcache;
     uint32_t layers, max_context;
@@ -50,6 +51,22 @@ struct HeadArgs {
     const float* norm;
 };
 
+// RoPE of one pair in the reference's arithmetic (test/reference/ops.ts:103-109): f64 products
+// rounded separately (no fused multiply-add), one rounding to float.
+__device__ __forceinline__ void rope_pair(float& a, float& b, double c, double s) {
+    const double da = a, db = b;
+    const float ra = (float)__dsub_rn(__dmul_rn(da, c), __dmul_rn(db, s));
+    const float rb = (float)__dadd_rn(__dmul_rn(db, c), __dmul_rn(da, s));
+    a = ra;
+    b = rb;
+}
+
+// SiLU(g) * u in double, rounded once (test/reference/ops.ts:207-216).
+__device__ __forceinline__ float silu_mul_value(float g, float u) {
+    const double gd = g;
+    return (float)__dmul_rn(__ddiv_rn(gd, __dadd_rn(1.0, exp(-gd))), (double)u);
+}
+
 int num_sms();
 cudaError_t launch_embed(const uint32_t* ids, const QW& table, int bits, float* out, uint32_t seq,
                          uint32_t row_begin, uint32_t row_count, uint32_t out_stride,
@@ -59,9 +76,8 @@ cudaError_t launch_matmul(int bits, const float* x, const QW& w, const float* bi
                           bool pdl);
 cudaError_t launch_layer(uint32_t mt, const LayerArgs& L, const StepArgs& S, cudaStream_t st);
 cudaError_t launch_head(uint32_t mt, int bits, const HeadArgs& Hd, const StepArgs& S, cudaStream_t st);
-// Split-history attention of `ntok` queries (S.q rows) over the cache, then the merge into
-// out[ntok][hidden].  Used by prefill and by the raw enx_attn_* entry points.
-cudaError_t launch_attn(const StepArgs& S, uint32_t layer, uint32_t ntok, cudaStream_t st);
-cudaError_t launch_attn_merge(const StepArgs& S, float* out, uint32_t ntok, cudaStream_t st);
+// Attention of `ntok` queries (S.q rows) over the cache: scores into S.scores, then softmax and
+// V into `out` [ntok][hidden].  Used by the layer path, prefill and the raw entry points.
+cudaError_t launch_attn(const StepArgs& S, uint32_t layer, uint32_t ntok, float* out, cudaStream_t st, bool pdl);
 
 }  // namespace enx

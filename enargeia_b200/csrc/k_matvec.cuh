@@ -5,12 +5,20 @@
 // scale per 64-element block; zero-points packed 8 (int4) or 4 (int8) per u32 word, block index
 // r*(K/64) + k/64.
 //
+// Arithmetic is faithful to the reference's CPU path (test/reference/quant.ts:95-112): products
+// and sums in double, the result rounded to float once.  This is not a luxury: K and V are
+// rounded to f16 in the cache, and a float-accumulated projection that differs from the f64
+// reference in the last bit lands on the other side of an f16 rounding boundary often enough to
+// move logits by ~1e-4 after a few layers.  Done this way the device results match the CPU
+// reference except where an f64 sum taken in a different order rounds differently (about one
+// value in 10^8).
+//
 // Work split: a "chunk" is 16 bytes of packed codes (32 int4 or 16 int8 elements).  Lane l of a
-// warp always handles chunks l, l+32, ... of whatever row the warp is on, so a row is read with
-// fully coalesced 16-byte loads.  The activations sit in shared memory transposed by chunk
-// (X4[(t*F4 + j)*nchunk + c] = x[t][c*E + 4j .. 4j+3]) so that the lanes' float4 reads are
-// conflict-free.  Codes become floats with the 2^23 exponent trick and (q - z) is formed exactly,
-// then scaled once per chunk: acc += s * sum_j (q_j - z) * x_j.
+// warp handles chunks l, l+32, ... of the row it is on, so a row is read with coalesced 16-byte
+// loads.  Activations sit in shared memory as doubles transposed by chunk
+// (XD[(t*F2 + j)*nchunk + c] = x[t][c*E + 2j .. 2j+1]) so the lanes' 16-byte reads are
+// conflict-free.  A code becomes an exact double with the 2^52 exponent trick, (q - z) is exact,
+// and each chunk contributes s * sum_j (q_j - z) * x_j.
 #pragma once
 
 #include "enx_internal.cuh"
@@ -27,7 +35,7 @@ struct QW {
 template <int BITS>
 struct Geom {
     static constexpr int E = BITS == 4 ? 32 : 16;   // elements per 16-byte chunk
-    static constexpr int F4 = E / 4;                // float4 of x per chunk
+    static constexpr int F2 = E / 2;                // double2 of x per chunk
     static constexpr int CPB = kBlock / E;          // chunks per quantisation block
 };
 
@@ -37,98 +45,116 @@ __device__ __forceinline__ uint32_t zero_code(const uint32_t* zeros, uint32_t bl
     return (__ldg(zeros + (blk >> 2)) >> ((blk & 3u) * 8u)) & 0xFFu;
 }
 
-// Stage MT activation rows (x[t*K + k], optionally times `scale[t]` and `gain[k]`) into the
-// chunk-transposed layout.  Call with the whole block; ends with __syncthreads().
-template <int BITS, int MT>
-__device__ __forceinline__ void stage_x(float4* X4, const float* x, uint32_t K, const float* rs,
-                                        const float* gain) {
-    constexpr int E = Geom<BITS>::E, F4 = Geom<BITS>::F4;
-    const uint32_t nchunk = K / E;
-    const uint32_t n4 = K / 4;
-    for (uint32_t i = threadIdx.x; i < MT * n4; i += blockDim.x) {
-        uint32_t t = i / n4, e4 = i % n4;
-        float4 v = reinterpret_cast<const float4*>(x + (size_t)t * K)[e4];
-        if (rs) {
-            float s = rs[t];
-            float4 g = gain ? reinterpret_cast<const float4*>(gain)[e4] : make_float4(1.f, 1.f, 1.f, 1.f);
-            // x * scale * w, in that order (src/kernels/rmsnorm.wgsl:60)
-            v.x = v.x * s * g.x; v.y = v.y * s * g.y; v.z = v.z * s * g.z; v.w = v.w * s * g.w;
+// 2^52 + v as a double (0 <= v < 2^32): (2^52 + q) - (2^52 + z) is exactly q - z.
+__device__ __forceinline__ double magic_d(uint32_t v) { return __hiloint2double(0x43300000, (int)v); }
+
+// Chunk-transposed index of element k of token t.
+template <int BITS>
+__device__ __forceinline__ uint32_t xd_index(uint32_t t, uint32_t k, uint32_t nchunk) {
+    constexpr int E = Geom<BITS>::E, F2 = Geom<BITS>::F2;
+    return ((t * F2 + (k % E) / 2) * nchunk + k / E) * 2 + (k & 1);
+}
+
+// Per-token RMS scale 1/sqrt(mean(x^2) + eps) in double (test/reference/ops.ts:38-45), of MT
+// rows of length K, into rs[MT] (shared).  `red` needs MT * warps doubles.  Whole block; ends
+// with __syncthreads().
+template <int MT, bool CG>
+__device__ __forceinline__ void rms_scale_d(double* rs, double* red, const float* x, uint32_t K, float eps) {
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, nw = blockDim.x >> 5;
+    for (int t = 0; t < MT; ++t) {
+        double s = 0.0;
+        for (uint32_t k = threadIdx.x; k < K; k += blockDim.x) {
+            const double v = CG ? __ldcg(x + (size_t)t * K + k) : x[(size_t)t * K + k];
+            s = fma(v, v, s);
         }
-        uint32_t c = (e4 * 4) / E, j = e4 % F4;
-        X4[(t * F4 + j) * nchunk + c] = v;
+        s = warp_sum_d(s);
+        if (lane == 0) red[t * nw + warp] = s;
+    }
+    __syncthreads();
+    if ((int)threadIdx.x < MT) {
+        double tot = 0.0;
+        for (int w = 0; w < nw; ++w) tot += red[threadIdx.x * nw + w];
+        rs[threadIdx.x] = 1.0 / sqrt(tot / (double)K + (double)eps);
     }
     __syncthreads();
 }
 
-// Per-token RMS scale 1/sqrt(mean(x^2) + eps) of MT rows of length K, into rs[MT] (shared).
-// Whole block; ends with __syncthreads().
-template <int MT>
-__device__ __forceinline__ void rms_scale(float* rs, float* red, const float* x, uint32_t K,
-                                          float eps) {
-    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, nw = blockDim.x >> 5;
+// The stored (float) RMSNorm output x * scale * w, exactly as the reference rounds it.
+__device__ __forceinline__ float norm_value(float x, double scale, float w) {
+    return (float)__dmul_rn(__dmul_rn((double)x, scale), (double)w);
+}
+
+// Stage MT activation rows into the chunk-transposed double layout: rs == nullptr stages x as
+// is, otherwise the RMSNorm output (float-rounded, then widened).  Ends with __syncthreads().
+template <int BITS, int MT, bool CG>
+__device__ __forceinline__ void stage_x_d(double* XD, const float* x, uint32_t K, const double* rs,
+                                          const float* gain) {
+    const uint32_t nchunk = K / Geom<BITS>::E;
+    for (uint32_t i = threadIdx.x; i < MT * K; i += blockDim.x) {
+        const uint32_t t = i / K, k = i % K;
+        float v = CG ? __ldcg(x + i) : x[i];
+        if (rs) v = norm_value(v, rs[t], gain[k]);
+        XD[xd_index<BITS>(t, k, nchunk)] = (double)v;
+    }
+    __syncthreads();
+}
+
+// Shared inner step: one chunk of R rows (codes q[r], scale s[r], zero zc[r]) against MT tokens.
+template <int BITS, int MT, int R>
+__device__ __forceinline__ void chunk_dot(const uint4 (&q)[R], const float (&s)[R], const uint32_t (&zc)[R],
+                                          const double2* __restrict__ XD, uint32_t nchunk, uint32_t c,
+                                          double (&acc)[R][MT]) {
+    constexpr int F2 = Geom<BITS>::F2;
+    double zd[R];
+#pragma unroll
+    for (int r = 0; r < R; ++r) zd[r] = magic_d(zc[r]);
+#pragma unroll
     for (int t = 0; t < MT; ++t) {
-        float s = 0.f;
-        for (uint32_t k = threadIdx.x; k < K; k += blockDim.x) {
-            float v = x[(size_t)t * K + k];
-            s = fmaf(v, v, s);
+        double part[R];
+#pragma unroll
+        for (int r = 0; r < R; ++r) part[r] = 0.0;
+#pragma unroll
+        for (int j = 0; j < F2; ++j) {
+            const double2 xv = XD[(t * F2 + j) * nchunk + c];
+#pragma unroll
+            for (int e = 0; e < 2; ++e) {
+                const int el = j * 2 + e;
+                const int word = BITS == 4 ? el >> 3 : el >> 2;
+                const int sh = BITS == 4 ? (el & 7) * 4 : (el & 3) * 8;
+                const uint32_t mask = BITS == 4 ? 0xFu : 0xFFu;
+                const double xe = e == 0 ? xv.x : xv.y;
+#pragma unroll
+                for (int r = 0; r < R; ++r) {
+                    const uint32_t wd = word == 0 ? q[r].x : word == 1 ? q[r].y : word == 2 ? q[r].z : q[r].w;
+                    part[r] = fma(magic_d((wd >> sh) & mask) - zd[r], xe, part[r]);
+                }
+            }
         }
-        s = warp_sum(s);
-        if (lane == 0) red[warp] = s;
-        __syncthreads();
-        if (threadIdx.x == 0) {
-            float tot = 0.f;
-            for (int w = 0; w < nw; ++w) tot += red[w];
-            rs[t] = 1.0f / sqrtf(tot / (float)K + eps);
-        }
-        __syncthreads();
+#pragma unroll
+        for (int r = 0; r < R; ++r) acc[r][t] = fma(part[r], (double)s[r], acc[r][t]);
     }
 }
 
-// acc[r][t] += lane's share of row rows[r] . x[t].  Caller reduces across the warp.
+// acc[r][t] += lane's share of row rows[r] . x[t], weights read from global memory.
 template <int BITS, int MT, int R>
-__device__ __forceinline__ void dot_rows(const QW& w, const uint32_t (&rows)[R],
-                                         const float4* __restrict__ X4, uint32_t nchunk, int lane,
-                                         float (&acc)[R][MT]) {
-    constexpr int F4 = Geom<BITS>::F4, CPB = Geom<BITS>::CPB;
+__device__ __forceinline__ void dot_rows_d(const QW& w, const uint32_t (&rows)[R], const double2* __restrict__ XD,
+                                           uint32_t nchunk, int lane, double (&acc)[R][MT]) {
+    constexpr int CPB = Geom<BITS>::CPB;
     const uint4* P = reinterpret_cast<const uint4*>(w.packed);
     const uint32_t bpr = w.cols / kBlock;
     for (uint32_t c = lane; c < nchunk; c += 32) {
         uint4 q[R];
+        float s[R];
+        uint32_t zc[R];
 #pragma unroll
         for (int r = 0; r < R; ++r) q[r] = ld_stream(P + (size_t)rows[r] * nchunk + c);
-        float s[R], zf[R];
 #pragma unroll
         for (int r = 0; r < R; ++r) {
-            uint32_t blk = rows[r] * bpr + c / CPB;
+            const uint32_t blk = rows[r] * bpr + c / CPB;
             s[r] = __ldg(w.scales + blk);
-            zf[r] = magic_u(zero_code<BITS>(w.zeros, blk));
+            zc[r] = zero_code<BITS>(w.zeros, blk);
         }
-#pragma unroll
-        for (int t = 0; t < MT; ++t) {
-            float part[R];
-#pragma unroll
-            for (int r = 0; r < R; ++r) part[r] = 0.f;
-#pragma unroll
-            for (int j = 0; j < F4; ++j) {
-                float4 xv = X4[(t * F4 + j) * nchunk + c];
-                float xs[4] = {xv.x, xv.y, xv.z, xv.w};
-#pragma unroll
-                for (int e = 0; e < 4; ++e) {
-                    const int el = j * 4 + e;          // element within the chunk
-                    const int word = BITS == 4 ? el >> 3 : el >> 2;
-                    const int sh = BITS == 4 ? (el & 7) * 4 : (el & 3) * 8;
-                    const uint32_t mask = BITS == 4 ? 0xFu : 0xFFu;
-#pragma unroll
-                    for (int r = 0; r < R; ++r) {
-                        uint32_t wd = word == 0 ? q[r].x : word == 1 ? q[r].y : word == 2 ? q[r].z : q[r].w;
-                        float wv = magic_u((wd >> sh) & mask) - zf[r];  // exact q - z
-                        part[r] = fmaf(wv, xs[e], part[r]);
-                    }
-                }
-            }
-#pragma unroll
-            for (int r = 0; r < R; ++r) acc[r][t] = fmaf(part[r], s[r], acc[r][t]);
-        }
+        chunk_dot<BITS, MT, R>(q, s, zc, XD, nchunk, c, acc);
     }
 }
 

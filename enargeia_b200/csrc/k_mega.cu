@@ -274,102 +274,32 @@ __device__ bool grid_sync(const MegaArgs& A, uint32_t& index, int* s_fail) {
 
 template <int BITS, int MT, int R>
 __device__ __forceinline__ void dot_staged(const uint8_t* slot, const SRange& S, const uint32_t (&rows)[R],
-                                           const float4* __restrict__ X4, uint32_t nchunk, int lane,
-                                           float (&acc)[R][MT]) {
-    constexpr int F4 = Geom<BITS>::F4, CPB = Geom<BITS>::CPB;
+                                           const double2* __restrict__ XD, uint32_t nchunk, int lane,
+                                           double (&acc)[R][MT]) {
+    constexpr int CPB = Geom<BITS>::CPB;
     const uint32_t bpr = S.w->cols / kBlock;
     const uint4* P = reinterpret_cast<const uint4*>(slot + S.off_p);
     const float* sc = reinterpret_cast<const float*>(slot + S.off_s);
     const uint32_t* zw = reinterpret_cast<const uint32_t*>(slot + S.off_z);
     for (uint32_t c = lane; c < nchunk; c += 32) {
         uint4 q[R];
-        float s[R], zf[R];
+        float s[R];
+        uint32_t zc[R];
 #pragma unroll
         for (int r = 0; r < R; ++r) {
-            const uint32_t lr = rows[r] - S.r0;
-            q[r] = P[(size_t)lr * nchunk + c];
+            q[r] = P[(size_t)(rows[r] - S.r0) * nchunk + c];
             const uint32_t blk = rows[r] * bpr + c / CPB;
             s[r] = sc[blk - S.s_base];
-            const uint32_t zc = BITS == 4 ? (zw[(blk >> 3) - S.z_base] >> ((blk & 7u) * 4u)) & 0xFu
-                                          : (zw[(blk >> 2) - S.z_base] >> ((blk & 3u) * 8u)) & 0xFFu;
-            zf[r] = magic_u(zc);
+            zc[r] = BITS == 4 ? (zw[(blk >> 3) - S.z_base] >> ((blk & 7u) * 4u)) & 0xFu
+                              : (zw[(blk >> 2) - S.z_base] >> ((blk & 3u) * 8u)) & 0xFFu;
         }
-#pragma unroll
-        for (int t = 0; t < MT; ++t) {
-            float part[R];
-#pragma unroll
-            for (int r = 0; r < R; ++r) part[r] = 0.f;
-#pragma unroll
-            for (int j = 0; j < F4; ++j) {
-                const float4 xv = X4[(t * F4 + j) * nchunk + c];
-                const float xs[4] = {xv.x, xv.y, xv.z, xv.w};
-#pragma unroll
-                for (int e = 0; e < 4; ++e) {
-                    const int el = j * 4 + e;
-                    const int word = BITS == 4 ? el >> 3 : el >> 2;
-                    const int sh = BITS == 4 ? (el & 7) * 4 : (el & 3) * 8;
-                    const uint32_t mask = BITS == 4 ? 0xFu : 0xFFu;
-#pragma unroll
-                    for (int r = 0; r < R; ++r) {
-                        const uint32_t wd = word == 0 ? q[r].x : word == 1 ? q[r].y : word == 2 ? q[r].z : q[r].w;
-                        part[r] = fmaf(magic_u((wd >> sh) & mask) - zf[r], xs[e], part[r]);
-                    }
-                }
-            }
-#pragma unroll
-            for (int r = 0; r < R; ++r) acc[r][t] = fmaf(part[r], s[r], acc[r][t]);
-        }
+        chunk_dot<BITS, MT, R>(q, s, zc, XD, nchunk, c, acc);
     }
-}
-
-// RMSNorm of MT rows of x (read from L2) into the chunk-transposed activation layout.
-template <int BITS, int MT>
-__device__ void norm_stage(float4* X4, float* rs, float* red, const float* x, uint32_t K, const float* gain,
-                           float eps) {
-    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    for (int t = 0; t < MT; ++t) {
-        float s = 0.f;
-        for (uint32_t k = threadIdx.x; k < K; k += blockDim.x) {
-            const float v = ldcg(x + (size_t)t * K + k);
-            s = fmaf(v, v, s);
-        }
-        s = warp_sum(s);
-        if (lane == 0) red[t * kMWarps + warp] = s;
-    }
-    __syncthreads();
-    if (threadIdx.x < MT) {
-        float tot = 0.f;
-        for (int w = 0; w < kMWarps; ++w) tot += red[threadIdx.x * kMWarps + w];
-        rs[threadIdx.x] = 1.0f / sqrtf(tot / (float)K + eps);
-    }
-    __syncthreads();
-    constexpr int E = Geom<BITS>::E, F4 = Geom<BITS>::F4;
-    const uint32_t nchunk = K / E, n4 = K / 4;
-    for (uint32_t i = threadIdx.x; i < MT * n4; i += blockDim.x) {
-        const uint32_t t = i / n4, e4 = i % n4;
-        float4 v = __ldcg(reinterpret_cast<const float4*>(x + (size_t)t * K) + e4);
-        const float4 g = reinterpret_cast<const float4*>(gain)[e4];
-        const float s = rs[t];
-        v.x = v.x * s * g.x; v.y = v.y * s * g.y; v.z = v.z * s * g.z; v.w = v.w * s * g.w;
-        X4[(t * F4 + e4 % F4) * nchunk + (e4 * 4) / E] = v;
-    }
-    __syncthreads();
-}
-
-template <int BITS, int MT>
-__device__ void plain_stage(float4* X4, const float* x, uint32_t K) {
-    constexpr int E = Geom<BITS>::E, F4 = Geom<BITS>::F4;
-    const uint32_t nchunk = K / E, n4 = K / 4;
-    for (uint32_t i = threadIdx.x; i < MT * n4; i += blockDim.x) {
-        const uint32_t t = i / n4, e4 = i % n4;
-        X4[(t * F4 + e4 % F4) * nchunk + (e4 * 4) / E] = __ldcg(reinterpret_cast<const float4*>(x + (size_t)t * K) + e4);
-    }
-    __syncthreads();
 }
 
 template <int MT>
-__device__ __forceinline__ float pick(const float (&a)[MT], int t) {
-    float v = 0.f;
+__device__ __forceinline__ double pick(const double (&a)[MT], int t) {
+    double v = 0.0;
 #pragma unroll
     for (int i = 0; i < MT; ++i)
         if (i == t) v = a[i];
@@ -382,7 +312,7 @@ __device__ __forceinline__ float pick(const float (&a)[MT], int t) {
 template <int MT, int HB>
 __global__ void __launch_bounds__(kMThreads, 1) k_mega(const __grid_constant__ MegaArgs A) {
     extern __shared__ __align__(128) uint8_t smem[];
-    __shared__ float rs[MT], red[MT * kMWarps];
+    __shared__ double rs[MT], red[MT * kMWarps];
     __shared__ int s_fail;
     const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
     const uint32_t G = gridDim.x, c = blockIdx.x;
@@ -394,9 +324,10 @@ __global__ void __launch_bounds__(kMThreads, 1) k_mega(const __grid_constant__ M
     R.slot_bytes = A.slot_bytes;
     R.slots = smem + 128;
     R.total = num_slices(A);
-    float4* X4 = reinterpret_cast<float4*>(smem + 128 + (size_t)A.nslots * A.slot_bytes);
-    float* Xf = reinterpret_cast<float*>(X4);
-    float* qs = Xf + (size_t)MT * A.x4_floats;  // [MT][H]: queries for attention, or a temporary
+    double2* XD = reinterpret_cast<double2*>(smem + 128 + (size_t)A.nslots * A.slot_bytes);
+    double* Xd = reinterpret_cast<double*>(XD);   // [MT][x4] activations as doubles
+    float* Xf = reinterpret_cast<float*>(XD);     // the same area, as float attention scratch
+    float* qs = reinterpret_cast<float*>(Xd + (size_t)MT * A.x4_floats);  // [MT][H] queries / temporary
     uint16_t* kvs = reinterpret_cast<uint16_t*>(qs + (size_t)MT * H);  // [kKvStage][kv_heads*hd] f16
 
     if (tid == 0) {
@@ -439,31 +370,11 @@ __global__ void __launch_bounds__(kMThreads, 1) k_mega(const __grid_constant__ M
                 if (k >= o0 && k < o1) A.S.x[i] = v;
             }
             __syncthreads();
-            for (int t = 0; t < MT; ++t) {
-                float s = 0.f;
-                for (uint32_t k = tid; k < H; k += blockDim.x) s = fmaf(qs[t * H + k], qs[t * H + k], s);
-                s = warp_sum(s);
-                if (lane == 0) red[t * kMWarps + warp] = s;
-            }
-            __syncthreads();
-            if (tid < MT) {
-                float tot = 0.f;
-                for (int w = 0; w < kMWarps; ++w) tot += red[tid * kMWarps + w];
-                rs[tid] = 1.0f / sqrtf(tot / (float)H + A.eps);
-            }
-            __syncthreads();
-            const uint32_t nchunk = H / 32, n4 = H / 4;
-            for (uint32_t i = tid; i < MT * n4; i += blockDim.x) {
-                const uint32_t t = i / n4, e4 = i % n4;
-                float4 v = reinterpret_cast<const float4*>(qs + (size_t)t * H)[e4];
-                const float4 g = reinterpret_cast<const float4*>(La.norm_in)[e4];
-                const float s = rs[t];
-                v.x = v.x * s * g.x; v.y = v.y * s * g.y; v.z = v.z * s * g.z; v.w = v.w * s * g.w;
-                X4[(t * 8 + e4 % 8) * nchunk + (e4 * 4) / 32] = v;
-            }
-            __syncthreads();
+            rms_scale_d<MT, false>(rs, red, qs, H, A.eps);
+            stage_x_d<4, MT, false>(Xd, qs, H, rs, La.norm_in);
         } else {
-            norm_stage<4, MT>(X4, rs, red, A.S.x, H, La.norm_in, A.eps);
+            rms_scale_d<MT, true>(rs, red, A.S.x, H, A.eps);
+            stage_x_d<4, MT, true>(Xd, A.S.x, H, rs, La.norm_in);
         }
         plan_slice(A, slice, P);
         if (!wait_slice(A, R, slice)) { fail_out(); return; }
@@ -477,24 +388,21 @@ __global__ void __launch_bounds__(kMThreads, 1) k_mega(const __grid_constant__ M
                 const SRange& Ra = P.r[(pi / 4) * 2];
                 const SRange& Rb = P.r[(pi / 4) * 2 + 1];
                 const uint32_t ra = Ra.r0 + pi % 4, rb = Rb.r0 + pi % 4;
-                float aa[1][MT] = {}, ab[1][MT] = {};
+                double aa[1][MT] = {}, ab[1][MT] = {};
                 const uint32_t rowa[1] = {ra}, rowb[1] = {rb};
-                dot_staged<4, MT, 1>(slot, Ra, rowa, X4, nchunk, lane, aa);
-                dot_staged<4, MT, 1>(slot, Rb, rowb, X4, nchunk, lane, ab);
+                dot_staged<4, MT, 1>(slot, Ra, rowa, XD, nchunk, lane, aa);
+                dot_staged<4, MT, 1>(slot, Rb, rowb, XD, nchunk, lane, ab);
 #pragma unroll
-                for (int t = 0; t < MT; ++t) { aa[0][t] = warp_sum(aa[0][t]); ab[0][t] = warp_sum(ab[0][t]); }
+                for (int t = 0; t < MT; ++t) { aa[0][t] = warp_sum_d(aa[0][t]); ab[0][t] = warp_sum_d(ab[0][t]); }
                 if (lane < MT) {
                     const int kind = Ra.w == &La.wq ? 0 : Ra.w == &La.wk ? 1 : 2;
                     const float* bias = kind == 0 ? La.bq : kind == 1 ? La.bk : La.bv;
-                    float a = pick<MT>(aa[0], lane) + bias[ra], b = pick<MT>(ab[0], lane) + bias[rb];
+                    float a = (float)(pick<MT>(aa[0], lane) + (double)bias[ra]);
+                    float b = (float)(pick<MT>(ab[0], lane) + (double)bias[rb]);
                     const uint32_t head = ra / hd, i = ra % hd;
                     const uint32_t pos = A.S.pos_of(lane);
-                    if (kind != 2) {  // half-rotation RoPE (src/kernels/rope.wgsl:42-52)
-                        const float cs = A.S.rope_cos[(size_t)pos * half + i], sn = A.S.rope_sin[(size_t)pos * half + i];
-                        const float x0 = a * cs - b * sn, x1 = b * cs + a * sn;
-                        a = x0;
-                        b = x1;
-                    }
+                    if (kind != 2)  // half-rotation RoPE (src/kernels/rope.wgsl:42-52)
+                        rope_pair(a, b, A.S.rope_cos[(size_t)pos * half + i], A.S.rope_sin[(size_t)pos * half + i]);
                     if (kind == 0) {
                         A.S.q[(size_t)lane * H + ra] = a;
                         A.S.q[(size_t)lane * H + rb] = b;
@@ -527,41 +435,23 @@ __global__ void __launch_bounds__(kMThreads, 1) k_mega(const __grid_constant__ M
                 const uint16_t* Vc = A.S.vcache + A.S.cache_offset(A.S.seq_of(t), l, 0);
                 const float* qt = qs + (size_t)t * H;
                 // K and V pass through shared memory kKvStage positions at a time: all threads load
-                // a chunk with independent 16-byte reads (one L2 latency per chunk), then compute
+                // a chunk with independent 16-byte reads, then compute.  Arithmetic and rounding
+                // follow test/reference/ops.ts:123-204 (double sums, float scores and weights).
                 const uint32_t row16 = kvd / 8;  // uint4 per cached position
+                const double scale = 1.0 / sqrt((double)hd);
                 for (uint32_t j0 = 0; j0 < npos; j0 += kKvStage) {
                     const uint32_t n = min(kKvStage, npos - j0);
                     for (uint32_t i = tid; i < n * row16; i += blockDim.x)
                         reinterpret_cast<uint4*>(kvs)[i] = __ldcg(reinterpret_cast<const uint4*>(Kc + (size_t)j0 * kvd) + i);
                     __syncthreads();
-                    for (uint32_t w = tid; w < n * A.kv_heads; w += blockDim.x) {
-                        const uint32_t j = w / A.kv_heads, g = w % A.kv_heads;
-                        const uint4* kr = reinterpret_cast<const uint4*>(kvs + (size_t)j * kvd + g * hd);
-                        float acc[kMaxGroup];
-#pragma unroll
-                        for (int h = 0; h < (int)kMaxGroup; ++h) acc[h] = 0.f;
-                        for (uint32_t d8 = 0; d8 < hd / 8; ++d8) {
-                            const uint4 u = kr[d8];
-                            const __half2* h2 = reinterpret_cast<const __half2*>(&u);
-                            float kf[8];
-#pragma unroll
-                            for (int e = 0; e < 4; ++e) {
-                                const float2 f2 = __half22float2(h2[e]);
-                                kf[2 * e] = f2.x;
-                                kf[2 * e + 1] = f2.y;
-                            }
-#pragma unroll
-                            for (int h = 0; h < (int)kMaxGroup; ++h) {
-                                if (h < (int)group) {
-                                    const float* qh = qt + (g * group + h) * hd + d8 * 8;
-#pragma unroll
-                                    for (int e = 0; e < 8; ++e) acc[h] = fmaf(qh[e], kf[e], acc[h]);
-                                }
-                            }
-                        }
-#pragma unroll
-                        for (int h = 0; h < (int)kMaxGroup; ++h)
-                            if (h < (int)group) sc[(g * group + h) * npos + j0 + j] = acc[h] * A.attn_scale;
+                    for (uint32_t w = tid; w < n * A.heads; w += blockDim.x) {
+                        const uint32_t j = w / A.heads, h = w % A.heads, g = h / group;
+                        const uint16_t* kr = kvs + (size_t)j * kvd + g * hd;
+                        const float* qh = qt + h * hd;
+                        double acc = 0.0;
+                        for (uint32_t d = 0; d < hd; ++d)
+                            acc = fma((double)qh[d], (double)__half2float(__ushort_as_half(kr[d])), acc);
+                        sc[h * npos + j0 + j] = (float)(acc * scale);
                     }
                     __syncthreads();
                 }
@@ -569,17 +459,17 @@ __global__ void __launch_bounds__(kMThreads, 1) k_mega(const __grid_constant__ M
                     float m = -INFINITY;
                     for (uint32_t j = lane; j < npos; j += 32) m = fmaxf(m, sc[h * npos + j]);
                     m = warp_max(m);
-                    float s = 0.f;
+                    double s = 0.0;
                     for (uint32_t j = lane; j < npos; j += 32) {
-                        const float e = __expf(sc[h * npos + j] - m);
-                        sc[h * npos + j] = e;
+                        const double e = exp((double)sc[h * npos + j] - (double)m);
+                        sc[h * npos + j] = (float)e;
                         s += e;
                     }
-                    s = warp_sum(s);
-                    for (uint32_t j = lane; j < npos; j += 32) sc[h * npos + j] /= s;
+                    s = warp_sum_d(s);
+                    for (uint32_t j = lane; j < npos; j += 32) sc[h * npos + j] = (float)((double)sc[h * npos + j] / s);
                 }
                 __syncthreads();
-                float acc2[2] = {0.f, 0.f};
+                double acc2[2] = {0.0, 0.0};
                 for (uint32_t j0 = 0; j0 < npos; j0 += kKvStage) {
                     const uint32_t n = min(kKvStage, npos - j0);
                     for (uint32_t i = tid; i < n * row16; i += blockDim.x)
@@ -590,20 +480,20 @@ __global__ void __launch_bounds__(kMThreads, 1) k_mega(const __grid_constant__ M
                         const uint32_t h = o / hd, d = o % hd, g = h / group;
                         const float* wv = sc + h * npos + j0;
                         const uint16_t* vp = kvs + g * hd + d;
-                        float a = acc2[k & 1];
-                        for (uint32_t j = 0; j < n; ++j) a = fmaf(wv[j], __half2float(__ushort_as_half(vp[(size_t)j * kvd])), a);
+                        double a = acc2[k & 1];
+                        for (uint32_t j = 0; j < n; ++j)
+                            a = fma((double)wv[j], (double)__half2float(__ushort_as_half(vp[(size_t)j * kvd])), a);
                         acc2[k & 1] = a;
                     }
                     __syncthreads();
                 }
-                out_v[t * 2 + 0] = acc2[0];
-                out_v[t * 2 + 1] = acc2[1];
+                out_v[t * 2 + 0] = (float)acc2[0];
+                out_v[t * 2 + 1] = (float)acc2[1];
             }
-            const uint32_t nchunk = H / 32;
             for (int t = 0; t < MT; ++t) {
                 uint32_t k = 0;
                 for (uint32_t o = tid; o < H; o += blockDim.x, ++k)
-                    Xf[((t * 8 + (o % 32) / 4) * nchunk + o / 32) * 4 + (o % 4)] = out_v[t * 2 + k];
+                    Xd[xd_index<4>(t, o, H / 32)] = (double)out_v[t * 2 + k];
             }
             __syncthreads();
         }
@@ -614,14 +504,14 @@ __global__ void __launch_bounds__(kMThreads, 1) k_mega(const __grid_constant__ M
             const uint8_t* slot = R.slots + (size_t)(slice % R.nslots) * R.slot_bytes;
             const SRange& S = P.r[0];
             for (uint32_t r = S.r0 + warp; r < S.r1; r += kMWarps) {
-                float acc[1][MT] = {};
+                double acc[1][MT] = {};
                 const uint32_t rows[1] = {r};
-                dot_staged<4, MT, 1>(slot, S, rows, X4, H / 32, lane, acc);
+                dot_staged<4, MT, 1>(slot, S, rows, XD, H / 32, lane, acc);
 #pragma unroll
-                for (int t = 0; t < MT; ++t) acc[0][t] = warp_sum(acc[0][t]);
+                for (int t = 0; t < MT; ++t) acc[0][t] = warp_sum_d(acc[0][t]);
                 if (lane < MT) {
                     float* xp = A.S.x + (size_t)lane * H + r;
-                    *xp = ldcg(xp) + pick<MT>(acc[0], lane);
+                    *xp = ldcg(xp) + (float)pick<MT>(acc[0], lane);
                 }
             }
         }
@@ -631,7 +521,8 @@ __global__ void __launch_bounds__(kMThreads, 1) k_mega(const __grid_constant__ M
         stamp(A, 3 * (4 * l + 2));
 
         // ---------------- S4: RMSNorm + gate|up + SiLU --------------------------------------
-        norm_stage<4, MT>(X4, rs, red, A.S.x, H, La.norm_post, A.eps);
+        rms_scale_d<MT, true>(rs, red, A.S.x, H, A.eps);
+        stage_x_d<4, MT, true>(Xd, A.S.x, H, rs, La.norm_post);
         plan_slice(A, slice, P);
         if (!wait_slice(A, R, slice)) { fail_out(); return; }
         stamp(A, 3 * (4 * l + 2) + 1);
@@ -640,16 +531,15 @@ __global__ void __launch_bounds__(kMThreads, 1) k_mega(const __grid_constant__ M
             const SRange& Sg = P.r[0];
             const SRange& Su = P.r[1];
             for (uint32_t r = Sg.r0 + warp; r < Sg.r1; r += kMWarps) {
-                float ag[1][MT] = {}, au[1][MT] = {};
+                double ag[1][MT] = {}, au[1][MT] = {};
                 const uint32_t rows[1] = {r};
-                dot_staged<4, MT, 1>(slot, Sg, rows, X4, H / 32, lane, ag);
-                dot_staged<4, MT, 1>(slot, Su, rows, X4, H / 32, lane, au);
+                dot_staged<4, MT, 1>(slot, Sg, rows, XD, H / 32, lane, ag);
+                dot_staged<4, MT, 1>(slot, Su, rows, XD, H / 32, lane, au);
 #pragma unroll
-                for (int t = 0; t < MT; ++t) { ag[0][t] = warp_sum(ag[0][t]); au[0][t] = warp_sum(au[0][t]); }
-                if (lane < MT) {
-                    const float g = pick<MT>(ag[0], lane), u = pick<MT>(au[0], lane);
-                    A.S.gated[(size_t)lane * I + r] = g / (1.0f + expf(-g)) * u;
-                }
+                for (int t = 0; t < MT; ++t) { ag[0][t] = warp_sum_d(ag[0][t]); au[0][t] = warp_sum_d(au[0][t]); }
+                if (lane < MT)
+                    A.S.gated[(size_t)lane * I + r] =
+                        silu_mul_value((float)pick<MT>(ag[0], lane), (float)pick<MT>(au[0], lane));
             }
         }
         stamp(A, 3 * (4 * l + 2) + 2);
@@ -658,7 +548,7 @@ __global__ void __launch_bounds__(kMThreads, 1) k_mega(const __grid_constant__ M
         stamp(A, 3 * (4 * l + 3));
 
         // ---------------- S5: down + residual -----------------------------------------------
-        plain_stage<4, MT>(X4, A.S.gated, I);
+        stage_x_d<4, MT, true>(Xd, A.S.gated, I, nullptr, nullptr);
         plan_slice(A, slice, P);
         if (!wait_slice(A, R, slice)) { fail_out(); return; }
         stamp(A, 3 * (4 * l + 3) + 1);
@@ -666,14 +556,14 @@ __global__ void __launch_bounds__(kMThreads, 1) k_mega(const __grid_constant__ M
             const uint8_t* slot = R.slots + (size_t)(slice % R.nslots) * R.slot_bytes;
             const SRange& S = P.r[0];
             for (uint32_t r = S.r0 + warp; r < S.r1; r += kMWarps) {
-                float acc[1][MT] = {};
+                double acc[1][MT] = {};
                 const uint32_t rows[1] = {r};
-                dot_staged<4, MT, 1>(slot, S, rows, X4, I / 32, lane, acc);
+                dot_staged<4, MT, 1>(slot, S, rows, XD, I / 32, lane, acc);
 #pragma unroll
-                for (int t = 0; t < MT; ++t) acc[0][t] = warp_sum(acc[0][t]);
+                for (int t = 0; t < MT; ++t) acc[0][t] = warp_sum_d(acc[0][t]);
                 if (lane < MT) {
                     float* xp = A.S.x + (size_t)lane * H + r;
-                    *xp = ldcg(xp) + pick<MT>(acc[0], lane);
+                    *xp = ldcg(xp) + (float)pick<MT>(acc[0], lane);
                 }
             }
         }
@@ -684,10 +574,11 @@ __global__ void __launch_bounds__(kMThreads, 1) k_mega(const __grid_constant__ M
 
     // ---------------- final RMSNorm + tied head ---------------------------------------------
     stamp(A, 3 * (4 * A.layers));
-    norm_stage<HB, MT>(X4, rs, red, A.S.x, H, A.final_norm, A.eps);
+    rms_scale_d<MT, true>(rs, red, A.S.x, H, A.eps);
+    stage_x_d<HB, MT, true>(Xd, A.S.x, H, rs, A.final_norm);
     if (c == 0)
         for (uint32_t i = tid; i < MT * H; i += blockDim.x)
-            A.S.normed[i] = ldcg(A.S.x + i) * rs[i / H] * A.final_norm[i % H];
+            A.S.normed[i] = norm_value(ldcg(A.S.x + i), rs[i / H], A.final_norm[i % H]);
     const uint32_t nchunk = H / Geom<HB>::E;
     while (slice < R.total) {
         Plan P;
@@ -698,15 +589,15 @@ __global__ void __launch_bounds__(kMThreads, 1) k_mega(const __grid_constant__ M
             const SRange& S = P.r[0];
             for (uint32_t r0 = S.r0 + 2 * warp; r0 < S.r1; r0 += 2 * kMWarps) {
                 const uint32_t rows[2] = {r0, min(r0 + 1, S.r1 - 1)};
-                float acc[2][MT] = {};
-                dot_staged<HB, MT, 2>(slot, S, rows, X4, nchunk, lane, acc);
+                double acc[2][MT] = {};
+                dot_staged<HB, MT, 2>(slot, S, rows, XD, nchunk, lane, acc);
 #pragma unroll
                 for (int r = 0; r < 2; ++r)
 #pragma unroll
-                    for (int t = 0; t < MT; ++t) acc[r][t] = warp_sum(acc[r][t]);
+                    for (int t = 0; t < MT; ++t) acc[r][t] = warp_sum_d(acc[r][t]);
                 if (lane < MT) {
-                    A.S.logits[(size_t)lane * A.vocab + r0] = pick<MT>(acc[0], lane);
-                    if (r0 + 1 < S.r1) A.S.logits[(size_t)lane * A.vocab + r0 + 1] = pick<MT>(acc[1], lane);
+                    A.S.logits[(size_t)lane * A.vocab + r0] = (float)pick<MT>(acc[0], lane);
+                    if (r0 + 1 < S.r1) A.S.logits[(size_t)lane * A.vocab + r0 + 1] = (float)pick<MT>(acc[1], lane);
                 }
             }
         }
@@ -759,14 +650,14 @@ MegaGeometry mega_geometry(uint32_t mt, const MegaArgs& A) {
     if (hc > slot) slot = hc;
     slot = (slot + 127) & ~127u;
     g.slot_bytes = slot;
-    const size_t fixed = 128 + (size_t)mt * x4 * 4 + (size_t)mt * A.hidden * 4 +
+    const size_t fixed = 128 + (size_t)mt * x4 * 8 + (size_t)mt * A.hidden * 4 +
                          (size_t)kKvStage * A.kv_heads * A.head_dim * 2;
     const int64_t room = (int64_t)maxsm - (int64_t)fixed - 2048;  // static shared memory and slack
     int ns = room > 0 ? (int)(room / slot) : 0;
     if (ns > 8) ns = 8;
     g.nslots = (uint32_t)ns;
     g.smem = fixed + (size_t)g.nslots * slot;
-    g.max_positions = (uint32_t)(((size_t)mt * x4) / A.heads);  // scores share the activation area
+    g.max_positions = (uint32_t)(((size_t)mt * x4 * 2) / A.heads);  // float scores share the double area
     return g;
 }
 

@@ -1,12 +1,12 @@
 // enx_attn_decode_noalloc: decode attention that needs no caller workspace and allocates nothing.
 //
-// enx_attn_decode keeps its per-split softmax partials in a workspace the caller allocates.
+// enx_attn_decode keeps its attention scores in a workspace the caller allocates.
 // Some callers cannot allocate device memory at the point where they run attention: code that
 // runs inside a host callback or a real-time loop where cudaMalloc's implicit synchronisation is
 // not allowed, plugin hosts that hand over only fixed input/output buffers, and embedders with
-// their own memory manager that forbids outside allocations.  This variant keeps the partials
+// their own memory manager that forbids outside allocations.  This variant keeps the scores
 // in one file-scope device array instead, sized for the limits below.  Every GPU that loads the
-// library holds that array (kScratchFloats * 4 bytes, about 528 KB) until the process exits.
+// library holds that array (kScratchFloats * 4 bytes, 512 KB) until the process exits.
 
 #include <mutex>
 #include <string>
@@ -17,9 +17,9 @@
 
 namespace enx {
 
-// Capacity: up to 64 position splits (positions 0..4095) x 32 query heads x (64 + 2) floats.
+// Capacity: attention scores of up to 32 query heads x 4096 positions.
 constexpr uint32_t kNoAllocMaxPositions = 4096;
-constexpr size_t kScratchFloats = (size_t)(kNoAllocMaxPositions / kAttnChunk) * 32 * (64 + 2);
+constexpr size_t kScratchFloats = (size_t)kNoAllocMaxPositions * 32;
 
 static __device__ __align__(256) float g_attn_scratch[kScratchFloats];
 
@@ -50,14 +50,14 @@ using namespace enx;
 extern "C" enx_status enx_attn_decode_noalloc(const float* q, const uint16_t* k_cache, const uint16_t* v_cache,
                                               float* out, const enx_attn_decode_dims* d, void* stream) {
     if (!d || !q || !k_cache || !v_cache || !out) return fail(ENX_ERR_INVALID, "enx_attn_decode_noalloc: null pointer");
-    if (d->kv_heads == 0 || d->heads % d->kv_heads != 0)
-        return fail(ENX_ERR_INVALID, "enx_attn_decode_noalloc: heads must be a multiple of kv_heads");
+    if (d->kv_heads == 0 || d->heads % d->kv_heads != 0 || d->heads / d->kv_heads > 8)
+        return fail(ENX_ERR_INVALID, "enx_attn_decode_noalloc: heads must be a multiple of kv_heads, at most 8 per kv head");
     if (d->head_dim == 0 || d->head_dim % 2 != 0 || d->head_dim > 64)
         return fail(ENX_ERR_INVALID, "enx_attn_decode_noalloc: head_dim must be even and <= 64");
     if (d->cache_stride != d->kv_heads * d->head_dim)
         return fail(ENX_ERR_INVALID, "enx_attn_decode_noalloc: cache_stride must be kv_heads*head_dim");
     const uint32_t splits = (d->position + 1 + kAttnChunk - 1) / kAttnChunk;
-    const size_t need = (size_t)splits * d->heads * (d->head_dim + 2);
+    const size_t need = (size_t)splits * kAttnChunk * d->heads;
     if (d->position >= kNoAllocMaxPositions || d->heads > 32 || need > kScratchFloats)
         return fail(ENX_ERR_RANGE, "enx_attn_decode_noalloc: position " + std::to_string(d->position) + " / heads " +
                                        std::to_string(d->heads) +
@@ -65,7 +65,7 @@ extern "C" enx_status enx_attn_decode_noalloc(const float* q, const uint16_t* k_
                                        "use enx_attn_decode with a workspace");
     float* scratch = nullptr;
     ENX_TRY(scratch_for_current_device(&scratch));
-    // Every partial the merge reads is written first by the split kernel in the same call, so the
+    // Every score the softmax reads is written first by the score kernel of the same call, so the
     // shared array needs no clearing between calls.
     StepArgs S{};
     S.hidden = d->heads * d->head_dim;
@@ -73,8 +73,8 @@ extern "C" enx_status enx_attn_decode_noalloc(const float* q, const uint16_t* k_
     S.kv_heads = d->kv_heads;
     S.head_dim = d->head_dim;
     S.q = const_cast<float*>(q);
-    S.attn_part = scratch;
-    S.splits = splits;
+    S.scores = scratch;
+    S.score_stride = splits * kAttnChunk;
     S.pos = nullptr;
     S.pos_base = d->position;
     S.seq_fixed = 0;
@@ -83,7 +83,6 @@ extern "C" enx_status enx_attn_decode_noalloc(const float* q, const uint16_t* k_
     S.layers = 1;
     S.max_context = d->position + 1;
     cudaStream_t st = as_stream(stream);
-    ENX_CUDA(launch_attn(S, 0, 1, st));
-    ENX_CUDA(launch_attn_merge(S, out, 1, st));
+    ENX_CUDA(launch_attn(S, 0, 1, out, st, false));
     return ENX_OK;
 }

@@ -4,43 +4,46 @@
 // (src/kernels/silu_mul.wgsl:19-26) and add (src/kernels/add.wgsl:15-21).
 
 #include "enx_internal.cuh"
+#include "k_decode.cuh"
 #include "k_small.cuh"
 
 namespace enx {
 
+// RMSNorm in the reference's arithmetic: f64 sum of squares, f64 scale, one rounding per output.
 __global__ void k_rmsnorm(const float* __restrict__ x, const float* __restrict__ w,
                           float* __restrict__ out, uint32_t features, float eps) {
-    __shared__ float red[32];
-    __shared__ float scale;
+    __shared__ double red[32];
+    __shared__ double scale;
     const float* xr = x + (size_t)blockIdx.x * features;
-    float s = 0.f;
-    for (uint32_t f = threadIdx.x; f < features; f += blockDim.x) s = fmaf(xr[f], xr[f], s);
-    s = warp_sum(s);
+    double s = 0.0;
+    for (uint32_t f = threadIdx.x; f < features; f += blockDim.x) s = fma((double)xr[f], (double)xr[f], s);
+    s = warp_sum_d(s);
     if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = s;
     __syncthreads();
     if (threadIdx.x == 0) {
-        float t = 0.f;
+        double t = 0.0;
         for (uint32_t i = 0; i < blockDim.x / 32; ++i) t += red[i];
-        scale = 1.0f / sqrtf(t / (float)features + eps);
+        scale = 1.0 / sqrt(t / (double)features + (double)eps);
     }
     __syncthreads();
     float* o = out + (size_t)blockIdx.x * features;
-    for (uint32_t f = threadIdx.x; f < features; f += blockDim.x) o[f] = xr[f] * scale * w[f];
+    for (uint32_t f = threadIdx.x; f < features; f += blockDim.x) o[f] = norm_value(xr[f], scale, w[f]);
 }
 
-__global__ void k_rope(const float* __restrict__ x, float* __restrict__ out,
-                       const float* __restrict__ ct, const float* __restrict__ st, uint32_t seq,
-                       uint32_t heads, uint32_t hd, uint32_t pos0, uint32_t out_offset) {
+template <typename T>
+__global__ void k_rope(const float* __restrict__ x, float* __restrict__ out, const T* __restrict__ ct,
+                       const T* __restrict__ st, uint32_t seq, uint32_t heads, uint32_t hd, uint32_t pos0,
+                       uint32_t out_offset) {
     const uint32_t half = hd / 2, per_row = heads * half;
     const uint32_t total = seq * per_row;
     for (uint32_t g = blockIdx.x * blockDim.x + threadIdx.x; g < total; g += gridDim.x * blockDim.x) {
-        uint32_t s = g / per_row, rem = g % per_row, h = rem / half, i = rem % half;
-        uint32_t pos = pos0 + s;
-        float c = ct[(size_t)pos * half + i], sn = st[(size_t)pos * half + i];
-        size_t base = ((size_t)s * heads + h) * hd;
+        const uint32_t s = g / per_row, rem = g % per_row, h = rem / half, i = rem % half;
+        const uint32_t pos = pos0 + s;
+        const size_t base = ((size_t)s * heads + h) * hd;
         float a = x[base + i], b = x[base + i + half];
-        out[out_offset + base + i] = a * c - b * sn;
-        out[out_offset + base + i + half] = b * c + a * sn;
+        rope_pair(a, b, (double)ct[(size_t)pos * half + i], (double)st[(size_t)pos * half + i]);
+        out[out_offset + base + i] = a;
+        out[out_offset + base + i + half] = b;
     }
 }
 
@@ -53,8 +56,7 @@ __global__ void k_cache_pack(const float* __restrict__ src, uint16_t* __restrict
 __global__ void k_silu_mul(const float* __restrict__ g, const float* __restrict__ u,
                            float* __restrict__ out, uint32_t n) {
     for (uint32_t i = blockIdx.x * blockDim.x + threadIdx.x; i < n; i += gridDim.x * blockDim.x) {
-        float v = g[i];
-        out[i] = v / (1.0f + expf(-v)) * u[i];
+        out[i] = silu_mul_value(g[i], u[i]);
     }
 }
 
@@ -81,7 +83,15 @@ cudaError_t launch_rope(const float* x, float* out, const float* ct, const float
                         cudaStream_t st) {
     uint32_t n = seq * heads * (hd / 2);
     if (n == 0) return cudaSuccess;
-    k_rope<<<blocks_for(n), 256, 0, st>>>(x, out, ct, sn, seq, heads, hd, pos0, out_offset);
+    k_rope<float><<<blocks_for(n), 256, 0, st>>>(x, out, ct, sn, seq, heads, hd, pos0, out_offset);
+    return cudaGetLastError();
+}
+
+cudaError_t launch_rope_d(const float* x, float* out, const double* ct, const double* sn, uint32_t seq,
+                          uint32_t heads, uint32_t hd, uint32_t pos0, uint32_t out_offset, cudaStream_t st) {
+    uint32_t n = seq * heads * (hd / 2);
+    if (n == 0) return cudaSuccess;
+    k_rope<double><<<blocks_for(n), 256, 0, st>>>(x, out, ct, sn, seq, heads, hd, pos0, out_offset);
     return cudaGetLastError();
 }
 

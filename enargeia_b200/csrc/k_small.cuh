@@ -10,6 +10,8 @@ cudaError_t launch_rmsnorm(const float* x, const float* w, float* out, uint32_t 
 cudaError_t launch_rope(const float* x, float* out, const float* ct, const float* sn, uint32_t seq,
                         uint32_t heads, uint32_t hd, uint32_t pos0, uint32_t out_offset,
                         cudaStream_t st);
+cudaError_t launch_rope_d(const float* x, float* out, const double* ct, const double* sn, uint32_t seq,
+                          uint32_t heads, uint32_t hd, uint32_t pos0, uint32_t out_offset, cudaStream_t st);
 cudaError_t launch_cache_pack(const float* src, uint16_t* dst, uint32_t count, uint32_t dst_offset,
                               cudaStream_t st);
 cudaError_t launch_silu_mul(const float* g, const float* u, float* out, uint32_t n, cudaStream_t st);

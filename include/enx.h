@@ -137,7 +137,7 @@ ENX_API enx_status enx_attn_decode(const float* q, const uint16_t* k_cache, cons
 /* Same computation as enx_attn_decode, for callers that cannot allocate device memory (for
  * example code running where cudaMalloc's implicit synchronisation is not allowed, or hosts that
  * only hand over fixed buffers).  No counterpart in the reference: its WebGPU path always has a
- * buffer pool.  The split partials live in one library-owned device array (about 528 KB, held on
+ * buffer pool.  The attention scores live in one library-owned device array (512 KB, held on
  * every GPU that loads the library until exit); limits: position < 4096, heads <= 32,
  * head_dim <= 64, else ENX_ERR_RANGE.  The first call on each device looks up that array's
  * device address (cudaGetSymbolAddress, with the device current): make that first call before

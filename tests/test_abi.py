@@ -58,5 +58,7 @@ def test_bad_dims_are_rejected(lib):
 
 
 def test_workspace_sizes(lib):
-    assert lib.enx_attn_decode_workspace_bytes(2048, 14, 64) == 32 * 14 * 66 * 4
-    assert lib.enx_attn_prefill_workspace_bytes(256, 2048, 14, 64) == 256 * 32 * 14 * 66 * 4
+    # float attention scores: heads x positions rounded up to the 64-position split
+    assert lib.enx_attn_decode_workspace_bytes(2048, 14, 64) == 14 * 2048 * 4
+    assert lib.enx_attn_decode_workspace_bytes(100, 14, 64) == 14 * 128 * 4
+    assert lib.enx_attn_prefill_workspace_bytes(256, 2048, 14, 64) == 256 * 14 * 2048 * 4

@@ -15,11 +15,15 @@ pytestmark = pytest.mark.gpu
 LOGIT_ATOL, LOGIT_RTOL = 1e-4, 1e-3
 
 
-def within(actual, expected, atol=LOGIT_ATOL, rtol=LOGIT_RTOL):
+def within(actual, expected, atol=LOGIT_ATOL, rtol=LOGIT_RTOL, min_identical=0.999):
+    """BASELINE's tolerance, and near bit-identity: the device sums in double and rounds where the
+    reference rounds, so all but a rare last-bit difference must match exactly."""
     err = np.abs(actual.astype(np.float64) - expected)
     ratio = err / (atol + rtol * np.abs(expected))
     i = int(np.argmax(ratio))
     assert ratio[i] <= 1.0, f"worst logit {i}: {actual[i]} vs {expected[i]} ({ratio[i]:.2f} of tol)"
+    same = float(np.mean(actual == expected))
+    assert same >= min_identical, f"only {same:.5f} of logits bit-identical"
 
 
 def gpu_model(path, cfg, ctx, batch=1):
@@ -109,9 +113,8 @@ def test_tiny_kv_cache_matches_oracle(gpu, oracle, tiny_file):
             got = np.empty(n, np.uint16)
             _copy_device(ptr, got)
             diff = got != ref[:n]
-            # f16 rounding of a value within an f32 ulp of a half-way point may land one half-ulp
-            # away; anything beyond one f16 ulp is a bug
-            assert diff.mean() < 1e-2, (layer, int(diff.sum()))
+            # only a rare last-bit tie may differ; anything beyond one f16 ulp is a bug
+            assert diff.mean() < 1e-3, (layer, int(diff.sum()))
             if diff.any():
                 a = got[diff].view(np.float16).astype(np.float32)
                 b = ref[:n][diff].view(np.float16).astype(np.float32)
