@@ -316,6 +316,9 @@ struct enx_ctx {
     uint32_t trace_len = 0;
     bool graph_mega[kMaxStepBatch + 1] = {};
     bool loop_mega[kMaxStepBatch + 1] = {};
+    MegaSlice* d_table = nullptr;      // slice table of the persistent step kernel (per CTA)
+    uint32_t* d_nslices = nullptr;
+    uint32_t table_stride = 0, table_grid = 0;
     uint32_t last_launches = 0;
     // prefill buffers (chunk-sized)
     uint32_t pf_chunk = 0;
@@ -363,6 +366,9 @@ void free_graphs(enx_ctx* c) {
         if (g) cudaGraphExecDestroy(g);
         g = nullptr;
     }
+    dfree(c->d_table);
+    dfree(c->d_nslices);
+    c->table_stride = c->table_grid = 0;
 }
 
 void free_prefill(enx_ctx* c) {
@@ -829,7 +835,6 @@ static bool mega_eligible(enx_ctx* c, uint32_t B, const StepArgs& S, MegaArgs& A
     A.vocab = C.vocab;
     A.layers = C.layers;
     A.eps = C.rms_norm_eps;
-    A.attn_scale = 1.0f / std::sqrt((float)C.head_dim);
     for (uint32_t l = 0; l < C.layers; ++l) A.layer[l] = c->layers[l];
     A.head = c->head.embed;
     A.head_bits = c->head.bits;
@@ -838,13 +843,34 @@ static bool mega_eligible(enx_ctx* c, uint32_t B, const StepArgs& S, MegaArgs& A
     A.tokens = c->d_step->tokens;
     A.bar = c->d_bar;
     A.err = &c->d_step->err;
-    A.head_chunk = 32;
     A.trace = c->d_trace;
     geo = mega_geometry(B, A);
     if (geo.nslots < 2 || c->max_ctx > geo.max_positions) return false;
     A.nslots = geo.nslots;
     A.slot_bytes = geo.slot_bytes;
     A.x4_floats = geo.x4_floats;
+    if (!c->d_table || c->table_grid != geo.grid) {
+        // the table depends on the weights and the grid only, so every batch size shares it
+        dfree(c->d_table);
+        dfree(c->d_nslices);
+        std::vector<MegaSlice> table;
+        std::vector<uint32_t> counts;
+        uint32_t stride = 0;
+        mega_build_table(A, geo, table, counts, stride);
+        if (dalloc(&c->d_table, table.size(), "mega table") != ENX_OK ||
+            dalloc(&c->d_nslices, counts.size(), "mega counts") != ENX_OK ||
+            cudaMemcpy(c->d_table, table.data(), table.size() * sizeof(MegaSlice), cudaMemcpyHostToDevice) != cudaSuccess ||
+            cudaMemcpy(c->d_nslices, counts.data(), counts.size() * 4, cudaMemcpyHostToDevice) != cudaSuccess) {
+            dfree(c->d_table);
+            dfree(c->d_nslices);
+            return false;
+        }
+        c->table_stride = stride;
+        c->table_grid = geo.grid;
+    }
+    A.table = c->d_table;
+    A.nslices = c->d_nslices;
+    A.table_stride = c->table_stride;
     return true;
 }
 
@@ -853,6 +879,10 @@ static enx_status capture_step(enx_ctx* c, uint32_t B, bool loop) {
     StepArgs S = step_args(c);
     S.pos = c->d_step->pos;
     const size_t in_bytes = offsetof(StepBlock, out);
+    // decided (and the slice table uploaded) before capture: no synchronous copies inside it
+    MegaArgs A;
+    MegaGeometry geo{};
+    const bool mega = mega_eligible(c, B, S, A, geo);
     ENX_CUDA(cudaStreamBeginCapture(st, cudaStreamCaptureModeThreadLocal));
     cudaError_t e = cudaSuccess;
     if (loop) {
@@ -865,11 +895,7 @@ static enx_status capture_step(enx_ctx* c, uint32_t B, bool loop) {
             e = cudaGetLastError();
         }
     }
-    bool mega = false;
     if (e == cudaSuccess) {
-        MegaArgs A;
-        MegaGeometry geo{};
-        mega = mega_eligible(c, B, S, A, geo);
         if (mega) {
             e = cudaMemsetAsync(c->d_bar, 0, sizeof(unsigned long long), st);
             if (e == cudaSuccess) e = launch_mega(B, A, geo, st);
@@ -1085,7 +1111,7 @@ extern "C" enx_status enx_set_tracing(enx_ctx* c, int on) {
     dfree(c->d_trace);
     c->trace_len = 0;
     if (on) {
-        c->trace_len = 3 * (4 * c->cfg.layers + 1);
+        c->trace_len = 3 * (kMegaStages * c->cfg.layers + 1);
         ENX_TRY(dalloc(&c->d_trace, c->trace_len, "trace"));
         ENX_CUDA(cudaMemset(c->d_trace, 0, (size_t)c->trace_len * 8));
     }

@@ -45,6 +45,14 @@ __device__ __forceinline__ uint32_t zero_code(const uint32_t* zeros, uint32_t bl
     return (__ldg(zeros + (blk >> 2)) >> ((blk & 3u) * 8u)) & 0xFFu;
 }
 
+// Block barrier of the helpers below: NT == 0 is __syncthreads(); otherwise named barrier 1 over
+// the first NT threads (the persistent kernel's consumer warps, excluding its producer warp).
+template <int NT>
+__device__ __forceinline__ void csync() {
+    if (NT == 0) __syncthreads();
+    else asm volatile("bar.sync 1, %0;" ::"n"(NT) : "memory");
+}
+
 // 2^52 + v as a double (0 <= v < 2^32): (2^52 + q) - (2^52 + z) is exactly q - z.
 __device__ __forceinline__ double magic_d(uint32_t v) { return __hiloint2double(0x43300000, (int)v); }
 
@@ -58,25 +66,26 @@ __device__ __forceinline__ uint32_t xd_index(uint32_t t, uint32_t k, uint32_t nc
 // Per-token RMS scale 1/sqrt(mean(x^2) + eps) in double (test/reference/ops.ts:38-45), of MT
 // rows of length K, into rs[MT] (shared).  `red` needs MT * warps doubles.  Whole block; ends
 // with __syncthreads().
-template <int MT, bool CG>
+template <int MT, bool CG, int NT = 0>
 __device__ __forceinline__ void rms_scale_d(double* rs, double* red, const float* x, uint32_t K, float eps) {
-    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, nw = blockDim.x >> 5;
+    const uint32_t nthreads = NT ? NT : blockDim.x;
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, nw = nthreads >> 5;
     for (int t = 0; t < MT; ++t) {
         double s = 0.0;
-        for (uint32_t k = threadIdx.x; k < K; k += blockDim.x) {
+        for (uint32_t k = threadIdx.x; k < K; k += nthreads) {
             const double v = CG ? __ldcg(x + (size_t)t * K + k) : x[(size_t)t * K + k];
             s = fma(v, v, s);
         }
         s = warp_sum_d(s);
         if (lane == 0) red[t * nw + warp] = s;
     }
-    __syncthreads();
+    csync<NT>();
     if ((int)threadIdx.x < MT) {
         double tot = 0.0;
         for (int w = 0; w < nw; ++w) tot += red[threadIdx.x * nw + w];
         rs[threadIdx.x] = 1.0 / sqrt(tot / (double)K + (double)eps);
     }
-    __syncthreads();
+    csync<NT>();
 }
 
 // The stored (float) RMSNorm output x * scale * w, exactly as the reference rounds it.
@@ -86,17 +95,18 @@ __device__ __forceinline__ float norm_value(float x, double scale, float w) {
 
 // Stage MT activation rows into the chunk-transposed double layout: rs == nullptr stages x as
 // is, otherwise the RMSNorm output (float-rounded, then widened).  Ends with __syncthreads().
-template <int BITS, int MT, bool CG>
+template <int BITS, int MT, bool CG, int NT = 0>
 __device__ __forceinline__ void stage_x_d(double* XD, const float* x, uint32_t K, const double* rs,
                                           const float* gain) {
     const uint32_t nchunk = K / Geom<BITS>::E;
-    for (uint32_t i = threadIdx.x; i < MT * K; i += blockDim.x) {
+    const uint32_t nthreads = NT ? NT : blockDim.x;
+    for (uint32_t i = threadIdx.x; i < MT * K; i += nthreads) {
         const uint32_t t = i / K, k = i % K;
         float v = CG ? __ldcg(x + i) : x[i];
         if (rs) v = norm_value(v, rs[t], gain[k]);
         XD[xd_index<BITS>(t, k, nchunk)] = (double)v;
     }
-    __syncthreads();
+    csync<NT>();
 }
 
 // Shared inner step: one chunk of R rows (codes q[r], scale s[r], zero zc[r]) against MT tokens.

@@ -182,23 +182,23 @@ class Model:
         """Per-stage device times (us) of the last traced step, summed over layers: how long each
         stage waited for its barrier+weights and how long it computed (kernel-group telemetry of
         src/runtime/telemetry.ts, at stage granularity)."""
-        n = 3 * (4 * self.config.layers + 1)
+        n = 3 * (5 * self.config.layers + 1)
         buf = np.zeros(n, dtype=np.uint64)
         cnt = C.c_uint32()
         call("enx_trace", self._h, buf.ctypes.data, n, C.byref(cnt))
         t = buf.astype(np.float64).reshape(-1, 3) / 1e3
-        names = ["qkv", "attn_o", "gate_up", "down"]
+        names = ["qkv", "attn", "o", "gate_up", "down"]
         out = {f"{k}_{p}": 0.0 for k in names for p in ("wait", "weights", "compute")}
         L = self.config.layers
-        for i in range(4 * L):
-            k = names[i % 4]
+        for i in range(5 * L):
+            k = names[i % 5]
             prev_done = t[i - 1, 2] if i > 0 else t[i, 0]
             out[f"{k}_wait"] += t[i, 0] - prev_done          # barrier after the previous stage
             out[f"{k}_weights"] += max(t[i, 1] - t[i, 0], 0.0)  # includes the activation loads/norm
             out[f"{k}_compute"] += t[i, 2] - t[i, 1]
-        out["head_wait"] = t[4 * L, 0] - t[4 * L - 1, 2]
-        out["head"] = t[4 * L, 2] - t[4 * L, 0]
-        out["total"] = t[4 * L, 2] - t[0, 0]
+        out["head_wait"] = t[5 * L, 0] - t[5 * L - 1, 2]
+        out["head"] = t[5 * L, 2] - t[5 * L, 0]
+        out["total"] = t[5 * L, 2] - t[0, 0]
         return out
 
     def stream_handle(self) -> int:
