@@ -316,9 +316,13 @@ struct enx_ctx {
     uint32_t trace_len = 0;
     bool graph_mega[kMaxStepBatch + 1] = {};
     bool loop_mega[kMaxStepBatch + 1] = {};
-    MegaSlice* d_table = nullptr;      // slice table of the persistent step kernel (per CTA)
-    uint32_t* d_nslices = nullptr;
-    uint32_t table_stride = 0, table_grid = 0;
+    // persistent step kernel: slice tables per batch size, head-major o-projection, per-head partials
+    MegaSlice* d_table[kMaxStepBatch + 1] = {};
+    uint32_t* d_nslices[kMaxStepBatch + 1] = {};
+    uint32_t table_stride[kMaxStepBatch + 1] = {};
+    uint8_t* d_wo_heads = nullptr;
+    std::vector<QW> wo_heads;
+    double* d_opart = nullptr;
     uint32_t last_launches = 0;
     // prefill buffers (chunk-sized)
     uint32_t pf_chunk = 0;
@@ -366,9 +370,14 @@ void free_graphs(enx_ctx* c) {
         if (g) cudaGraphExecDestroy(g);
         g = nullptr;
     }
-    dfree(c->d_table);
-    dfree(c->d_nslices);
-    c->table_stride = c->table_grid = 0;
+    for (uint32_t b = 0; b <= kMaxStepBatch; ++b) {
+        dfree(c->d_table[b]);
+        dfree(c->d_nslices[b]);
+        c->table_stride[b] = 0;
+    }
+    dfree(c->d_wo_heads);
+    dfree(c->d_opart);
+    c->wo_heads.clear();
 }
 
 void free_prefill(enx_ctx* c) {
@@ -658,7 +667,7 @@ extern "C" enx_status enx_kv_alloc(enx_ctx* c, uint32_t max_context, uint32_t ba
     std::memset(c->h_step, 0, sizeof(StepBlock));
     // device-fed loop: room for every step the caches can hold
     c->loop_cap = max_context * B;
-    ENX_TRY(dalloc(&c->d_bar, 1, "barrier counter"));
+    ENX_TRY(dalloc(&c->d_bar, kMegaBarWords, "barrier counters"));
     ENX_CUDA(cudaMemsetAsync(c->d_step, 0, sizeof(StepBlock), c->stream));
     ENX_TRY(dalloc(&c->d_loop, 1, "loop state"));
     ENX_TRY(dalloc(&c->d_loop_rand, c->loop_cap, "loop randoms"));
@@ -842,6 +851,7 @@ static bool mega_eligible(enx_ctx* c, uint32_t B, const StepArgs& S, MegaArgs& A
     A.S = S;
     A.tokens = c->d_step->tokens;
     A.bar = c->d_bar;
+    A.ready = reinterpret_cast<uint32_t*>(c->d_bar + 8);
     A.err = &c->d_step->err;
     A.trace = c->d_trace;
     geo = mega_geometry(B, A);
@@ -849,28 +859,47 @@ static bool mega_eligible(enx_ctx* c, uint32_t B, const StepArgs& S, MegaArgs& A
     A.nslots = geo.nslots;
     A.slot_bytes = geo.slot_bytes;
     A.x4_floats = geo.x4_floats;
-    if (!c->d_table || c->table_grid != geo.grid) {
-        // the table depends on the weights and the grid only, so every batch size shares it
-        dfree(c->d_table);
-        dfree(c->d_nslices);
+    A.att_reps = geo.att_reps;
+    if (!c->d_wo_heads) {
+        // head-major copy of every o-projection and the per-head partial sums (built once)
+        const size_t per = mega_wo_heads_bytes(C.hidden, C.heads, C.head_dim);
+        if (dalloc(&c->d_wo_heads, per * C.layers, "o-projection by head") != ENX_OK ||
+            dalloc(&c->d_opart, (size_t)kMaxStepBatch * C.heads * C.hidden, "o partials") != ENX_OK) {
+            dfree(c->d_wo_heads);
+            dfree(c->d_opart);
+            return false;
+        }
+        c->wo_heads.assign(C.layers, QW{});
+        for (uint32_t l = 0; l < C.layers; ++l)
+            if (mega_wo_heads(c->layers[l].wo, C.heads, C.head_dim, c->d_wo_heads + per * l, &c->wo_heads[l], c->stream) !=
+                cudaSuccess) {
+                dfree(c->d_wo_heads);
+                return false;
+            }
+        if (cudaStreamSynchronize(c->stream) != cudaSuccess) {
+            dfree(c->d_wo_heads);
+            return false;
+        }
+    }
+    if (!c->d_table[B]) {
         std::vector<MegaSlice> table;
         std::vector<uint32_t> counts;
         uint32_t stride = 0;
-        mega_build_table(A, geo, table, counts, stride);
-        if (dalloc(&c->d_table, table.size(), "mega table") != ENX_OK ||
-            dalloc(&c->d_nslices, counts.size(), "mega counts") != ENX_OK ||
-            cudaMemcpy(c->d_table, table.data(), table.size() * sizeof(MegaSlice), cudaMemcpyHostToDevice) != cudaSuccess ||
-            cudaMemcpy(c->d_nslices, counts.data(), counts.size() * 4, cudaMemcpyHostToDevice) != cudaSuccess) {
-            dfree(c->d_table);
-            dfree(c->d_nslices);
+        mega_build_table(B, A, c->wo_heads.data(), geo, table, counts, stride);
+        if (dalloc(&c->d_table[B], table.size(), "mega table") != ENX_OK ||
+            dalloc(&c->d_nslices[B], counts.size(), "mega counts") != ENX_OK ||
+            cudaMemcpy(c->d_table[B], table.data(), table.size() * sizeof(MegaSlice), cudaMemcpyHostToDevice) != cudaSuccess ||
+            cudaMemcpy(c->d_nslices[B], counts.data(), counts.size() * 4, cudaMemcpyHostToDevice) != cudaSuccess) {
+            dfree(c->d_table[B]);
+            dfree(c->d_nslices[B]);
             return false;
         }
-        c->table_stride = stride;
-        c->table_grid = geo.grid;
+        c->table_stride[B] = stride;
     }
-    A.table = c->d_table;
-    A.nslices = c->d_nslices;
-    A.table_stride = c->table_stride;
+    A.opart = c->d_opart;
+    A.table = c->d_table[B];
+    A.nslices = c->d_nslices[B];
+    A.table_stride = c->table_stride[B];
     return true;
 }
 
@@ -897,7 +926,7 @@ static enx_status capture_step(enx_ctx* c, uint32_t B, bool loop) {
     }
     if (e == cudaSuccess) {
         if (mega) {
-            e = cudaMemsetAsync(c->d_bar, 0, sizeof(unsigned long long), st);
+            e = cudaMemsetAsync(c->d_bar, 0, kMegaBarWords * sizeof(unsigned long long), st);
             if (e == cudaSuccess) e = launch_mega(B, A, geo, st);
         } else {
             e = launch_embed(c->d_step->tokens, c->head.embed, c->head.bits, c->x, B, 0, c->cfg.vocab, c->cfg.hidden,
@@ -1111,7 +1140,7 @@ extern "C" enx_status enx_set_tracing(enx_ctx* c, int on) {
     dfree(c->d_trace);
     c->trace_len = 0;
     if (on) {
-        c->trace_len = 3 * (kMegaStages * c->cfg.layers + 1);
+        c->trace_len = 3 * (kMegaStages * c->cfg.layers + 1) + kMegaTraceDetail * c->cfg.layers;
         ENX_TRY(dalloc(&c->d_trace, c->trace_len, "trace"));
         ENX_CUDA(cudaMemset(c->d_trace, 0, (size_t)c->trace_len * 8));
     }

@@ -18,7 +18,7 @@
 // loads.  Activations sit in shared memory as doubles transposed by chunk
 // (XD[(t*F2 + j)*nchunk + c] = x[t][c*E + 2j .. 2j+1]) so the lanes' 16-byte reads are
 // conflict-free.  A code becomes an exact double with the 2^52 exponent trick, (q - z) is exact,
-// and each chunk contributes s * sum_j (q_j - z) * x_j.
+// and each chunk contributes s * sum_j (q_j - z) * x_j (four interleaved partial sums).
 #pragma once
 
 #include "enx_internal.cuh"
@@ -115,14 +115,17 @@ __device__ __forceinline__ void chunk_dot(const uint4 (&q)[R], const float (&s)[
                                           const double2* __restrict__ XD, uint32_t nchunk, uint32_t c,
                                           double (&acc)[R][MT]) {
     constexpr int F2 = Geom<BITS>::F2;
+    constexpr int NP = 4;  // independent partial sums per row: short dependency chains
     double zd[R];
 #pragma unroll
     for (int r = 0; r < R; ++r) zd[r] = magic_d(zc[r]);
 #pragma unroll
     for (int t = 0; t < MT; ++t) {
-        double part[R];
+        double part[R][NP];
 #pragma unroll
-        for (int r = 0; r < R; ++r) part[r] = 0.0;
+        for (int r = 0; r < R; ++r)
+#pragma unroll
+            for (int p = 0; p < NP; ++p) part[r][p] = 0.0;
 #pragma unroll
         for (int j = 0; j < F2; ++j) {
             const double2 xv = XD[(t * F2 + j) * nchunk + c];
@@ -136,12 +139,13 @@ __device__ __forceinline__ void chunk_dot(const uint4 (&q)[R], const float (&s)[
 #pragma unroll
                 for (int r = 0; r < R; ++r) {
                     const uint32_t wd = word == 0 ? q[r].x : word == 1 ? q[r].y : word == 2 ? q[r].z : q[r].w;
-                    part[r] = fma(magic_d((wd >> sh) & mask) - zd[r], xe, part[r]);
+                    part[r][el % NP] = fma(magic_d((wd >> sh) & mask) - zd[r], xe, part[r][el % NP]);
                 }
             }
         }
 #pragma unroll
-        for (int r = 0; r < R; ++r) acc[r][t] = fma(part[r], (double)s[r], acc[r][t]);
+        for (int r = 0; r < R; ++r)
+            acc[r][t] = fma((part[r][0] + part[r][1]) + (part[r][2] + part[r][3]), (double)s[r], acc[r][t]);
     }
 }
 

@@ -1,21 +1,28 @@
 // Persistent decode step: the whole decoder + tied head for MT tokens in ONE cooperative launch.
 //
-// A batch-1 decode step of this model moves 351 MB (54 us at the measured HBM rate) but has
-// ~100 dependent stages.  As separate kernels each stage pays a launch, a cold activation read
-// and a cold weight read in sequence (7-15 us per kernel, measured with ncu).  Here one CTA per
-// SM runs every stage.  A producer warp streams the CTA's weight slices for the coming stages
-// into a shared-memory ring with TMA bulk copies (cp.async.bulk, full/empty mbarriers), running
-// ahead of the grid barriers; 16 consumer warps compute.  What each CTA copies and computes in
-// every slice is a table built on the host (mega_build_table), so no thread plans on the device.
+// A batch-1 decode step of this model moves 351 MB (54 us at the measured HBM rate) but is a
+// chain of dependent stages.  As separate kernels each stage pays a launch, a cold activation
+// read and a cold weight read in sequence.  Here one CTA per SM runs every stage.  A producer
+// warp streams the CTA's weight slices for the coming stages into a shared-memory ring with bulk
+// copies (cp.async.bulk, full/empty mbarriers), running ahead of the grid barriers; 16 consumer
+// warps compute.  What each CTA copies and computes in every slice is a table built on the host
+// (mega_build_table), so no thread plans on the device.
 //
-// Stages per layer (a grid barrier after each):
-//   S1  RMSNorm(x) -> q|k|v rows (RoPE pairs) + bias + RoPE; q to global, k/v into the f16 cache
-//   S2  attention, one CTA per (token, query head) -> attn_out (no weights)
-//   S3  o-projection rows + residual into x
-//   S4  RMSNorm(x) -> gate|up rows -> SiLU(gate)*up into `gated`
-//   S5  down-projection rows + residual into x
-// then the final RMSNorm and this CTA's slice of the tied head rows, streamed in chunks.
-// Arithmetic is the faithful double-sum, float-store scheme of k_matvec.cuh.
+// A grid barrier costs ~1.9 us on this part (measured), so each layer has three of them:
+//   A  every CTA: RMSNorm(x) -> its units of q|k|v rows (4 RoPE pairs each) + bias + RoPE; q to
+//      global, k/v into the f16 cache; then it bumps the ready counter of the unit's kv head.
+//      Attention CTAs, att_reps per (token, query head), wait (bounded) for their kv head's
+//      counter instead of a grid barrier, run attention over the cached positions (history
+//      prefetched with cp.async at the start of the stage) and the o-projection restricted to
+//      this head's columns for their share of the rows, in double, into opart[t][h][:].
+//   C  every CTA: x += float(sum over heads of opart) (fixed head order, all rows, kept in
+//      shared memory) -> RMSNorm -> its gate|up rows -> SiLU(gate)*up into `gated`
+//   D  every CTA: its down-projection rows + residual (from shared memory) into x
+// then the final RMSNorm and this CTA's slice of the tied head rows, streamed in chunks.  Norm
+// gains and q|k|v biases travel in the slices with the weights.
+// Arithmetic is the faithful double-sum, float-store scheme of k_matvec.cuh.  Splitting the
+// o-projection sum by head and adding the per-head doubles in a fixed order only reorders f64
+// additions before the single rounding to float.
 //
 // Grid barriers are a monotonic 64-bit arrival counter (zeroed by a memset node before each
 // launch).  Every wait is bounded and reports through `err` instead of hanging; the producer
@@ -31,9 +38,9 @@ constexpr int kMWarps = 16;                  // consumer warps
 constexpr int kMConsumers = kMWarps * 32;    // consumer threads (named barrier 1)
 constexpr int kMThreads = kMConsumers + 32;  // + one producer warp
 constexpr uint32_t kSpinLimit = 1u << 24;    // bounded waits (well under a minute), then an error
-constexpr uint32_t kMaxGroup = 8;            // query heads per kv head
-constexpr uint32_t kKvStage = 64;            // cached positions staged in shared memory at a time
-constexpr int kMaxRes = 96;                  // rows of results exchanged in shared memory per stage
+constexpr uint32_t kKvHalfs = 16384;         // f16 staging of cached K and V rows (32 KB)
+constexpr int kMaxRes = 96;                  // rows per token exchanged in shared memory (C, D)
+constexpr int kHeadDimMax = 64;
 
 // ---------------------------------------------------------------------------------------------
 // PTX helpers
@@ -68,16 +75,28 @@ __device__ __forceinline__ void bulk_copy(uint32_t dst_smem, unsigned long long 
                  "l"(src), "r"(bytes), "r"(smem_u32(bar))
                  : "memory");
 }
+// 16-byte asynchronous copy global -> shared (L2 only), completed by cp_async_wait_all.
+__device__ __forceinline__ void cp_async16(void* dst, const void* src) {
+    asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(smem_u32(dst)), "l"(src) : "memory");
+}
+__device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
+__device__ __forceinline__ void cp_async_wait_all() { asm volatile("cp.async.wait_all;" ::: "memory"); }
 __device__ __forceinline__ void cbar() { asm volatile("bar.sync 1, %0;" ::"n"(kMConsumers) : "memory"); }
 
 // Stage trace: consumer thread 0 of CTA 0 stamps %globaltimer at the start of a stage (after its
-// barrier), when its weights have landed, and when its compute is done: trace[3*stage + k].
+// barrier), when its first weights have landed, and when its compute is done: trace[3*stage + k].
 __device__ __forceinline__ void stamp(const MegaArgs& A, uint32_t idx) {
     if (A.trace && blockIdx.x == 0 && threadIdx.x == 0) {
         unsigned long long t;
         asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
         A.trace[idx] = t;
     }
+}
+
+// Detail stamps of stage A (CTA 0): trace[3*(kMegaStages*layers + 1) + kADetail*l + k].
+constexpr uint32_t kADetail = kMegaTraceDetail;
+__device__ __forceinline__ void stamp_a(const MegaArgs& A, uint32_t l, uint32_t k) {
+    stamp(A, 3 * (kMegaStages * A.layers + 1) + kADetail * l + k);
 }
 
 // ---------------------------------------------------------------------------------------------
@@ -109,8 +128,9 @@ __device__ bool grid_sync(const MegaArgs& A, uint32_t& index, volatile int* s_fa
 }
 
 // ---------------------------------------------------------------------------------------------
-// dot product of one staged row over chunks [c0, c1): lane l takes chunks c0+l, c0+l+32, ...
+// dot products against staged rows
 
+// One staged row over chunks [c0, c1): lane l takes chunks c0+l, c0+l+32, ...
 template <int BITS, int MT>
 __device__ __forceinline__ void row_dot(const uint8_t* slot, const MegaRange& R, uint32_t row, uint32_t cols,
                                         const double2* __restrict__ XD, uint32_t nchunk, uint32_t c0, uint32_t c1,
@@ -176,50 +196,44 @@ __device__ __forceinline__ void row_dot2(const uint8_t* slot, const MegaRange& R
 }
 
 // One pass: read MT rows of x (L2 or shared), RMSNorm them in double, stage the float-rounded
-// outputs as doubles.  K * MT must be at most 8 * kMConsumers.
+// outputs as doubles.  K <= 2 * kMConsumers.
 template <int BITS, int MT>
 __device__ void load_norm(double* Xd, const float* x, bool from_smem, uint32_t K, const float* gain, float eps,
-                          double* rs, double* red) {
-    constexpr int PER = 8;
+                          double* rs, double* red, const MegaArgs* tr = nullptr, uint32_t tl = 0) {
+    constexpr int PER = 2;
     const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
-    float v[PER];
-    double ss[MT];
-#pragma unroll
-    for (int t = 0; t < MT; ++t) ss[t] = 0.0;
+    float v[MT][PER], gv[PER];
 #pragma unroll
     for (int k = 0; k < PER; ++k) {
         const uint32_t i = tid + k * kMConsumers;
-        v[k] = 0.f;
-        if (i < MT * K) v[k] = from_smem ? x[i] : __ldcg(x + i);
-    }
+        gv[k] = i < K ? gain[i] : 0.f;  // shared (staged with the weights) or global
 #pragma unroll
-    for (int k = 0; k < PER; ++k) {
-        const uint32_t i = tid + k * kMConsumers;
-        const uint32_t t = i / K;
-#pragma unroll
-        for (int u = 0; u < MT; ++u)
-            if (i < MT * K && t == (uint32_t)u) ss[u] = fma((double)v[k], (double)v[k], ss[u]);
+        for (int t = 0; t < MT; ++t) v[t][k] = i < K ? (from_smem ? x[t * K + i] : __ldcg(x + t * K + i)) : 0.f;
     }
 #pragma unroll
     for (int t = 0; t < MT; ++t) {
-        const double s = warp_sum_d(ss[t]);
-        if (lane == 0) red[t * kMWarps + warp] = s;
+        double ss = 0.0;
+#pragma unroll
+        for (int k = 0; k < PER; ++k) ss = fma((double)v[t][k], (double)v[t][k], ss);
+        ss = warp_sum_d(ss);
+        if (lane == 0) red[t * kMWarps + warp] = ss;
     }
     cbar();
+    if (tr) stamp_a(*tr, tl, 6);
     if (tid < MT) {
         double tot = 0.0;
         for (int w = 0; w < kMWarps; ++w) tot += red[tid * kMWarps + w];
         rs[tid] = 1.0 / sqrt(tot / (double)K + (double)eps);
     }
     cbar();
+    if (tr) stamp_a(*tr, tl, 7);
     const uint32_t nchunk = K / Geom<BITS>::E;
 #pragma unroll
     for (int k = 0; k < PER; ++k) {
         const uint32_t i = tid + k * kMConsumers;
-        if (i < MT * K) {
-            const uint32_t t = i / K, kk = i % K;
-            Xd[xd_index<BITS>(t, kk, nchunk)] = (double)norm_value(v[k], rs[t], __ldg(gain + kk));
-        }
+        if (i < K)
+#pragma unroll
+            for (int t = 0; t < MT; ++t) Xd[xd_index<BITS>(t, i, nchunk)] = (double)norm_value(v[t][k], rs[t], gv[k]);
     }
     cbar();
 }
@@ -246,38 +260,51 @@ __device__ __forceinline__ double half_bits_to_double(uint32_t b) {
     return __hiloint2double((int)(sgn | (ed << 20) | (m << 10)), 0);
 }
 
-// Attention of token t, query head h (test/reference/ops.ts:123-204), by one CTA:
+// Shared state of an attention CTA (one token, one head).
+struct HeadSmem {
+    double qd[kHeadDimMax];  // rotated query (float values)
+    double ad[kHeadDimMax];  // attention output (float values)
+    float red[kMWarps];
+    double redd[kMWarps];
+};
+
+// Attention of one query head over positions [0, npos) (test/reference/ops.ts:123-204):
 //   score_j = float(sum_d q[d] * K[j][d] / sqrt(hd))          (sum in double)
 //   w_j     = float(float(exp(score_j - max)) / sum_j exp(.))  (exp and sum in double)
 //   out[d]  = float(sum_j w_j * V[j][d])                       (sum in double)
-// Cached rows of the kv head are staged in shared memory a chunk at a time.  pw holds the scores,
-// then the weights, as doubles (npos <= the activation area's MT * x4 doubles).  `red` needs 32
-// doubles.
-__device__ void attend(const MegaArgs& A, uint32_t l, uint32_t t, uint32_t h, double* pw, double* qd,
-                       uint16_t* kvs, double* red) {
+// Rows [0, min(npos, cap)) of K and V are already staged in kst / vst; longer contexts stream
+// further chunks from the cache.  pw (npos doubles) holds the scores, then the weights.  Leaves
+// the output in hs.ad.
+__device__ void attend(const MegaArgs& A, uint32_t l, uint32_t t, uint32_t g, uint32_t pos, double* pw,
+                       uint16_t* kst, uint16_t* vst, uint32_t cap, HeadSmem& hs) {
     const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
-    const uint32_t hd = A.head_dim, kvd = A.kv_heads * hd, g = h / (A.heads / A.kv_heads);
-    const uint32_t npos = A.S.pos_of(t) + 1, row8 = hd / 8;
-    const uint32_t cap = kKvStage * A.kv_heads;  // positions of one kv head per staged chunk
+    const uint32_t hd = A.head_dim, kvd = A.kv_heads * hd, row8 = hd / 8, npos = pos + 1;
     const size_t base = A.S.cache_offset(A.S.seq_of(t), l, 0) + g * hd;
     const uint16_t* Kc = A.S.kcache + base;
     const uint16_t* Vc = A.S.vcache + base;
-    for (uint32_t d = tid; d < hd; d += kMConsumers) qd[d] = (double)__ldcg(A.S.q + (size_t)t * A.hidden + h * hd + d);
     const double scale = 1.0 / sqrt((double)hd);
+    const uint32_t lr8 = hd == 64 ? 3 : 2;  // row8 = 1 << lr8 (head_dim 32 or 64)
+    auto stage_rows = [&](uint16_t* st, const uint16_t* src, uint32_t j0, uint32_t n) {
+        for (uint32_t i = tid; i < (n << lr8); i += kMConsumers)
+            reinterpret_cast<uint4*>(st)[i] =
+                __ldcg(reinterpret_cast<const uint4*>(src + (size_t)(j0 + (i >> lr8)) * kvd) + (i & (row8 - 1)));
+    };
     // scores: 8 threads per position, hd/8 dims each, combined over the 8 lanes
     const uint32_t sub = tid & 7;
     float mloc = -INFINITY;
     for (uint32_t j0 = 0; j0 < npos; j0 += cap) {
         const uint32_t n = min(cap, npos - j0);
-        for (uint32_t i = tid; i < n * row8; i += kMConsumers)
-            reinterpret_cast<uint4*>(kvs)[i] = __ldcg(reinterpret_cast<const uint4*>(Kc + (size_t)(j0 + i / row8) * kvd) + i % row8);
-        cbar();
+        if (j0 > 0) {
+            cbar();  // previous chunk consumed
+            stage_rows(kst, Kc, j0, n);
+            cbar();
+        }
         for (uint32_t jb = 0; jb < n; jb += kMConsumers / 8) {
             const uint32_t j = jb + (tid >> 3);
             double acc = 0.0;
             if (j < n) {
-                const uint16_t* kr = kvs + (size_t)j * hd + sub * row8;
-                for (uint32_t d = 0; d < row8; ++d) acc = fma(qd[sub * row8 + d], half_bits_to_double(kr[d]), acc);
+                const uint16_t* kr = kst + (size_t)j * hd + sub * row8;
+                for (uint32_t d = 0; d < row8; ++d) acc = fma(hs.qd[sub * row8 + d], half_bits_to_double(kr[d]), acc);
             }
             acc += __shfl_xor_sync(0xffffffffu, acc, 1);
             acc += __shfl_xor_sync(0xffffffffu, acc, 2);
@@ -288,16 +315,13 @@ __device__ void attend(const MegaArgs& A, uint32_t l, uint32_t t, uint32_t h, do
                 mloc = fmaxf(mloc, sc);
             }
         }
-        cbar();  // chunk consumed
     }
-    stamp(A, 3 * (kMegaStages * l + 1) + 1);
     // softmax over npos
     mloc = warp_max(mloc);
-    float* redf = reinterpret_cast<float*>(red + kMWarps);
-    if (lane == 0) redf[warp] = mloc;
+    if (lane == 0) hs.red[warp] = mloc;
     cbar();
     float m = -INFINITY;
-    for (int w = 0; w < kMWarps; ++w) m = fmaxf(m, redf[w]);
+    for (int w = 0; w < kMWarps; ++w) m = fmaxf(m, hs.red[w]);
     double sloc = 0.0;
     for (uint32_t j = tid; j < npos; j += kMConsumers) {
         const double e = exp(pw[j] - (double)m);
@@ -305,10 +329,10 @@ __device__ void attend(const MegaArgs& A, uint32_t l, uint32_t t, uint32_t h, do
         sloc += e;
     }
     sloc = warp_sum_d(sloc);
-    if (lane == 0) red[warp] = sloc;
+    if (lane == 0) hs.redd[warp] = sloc;
     cbar();
     double sum = 0.0;
-    for (int w = 0; w < kMWarps; ++w) sum += red[w];
+    for (int w = 0; w < kMWarps; ++w) sum += hs.redd[w];
     for (uint32_t j = tid; j < npos; j += kMConsumers) pw[j] = (double)(float)(pw[j] / sum);
     // weighted V: thread (d, slice) sums positions j = slice, slice + S, ... of each chunk
     const uint32_t S = kMConsumers / hd, slice = tid / hd, d = tid % hd;
@@ -316,27 +340,29 @@ __device__ void attend(const MegaArgs& A, uint32_t l, uint32_t t, uint32_t h, do
     for (uint32_t j0 = 0; j0 < npos; j0 += cap) {
         const uint32_t n = min(cap, npos - j0);
         cbar();  // weights final / previous chunk consumed
-        for (uint32_t i = tid; i < n * row8; i += kMConsumers)
-            reinterpret_cast<uint4*>(kvs)[i] = __ldcg(reinterpret_cast<const uint4*>(Vc + (size_t)(j0 + i / row8) * kvd) + i % row8);
-        cbar();
+        if (j0 > 0) {
+            stage_rows(vst, Vc, j0, n);
+            cbar();
+        }
         if (slice < S) {
             uint32_t j = slice;
             for (; j + S < n; j += 2 * S) {
-                a0 = fma(pw[j0 + j], half_bits_to_double(kvs[(size_t)j * hd + d]), a0);
-                a1 = fma(pw[j0 + j + S], half_bits_to_double(kvs[(size_t)(j + S) * hd + d]), a1);
+                a0 = fma(pw[j0 + j], half_bits_to_double(vst[(size_t)j * hd + d]), a0);
+                a1 = fma(pw[j0 + j + S], half_bits_to_double(vst[(size_t)(j + S) * hd + d]), a1);
             }
-            if (j < n) a0 = fma(pw[j0 + j], half_bits_to_double(kvs[(size_t)j * hd + d]), a0);
+            if (j < n) a0 = fma(pw[j0 + j], half_bits_to_double(vst[(size_t)j * hd + d]), a0);
         }
     }
     cbar();
-    double* part = reinterpret_cast<double*>(kvs);  // [S][hd]
+    double* part = reinterpret_cast<double*>(kst);  // [S][hd]
     if (slice < S) part[slice * hd + d] = a0 + a1;
     cbar();
     if ((uint32_t)tid < hd) {
         double v = 0.0;
         for (uint32_t s2 = 0; s2 < S; ++s2) v += part[s2 * hd + tid];  // fixed order
-        A.S.attn_out[(size_t)t * A.hidden + h * hd + tid] = (float)v;
+        hs.ad[tid] = (double)(float)v;
     }
+    cbar();
 }
 
 // ---------------------------------------------------------------------------------------------
@@ -346,23 +372,36 @@ template <int MT, int HB>
 __global__ void __launch_bounds__(kMThreads, 1) k_mega(const __grid_constant__ MegaArgs A) {
     extern __shared__ __align__(128) uint8_t smem[];
     __shared__ double rs[MT], red[MT * kMWarps];
-    __shared__ double res[kMaxRes][MT];  // per-row results of a stage, exchanged between warps
+    __shared__ double res[kMaxRes * MT];  // per-row results of a stage, exchanged between warps
+    __shared__ double rope_c[MT][kHeadDimMax / 2], rope_s[MT][kHeadDimMax / 2];  // this step's RoPE rows
+    __shared__ HeadSmem hs;
+    __shared__ uint32_t spos[MT];  // this step's positions
+    __shared__ __align__(16) MegaSlice sdesc[kMegaSlots];  // descriptors of the slices in the ring
     __shared__ volatile int s_fail;
     const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
     const uint32_t c = blockIdx.x;
     const uint32_t H = A.hidden, I = A.intermediate, hd = A.head_dim, half = hd / 2;
     const uint32_t NS = A.nslots, SB = A.slot_bytes;
+    const uint32_t group = A.heads / A.kv_heads;
 
     uint64_t* full = reinterpret_cast<uint64_t*>(smem);
     uint64_t* empty = full + kMegaSlots;
     uint8_t* slots = smem + 256;
     double* Xd = reinterpret_cast<double*>(slots + (size_t)NS * SB);  // [MT][x4] activations (doubles)
     const double2* XD = reinterpret_cast<const double2*>(Xd);
-    float* qs = reinterpret_cast<float*>(Xd + (size_t)MT * A.x4_floats);  // [MT][H] queries / temporary
-    uint16_t* kvs = reinterpret_cast<uint16_t*>(qs + (size_t)MT * H);     // [kKvStage][kv*hd] f16 stage
+    float* xs = reinterpret_cast<float*>(Xd + (size_t)MT * A.x4_floats);  // [MT][H] residual after attention
+    uint16_t* kst = reinterpret_cast<uint16_t*>(xs + (((size_t)MT * H + 3) & ~size_t(3)));
+    uint16_t* vst = kst + kKvHalfs / 2;
+    const uint32_t cap = kKvHalfs / 2 / hd;  // cached positions per staged chunk
 
     const MegaSlice* T = A.table + (size_t)c * A.table_stride;
     const uint32_t total = A.nslices[c];
+    // attention role: (token, head, replica) for the first MT * heads * att_reps CTAs
+    const uint32_t R = A.att_reps;
+    const bool att = c < MT * A.heads * R;
+    const uint32_t at = att ? c / (A.heads * R) : 0, ah = att ? (c / R) % A.heads : 0, arep = att ? c % R : 0;
+    const uint32_t ag = ah / group;
+    const uint32_t units_per_group = (group + 2) * (hd / 8);
 
     if (tid == 0) {
         s_fail = 0;
@@ -375,25 +414,52 @@ __global__ void __launch_bounds__(kMThreads, 1) k_mega(const __grid_constant__ M
     __syncthreads();
 
     // ---------------- producer warp: stream every slice through the ring ---------------------
+    // Lane k issues copy k of a slice; the next slice's descriptor is fetched before waiting for
+    // its slot, so the table reads overlap the wait.
     if (warp == kMWarps) {
-        if (lane != 0) return;
+        static_assert(sizeof(MegaSlice) % 16 == 0 && sizeof(MegaSlice) / 16 <= 32, "descriptor = one uint4 per lane");
+        constexpr uint32_t kDescVecs = sizeof(MegaSlice) / 16;
+        uint4 dv = make_uint4(0, 0, 0, 0);  // this lane's 16 bytes of the next descriptor
+        auto fetch = [&](uint32_t i) {
+            if (i < total && (uint32_t)lane < kDescVecs) dv = reinterpret_cast<const uint4*>(T + i)[lane];
+            // descriptors further ahead: into L2 now, so the fetch above hits it later
+            const uint32_t ahead = i + 2 + lane / 4;
+            if ((lane & 3) < 4 && ahead < total && lane < 16)
+                asm volatile("prefetch.global.L2 [%0];" ::"l"(reinterpret_cast<const uint8_t*>(T + ahead) + (lane & 3) * 128));
+        };
+        fetch(0);
         uint32_t issued = 0;
         for (uint32_t i = 0; i < total; ++i) {
             const uint32_t slot = i % NS;
-            if (i >= NS && !mbar_wait_bounded(empty + slot, ((i / NS) - 1) & 1u)) {
-                atomicMax(A.err, 2u);
-                break;
+            int ok = 1;
+            if (lane == 0) {
+                if (i >= NS && !mbar_wait_bounded(empty + slot, ((i / NS) - 1) & 1u)) {
+                    atomicMax(A.err, 2u);
+                    ok = 0;
+                }
+                if (*reinterpret_cast<volatile uint32_t*>(A.err)) ok = 0;
             }
-            if (*reinterpret_cast<volatile uint32_t*>(A.err)) break;
-            const MegaSlice& D = T[i];
+            if (!__shfl_sync(0xffffffffu, ok, 0)) break;
+            // publish the descriptor next to its data slot; the consumers read it from there
+            if ((uint32_t)lane < kDescVecs) reinterpret_cast<uint4*>(sdesc + slot)[lane] = dv;
+            __syncwarp();
+            const MegaSlice& D = sdesc[slot];
+            if (lane == 0) {
+                asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+                mbar_expect_tx(full + slot, D.bytes);
+            }
+            __syncwarp();
             const uint32_t base = smem_u32(slots + (size_t)slot * SB);
-            asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
-            mbar_expect_tx(full + slot, D.bytes);
-            for (uint32_t k = 0; k < D.ncopy; ++k) bulk_copy(base + D.copy[k].dst, D.copy[k].src, D.copy[k].bytes, full + slot);
+            if ((uint32_t)lane < D.ncopy) bulk_copy(base + D.copy[lane].dst, D.copy[lane].src, D.copy[lane].bytes, full + slot);
+            for (uint32_t k = lane; k < D.rows.n; k += 32)
+                bulk_copy(base + D.rows.dst + k * D.rows.dst_stride, D.rows.src + (unsigned long long)k * D.rows.src_stride,
+                          D.rows.bytes, full + slot);
             issued = i + 1;
+            fetch(i + 1);
         }
         // no copy may still be writing into shared memory when the CTA retires
-        for (uint32_t i = issued > NS ? issued - NS : 0; i < issued; ++i) mbar_wait_bounded(full + i % NS, (i / NS) & 1u);
+        if (lane == 0)
+            for (uint32_t i = issued > NS ? issued - NS : 0; i < issued; ++i) mbar_wait_bounded(full + i % NS, (i / NS) & 1u);
         return;
     }
 
@@ -418,114 +484,190 @@ __global__ void __launch_bounds__(kMThreads, 1) k_mega(const __grid_constant__ M
     };
     auto slot_ptr = [&]() { return slots + (size_t)(slice % NS) * SB; };
 
+    if (tid < MT) spos[tid] = A.S.pos_of(tid);
+    cbar();
+    const uint32_t apos = att ? spos[at] : 0;
+    // the RoPE rows of this step's positions (same for every layer)
+    for (uint32_t i = tid; i < MT * half; i += kMConsumers) {
+        const uint32_t t = i / half, p = i % half, pos = spos[t];
+        rope_c[t][p] = __ldg(A.S.rope_cos + (size_t)pos * half + p);
+        rope_s[t][p] = __ldg(A.S.rope_sin + (size_t)pos * half + p);
+    }
+
     for (uint32_t l = 0; l < A.layers; ++l) {
         const LayerArgs& La = A.layer[l];
 
-        // ---------------- S1: RMSNorm + q|k|v + RoPE + cache ---------------------------------
+        // ---------------- A: q|k|v units, then (attention CTAs) attention + o partial -------
         stamp(A, 3 * (kMegaStages * l + 0));
-        if (l == 0) {
-            // embedding rows of the tied table (for this CTA's norm); the rows this CTA owns in
-            // S3 and S5 also initialise the residual stream
-            const MegaSlice& Do = T[1];
-            const uint32_t o0 = Do.nrange ? Do.range[0].r0 : 0, o1 = Do.nrange ? Do.range[0].r1 : 0;
-            const uint32_t bpr = H / kBlock;
-            for (uint32_t i = tid; i < MT * H; i += kMConsumers) {
-                const uint32_t t = i / H, k = i % H, row = A.tokens[t];
-                const size_t flat = (size_t)row * H + k;
-                const uint32_t q = HB == 4 ? (A.head.packed[flat >> 3] >> ((flat & 7) * 4)) & 0xFu
-                                           : (A.head.packed[flat >> 2] >> ((flat & 3) * 8)) & 0xFFu;
-                const uint32_t blk = row * bpr + k / kBlock;
-                const float v = ((float)q - (float)zero_code<HB>(A.head.zeros, blk)) * A.head.scales[blk];
-                qs[i] = v;
-                if (k >= o0 && k < o1) A.S.x[i] = v;
+        if (att) {  // this head's cached K/V rows [0, min(pos, cap)), in flight during the units
+            const uint32_t kvd = A.kv_heads * hd, row8 = hd / 8;
+            const size_t base = A.S.cache_offset(A.S.seq_of(at), l, 0) + ag * hd;
+            const uint32_t pre = min(apos, cap), lr8 = hd == 64 ? 3 : 2;  // row8 = hd / 8 = 1 << lr8
+            for (uint32_t i = tid; i < (pre << lr8); i += kMConsumers) {
+                const uint32_t j = i >> lr8, d8 = i & (row8 - 1);
+                const size_t off = base + (size_t)j * kvd + d8 * 8;
+                cp_async16(kst + (size_t)j * hd + d8 * 8, A.S.kcache + off);
+                cp_async16(vst + (size_t)j * hd + d8 * 8, A.S.vcache + off);
             }
-            cbar();
-            load_norm<4, MT>(Xd, qs, true, H, La.norm_in, A.eps, rs, red);
-        } else {
-            load_norm<4, MT>(Xd, A.S.x, false, H, La.norm_in, A.eps, rs, red);
+            cp_async_commit();
         }
         if (!wait_slice()) return;
         stamp(A, 3 * (kMegaStages * l + 0) + 1);
         {
-            const MegaSlice& D = T[slice];
+            const MegaSlice& D = sdesc[slice % NS];
             const uint8_t* slot = slot_ptr();
-            const uint32_t nrows = D.nrange * 4;  // ranges of 4 rows: (i0..i0+3) then (+half)
+            const float* gain = reinterpret_cast<const float*>(slot + D.off_v);
+            const bool work = D.nrange != 0;  // CTAs without q|k|v units skip the norm
+            if (l == 0) {
+                // embedding rows of the tied table; this CTA also starts its share of the residual
+                const uint32_t o0 = (uint32_t)(((uint64_t)H * c) / gridDim.x), o1 = (uint32_t)(((uint64_t)H * (c + 1)) / gridDim.x);
+                const uint32_t bpr = H / kBlock;
+                for (uint32_t i = tid; i < MT * H; i += kMConsumers) {
+                    const uint32_t t = i / H, k = i % H, row = A.tokens[t];
+                    const size_t flat = (size_t)row * H + k;
+                    const uint32_t q = HB == 4 ? (A.head.packed[flat >> 3] >> ((flat & 7) * 4)) & 0xFu
+                                               : (A.head.packed[flat >> 2] >> ((flat & 3) * 8)) & 0xFFu;
+                    const uint32_t blk = row * bpr + k / kBlock;
+                    const float v = ((float)q - (float)zero_code<HB>(A.head.zeros, blk)) * A.head.scales[blk];
+                    xs[i] = v;
+                    if (k >= o0 && k < o1) A.S.x[i] = v;
+                }
+                cbar();
+                if (work) load_norm<4, MT>(Xd, xs, true, H, gain, A.eps, rs, red);
+            } else if (work) {
+                load_norm<4, MT>(Xd, A.S.x, false, H, gain, A.eps, rs, red, &A, l);
+            }
+            stamp_a(A, l, 0);
+            // q|k|v units: ranges of 4 rows, (i0..i0+3) then (+half), a warp per row
+            const uint32_t nrows = D.nrange * 4;
             for (uint32_t w = warp; w < nrows; w += kMWarps) {
-                const MegaRange& R = D.range[w / 4];
+                const MegaRange& Rr = D.range[w / 4];
                 double acc[MT];
-                row_dot<4, MT>(slot, R, R.r0 + w % 4, H, XD, H / 32, 0, H / 32, lane, acc);
+                row_dot<4, MT>(slot, Rr, Rr.r0 + w % 4, H, XD, H / 32, 0, H / 32, lane, acc);
                 if (lane == 0)
 #pragma unroll
-                    for (int t = 0; t < MT; ++t) res[w][t] = acc[t];
+                    for (int t = 0; t < MT; ++t) res[w * MT + t] = acc[t];
             }
             cbar();
-            // epilogue: a thread per (RoPE pair, token)
+            // epilogue: a thread per (RoPE pair, token): bias, RoPE (q, k), f16 rounding (k, v)
             for (uint32_t e = tid; e < (nrows / 2) * MT; e += kMConsumers) {
                 const uint32_t p = e / MT, t = e % MT;
                 const uint32_t u = p / 4, i4 = p % 4;
                 const MegaRange& Ra = D.range[2 * u];
+                const MegaRange& Rb = D.range[2 * u + 1];
                 const uint32_t kind = Ra.tag;
-                const uint32_t ra = Ra.r0 + i4, rb = D.range[2 * u + 1].r0 + i4;
-                const float* bias = kind == 0 ? La.bq : kind == 1 ? La.bk : La.bv;
-                float a = (float)(res[(2 * u) * 4 + i4][t] + (double)bias[ra]);
-                float b = (float)(res[(2 * u + 1) * 4 + i4][t] + (double)bias[rb]);
+                const uint32_t ra = Ra.r0 + i4, rb = Rb.r0 + i4;
+                const float ba = reinterpret_cast<const float*>(slot + Ra.off_b)[i4];
+                const float bb = reinterpret_cast<const float*>(slot + Rb.off_b)[i4];
+                float a = (float)(res[((2 * u) * 4 + i4) * MT + t] + (double)ba);
+                float b = (float)(res[((2 * u + 1) * 4 + i4) * MT + t] + (double)bb);
                 const uint32_t head = ra / hd, i = ra % hd;
-                const uint32_t pos = A.S.pos_of(t);
-                if (kind != 2) rope_pair(a, b, A.S.rope_cos[(size_t)pos * half + i], A.S.rope_sin[(size_t)pos * half + i]);
+                if (kind != 2) rope_pair(a, b, rope_c[t][i], rope_s[t][i]);
                 if (kind == 0) {
                     A.S.q[(size_t)t * H + ra] = a;
                     A.S.q[(size_t)t * H + rb] = b;
                 } else {
-                    uint16_t* cache = (kind == 1 ? A.S.kcache : A.S.vcache) + A.S.cache_offset(A.S.seq_of(t), l, pos);
+                    uint16_t* cache = (kind == 1 ? A.S.kcache : A.S.vcache) + A.S.cache_offset(A.S.seq_of(t), l, spos[t]);
                     cache[head * hd + i] = __half_as_ushort(__float2half_rn(a));
                     cache[head * hd + i + half] = __half_as_ushort(__float2half_rn(b));
                 }
             }
+            cbar();  // every output written before the arrivals below
+            if (tid == 0) {
+                for (uint32_t u = 0; u < D.nrange / 2; ++u) {
+                    const MegaRange& Ra = D.range[2 * u];
+                    const uint32_t kvh = Ra.tag == 0 ? (Ra.r0 / hd) / group : Ra.r0 / hd;
+                    for (uint32_t t = 0; t < MT; ++t)
+                        asm volatile("red.release.gpu.global.add.u32 [%0], 1;" ::"l"(A.ready + t * A.kv_heads + kvh) : "memory");
+                }
+            }
+            release_slice();
         }
-        release_slice();
-        stamp(A, 3 * (kMegaStages * l + 0) + 2);
-        if (!grid_sync(A, bar_index, &s_fail)) return;
-
-        // ---------------- S2: attention, one CTA per (token, query head) ---------------------
-        stamp(A, 3 * (kMegaStages * l + 1));
-        if (c < MT * A.heads) attend(A, l, c / A.heads, c % A.heads, Xd, reinterpret_cast<double*>(qs), kvs, &res[0][0]);
-        stamp(A, 3 * (kMegaStages * l + 1) + 2);
-        if (!grid_sync(A, bar_index, &s_fail)) return;
-
-        // ---------------- S3: o-projection + residual -----------------------------------------
-        stamp(A, 3 * (kMegaStages * l + 2));
-        for (uint32_t i = tid; i < MT * H; i += kMConsumers) Xd[xd_index<4>(i / H, i % H, H / 32)] = (double)__ldcg(A.S.attn_out + i);
-        cbar();
-        if (!wait_slice()) return;
-        stamp(A, 3 * (kMegaStages * l + 2) + 1);
-        {
-            const MegaSlice& D = T[slice];
-            if (D.nrange) {
-                const MegaRange& R = D.range[0];
-                const uint8_t* slot = slot_ptr();
-                for (uint32_t r = R.r0 + warp; r < R.r1; r += kMWarps) {
-                    double acc[MT];
-                    row_dot<4, MT>(slot, R, r, H, XD, H / 32, 0, H / 32, lane, acc);
-                    if (lane < MT) {
-                        float* xp = A.S.x + (size_t)lane * H + r;
-                        *xp = __ldcg(xp) + (float)pick<MT>(acc, lane);
+        stamp_a(A, l, 1);
+        if (att) {
+            // wait for every q|k|v unit of this kv head (bounded), then attention
+            if (tid == 0) {
+                const uint32_t target = units_per_group * (l + 1);
+                const uint32_t* flag = A.ready + at * A.kv_heads + ag;
+                for (uint32_t it = 0;; ++it) {
+                    uint32_t v;
+                    asm volatile("ld.acquire.gpu.global.u32 %0, [%1];" : "=r"(v) : "l"(flag) : "memory");
+                    if (v >= target) break;
+                    if (it > kSpinLimit) {
+                        atomicMax(A.err, 1u);
+                        s_fail = 1;
+                        break;
                     }
                 }
             }
+            cbar();
+            if (s_fail) return;
+            stamp_a(A, l, 2);
+            const uint32_t kvd = A.kv_heads * hd, row8 = hd / 8;
+            for (uint32_t d = tid; d < hd; d += kMConsumers) hs.qd[d] = (double)__ldcg(A.S.q + (size_t)at * H + ah * hd + d);
+            if (apos < cap) {  // the row written this step
+                const size_t crow = A.S.cache_offset(A.S.seq_of(at), l, apos) + ag * hd;
+                for (uint32_t i = tid; i < 2 * row8; i += kMConsumers) {
+                    const uint16_t* src = (i < row8 ? A.S.kcache : A.S.vcache) + crow + (i % row8) * 8;
+                    reinterpret_cast<uint4*>((i < row8 ? kst : vst) + (size_t)apos * hd)[i % row8] = __ldcg(reinterpret_cast<const uint4*>(src));
+                }
+            }
+            cp_async_wait_all();
+            cbar();
+            stamp_a(A, l, 3);
+            attend(A, l, at, ag, apos, Xd, kst, vst, cap, hs);
+            stamp_a(A, l, 4);
+            // this head's share of the o-projection for rows [R.r0, R.r1) of the head-major copy
+            if (!wait_slice()) return;
+            stamp_a(A, l, 5);
+            {
+                const MegaRange& Rr = sdesc[slice % NS].range[0];
+                const uint8_t* slot = slot_ptr();
+                const uint32_t cpr = hd / 32;  // 32-element chunks per row of the head slice
+                const uint4* P = reinterpret_cast<const uint4*>(slot + Rr.off_p);
+                const float* sc = reinterpret_cast<const float*>(slot + Rr.off_s);
+                const uint32_t* zw = reinterpret_cast<const uint32_t*>(slot + Rr.off_z);
+                double* out = A.opart + ((size_t)at * A.heads + ah) * H;
+                for (uint32_t row = Rr.r0 + tid; row < Rr.r1; row += kMConsumers) {
+                    const double zd = magic_d((zw[(row >> 3) - Rr.z_base] >> ((row & 7u) * 4u)) & 0xFu);
+                    const double s = (double)sc[row - Rr.s_base];
+                    double acc = 0.0;
+                    for (uint32_t cc = 0; cc < cpr; ++cc) {
+                        const uint4 q = P[(size_t)(row - Rr.r0) * cpr + cc];
+                        const uint32_t w4[4] = {q.x, q.y, q.z, q.w};
+                        double p0 = 0.0, p1 = 0.0;
+#pragma unroll
+                        for (int e = 0; e < 32; e += 2) {
+                            const uint32_t wd = w4[e >> 3];
+                            p0 = fma(magic_d((wd >> ((e & 7) * 4)) & 0xFu) - zd, hs.ad[cc * 32 + e], p0);
+                            p1 = fma(magic_d((wd >> (((e + 1) & 7) * 4)) & 0xFu) - zd, hs.ad[cc * 32 + e + 1], p1);
+                        }
+                        acc = fma(p0 + p1, s, acc);
+                    }
+                    out[row - ah * H] = acc;
+                }
+            }
+            release_slice();
         }
-        release_slice();
-        stamp(A, 3 * (kMegaStages * l + 2) + 2);
+        stamp(A, 3 * (kMegaStages * l + 0) + 2);
         if (!grid_sync(A, bar_index, &s_fail)) return;
 
-        // ---------------- S4: RMSNorm + gate|up + SiLU --------------------------------------
-        stamp(A, 3 * (kMegaStages * l + 3));
-        load_norm<4, MT>(Xd, A.S.x, false, H, La.norm_post, A.eps, rs, red);
+        // ---------------- C: residual + RMSNorm + gate|up + SiLU ----------------------------
+        stamp(A, 3 * (kMegaStages * l + 1));
+        for (uint32_t t = 0; t < MT; ++t)
+            for (uint32_t r = tid; r < H; r += kMConsumers) {
+                const double* p = A.opart + (size_t)t * A.heads * H + r;
+                double o = 0.0;
+                for (uint32_t h = 0; h < A.heads; ++h) o += __ldcg(p + (size_t)h * H);  // fixed head order
+                xs[t * H + r] = __ldcg(A.S.x + t * H + r) + (float)o;
+            }
         if (!wait_slice()) return;
-        stamp(A, 3 * (kMegaStages * l + 3) + 1);
+        stamp(A, 3 * (kMegaStages * l + 1) + 1);
         {
-            const MegaSlice& D = T[slice];
+            const MegaSlice& D = sdesc[slice % NS];
+            const uint8_t* slot = slot_ptr();
+            load_norm<4, MT>(Xd, xs, true, H, reinterpret_cast<const float*>(slot + D.off_v), A.eps, rs, red);
             if (D.nrange) {
-                const uint8_t* slot = slot_ptr();
                 const MegaRange& Rg = D.range[0];
                 const MegaRange& Ru = D.range[1];
                 const uint32_t nr = Rg.r1 - Rg.r0;
@@ -535,86 +677,143 @@ __global__ void __launch_bounds__(kMThreads, 1) k_mega(const __grid_constant__ M
                     if (lane == 0)
 #pragma unroll
                         for (int t = 0; t < MT; ++t) {
-                            res[i][t] = acc[0][t];
-                            res[nr + i][t] = acc[1][t];
+                            res[i * MT + t] = acc[0][t];
+                            res[(nr + i) * MT + t] = acc[1][t];
                         }
                 }
                 cbar();
                 for (uint32_t e = tid; e < nr * MT; e += kMConsumers) {
                     const uint32_t i = e / MT, t = e % MT;
-                    A.S.gated[(size_t)t * I + Rg.r0 + i] = silu_mul_value((float)res[i][t], (float)res[nr + i][t]);
+                    A.S.gated[(size_t)t * I + Rg.r0 + i] = silu_mul_value((float)res[i * MT + t], (float)res[(nr + i) * MT + t]);
                 }
             }
         }
         release_slice();
-        stamp(A, 3 * (kMegaStages * l + 3) + 2);
+        stamp(A, 3 * (kMegaStages * l + 1) + 2);
         if (!grid_sync(A, bar_index, &s_fail)) return;
 
-        // ---------------- S5: down + residual -----------------------------------------------
-        stamp(A, 3 * (kMegaStages * l + 4));
+        // ---------------- D: down + residual ------------------------------------------------
+        stamp(A, 3 * (kMegaStages * l + 2));
         {
             const uint32_t nchunk = I / 32;
-            for (uint32_t i = tid; i < MT * I; i += kMConsumers)
-                Xd[xd_index<4>(i / I, i % I, nchunk)] = (double)__ldcg(A.S.gated + i);
-            cbar();
+            constexpr int PER = 8;
+            for (uint32_t t = 0; t < MT; ++t)
+                for (uint32_t i0 = tid; i0 < I; i0 += PER * kMConsumers) {  // batched L2 reads
+                    float v[PER];
+#pragma unroll
+                    for (int k = 0; k < PER; ++k) {
+                        const uint32_t i = i0 + k * kMConsumers;
+                        v[k] = i < I ? __ldcg(A.S.gated + t * I + i) : 0.f;
+                    }
+#pragma unroll
+                    for (int k = 0; k < PER; ++k) {
+                        const uint32_t i = i0 + k * kMConsumers;
+                        if (i < I) Xd[xd_index<4>(t, i, nchunk)] = (double)v[k];
+                    }
+                }
         }
         if (!wait_slice()) return;
-        stamp(A, 3 * (kMegaStages * l + 4) + 1);
+        stamp(A, 3 * (kMegaStages * l + 2) + 1);
         {
-            const MegaSlice& D = T[slice];
+            const MegaSlice& D = sdesc[slice % NS];
             if (D.nrange) {
-                const MegaRange& R = D.range[0];
+                const MegaRange& Rr = D.range[0];
                 const uint8_t* slot = slot_ptr();
-                const uint32_t nr = R.r1 - R.r0, nchunk = I / 32;
+                const uint32_t nr = Rr.r1 - Rr.r0, nchunk = I / 32;
                 const uint32_t parts = nr >= (uint32_t)kMWarps ? 1 : kMWarps / nr;  // split K across warps
                 for (uint32_t w = warp; w < nr * parts; w += kMWarps) {
                     const uint32_t i = w / parts, p = w % parts;
                     const uint32_t c0 = nchunk * p / parts, c1 = nchunk * (p + 1) / parts;
                     double acc[MT];
-                    row_dot<4, MT>(slot, R, R.r0 + i, I, XD, nchunk, c0, c1, lane, acc);
+                    row_dot<4, MT>(slot, Rr, Rr.r0 + i, I, XD, nchunk, c0, c1, lane, acc);
                     if (lane == 0)
 #pragma unroll
-                        for (int t = 0; t < MT; ++t) res[w][t] = acc[t];
+                        for (int t = 0; t < MT; ++t) res[w * MT + t] = acc[t];
                 }
                 cbar();
                 for (uint32_t e = tid; e < nr * MT; e += kMConsumers) {
                     const uint32_t i = e / MT, t = e % MT;
                     double v = 0.0;
-                    for (uint32_t p = 0; p < parts; ++p) v += res[i * parts + p][t];  // fixed order
-                    float* xp = A.S.x + (size_t)t * H + R.r0 + i;
-                    *xp = __ldcg(xp) + (float)v;
+                    for (uint32_t p = 0; p < parts; ++p) v += res[(i * parts + p) * MT + t];  // fixed order
+                    A.S.x[(size_t)t * H + Rr.r0 + i] = xs[(size_t)t * H + Rr.r0 + i] + (float)v;
                 }
             }
         }
         release_slice();
-        stamp(A, 3 * (kMegaStages * l + 4) + 2);
+        stamp(A, 3 * (kMegaStages * l + 2) + 2);
         if (!grid_sync(A, bar_index, &s_fail)) return;
     }
 
     // ---------------- final RMSNorm + tied head ---------------------------------------------
     stamp(A, 3 * (kMegaStages * A.layers));
-    load_norm<HB, MT>(Xd, A.S.x, false, H, A.final_norm, A.eps, rs, red);
-    if (c == 0)
-        for (uint32_t i = tid; i < MT * H; i += kMConsumers)
-            A.S.normed[i] = norm_value(__ldcg(A.S.x + i), rs[i / H], A.final_norm[i % H]);
     const uint32_t nchunk = H / Geom<HB>::E;
+    bool first = true;
     while (slice < total) {
         if (!wait_slice()) return;
-        const MegaSlice& D = T[slice];
+        const MegaSlice& D = sdesc[slice % NS];
+        const uint8_t* slot = slot_ptr();
+        if (first) {  // the first head slice carries the final-norm gain
+            const float* gain = reinterpret_cast<const float*>(slot + D.off_v);
+            load_norm<HB, MT>(Xd, A.S.x, false, H, gain, A.eps, rs, red);
+            if (c == 0)
+                for (uint32_t i = tid; i < MT * H; i += kMConsumers)
+                    A.S.normed[i] = norm_value(__ldcg(A.S.x + i), rs[i / H], gain[i % H]);
+            first = false;
+        }
         if (D.nrange) {
-            const MegaRange& R = D.range[0];
-            const uint8_t* slot = slot_ptr();
-            for (uint32_t r = R.r0 + 2 * warp; r < R.r1; r += 2 * kMWarps) {
-                const uint32_t r2 = r + 1 < R.r1 ? r + 1 : r;
-                double acc[2][MT];
-                row_dot2<HB, MT>(slot, R, r, R, r2, H, XD, nchunk, lane, acc);
-                if (lane < MT) A.S.logits[(size_t)lane * A.vocab + r] = (float)pick<MT>(acc[0], lane);
-                if (lane < MT && r2 != r) A.S.logits[(size_t)lane * A.vocab + r2] = (float)pick<MT>(acc[1], lane);
+            // a lane per row (rows at a padded stride), the chunks split over the warps, the
+            // warps' partial sums added in a fixed order
+            constexpr int CPB = Geom<HB>::CPB;
+            const MegaRange& Rr = D.range[0];
+            const uint32_t nr = Rr.r1 - Rr.r0, bpr = H / kBlock, pstride = D.rows.dst_stride;
+            const uint32_t c0 = nchunk * warp / kMWarps, c1 = nchunk * (warp + 1) / kMWarps;
+            double* hpart = reinterpret_cast<double*>(kst);  // [warps][32 rows][MT]
+            if ((uint32_t)lane < nr) {
+                const uint32_t row = Rr.r0 + lane;
+                const uint8_t* prow = slot + Rr.off_p + (size_t)lane * pstride;
+                const float* sc = reinterpret_cast<const float*>(slot + Rr.off_s);
+                const uint32_t* zw = reinterpret_cast<const uint32_t*>(slot + Rr.off_z);
+                double acc[1][MT];
+#pragma unroll
+                for (int t = 0; t < MT; ++t) acc[0][t] = 0.0;
+                for (uint32_t cc = c0; cc < c1; ++cc) {
+                    const uint4 q[1] = {*reinterpret_cast<const uint4*>(prow + cc * 16)};
+                    const uint32_t blk = row * bpr + cc / CPB;
+                    const float s[1] = {sc[blk - Rr.s_base]};
+                    const uint32_t zc[1] = {HB == 4 ? (zw[(blk >> 3) - Rr.z_base] >> ((blk & 7u) * 4u)) & 0xFu
+                                                    : (zw[(blk >> 2) - Rr.z_base] >> ((blk & 3u) * 8u)) & 0xFFu};
+                    chunk_dot<HB, MT, 1>(q, s, zc, XD, nchunk, cc, acc);
+                }
+#pragma unroll
+                for (int t = 0; t < MT; ++t) hpart[(warp * 32 + lane) * MT + t] = acc[0][t];
+            }
+            cbar();
+            for (uint32_t e = tid; e < nr * MT; e += kMConsumers) {
+                const uint32_t i = e / MT, t = e % MT;
+                double v = 0.0;
+                for (int w = 0; w < kMWarps; ++w) v += hpart[(w * 32 + i) * MT + t];
+                A.S.logits[(size_t)t * A.vocab + Rr.r0 + i] = (float)v;
             }
         }
         release_slice();
     }
     stamp(A, 3 * (kMegaStages * A.layers) + 2);
+}
+
+// Head-major copy of an o-projection (see mega_wo_heads): a thread per (head, 8 rows).
+__global__ void k_wo_heads(QW wo, uint32_t heads, uint32_t hd, uint32_t* P, float* S, uint32_t* Z) {
+    const uint32_t H = wo.rows, wpr = wo.cols / 8, hw = hd / 8, bpr = wo.cols / kBlock;
+    const uint32_t idx = blockIdx.x * blockDim.x + threadIdx.x;
+    if (idx >= heads * (H / 8)) return;
+    const uint32_t h = idx / (H / 8), r0 = (idx % (H / 8)) * 8;
+    uint32_t zword = 0;
+    for (uint32_t k = 0; k < 8; ++k) {
+        const uint32_t r = r0 + k, blk = r * bpr + (h * hd) / kBlock;
+        S[(size_t)h * H + r] = wo.scales[blk];
+        zword |= zero_code<4>(wo.zeros, blk) << (4 * k);
+        for (uint32_t w = 0; w < hw; ++w) P[((size_t)h * H + r) * hw + w] = wo.packed[(size_t)r * wpr + h * hw + w];
+    }
+    Z[(size_t)h * (H / 8) + r0 / 8] = zword;
 }
 
 // ---------------------------------------------------------------------------------------------
@@ -625,90 +824,161 @@ static uint32_t split_lo(uint32_t total, uint32_t parts, uint32_t i, uint32_t gr
     return (uint32_t)(((uint64_t)units * i) / parts) * granule;
 }
 
-// Adds the copies and the compute record of rows [r0, r1) of `w` at byte `cursor` of the slot.
+static size_t align256(size_t v) { return (v + 255) & ~size_t(255); }
+
+size_t mega_wo_heads_bytes(uint32_t hidden, uint32_t heads, uint32_t head_dim) {
+    const size_t rows = (size_t)heads * hidden;
+    return align256(rows * head_dim / 2) + align256(rows * 4) + align256(rows / 2);
+}
+
+cudaError_t mega_wo_heads(const QW& wo, uint32_t heads, uint32_t head_dim, uint8_t* out, QW* view, cudaStream_t st) {
+    const size_t rows = (size_t)heads * wo.rows;
+    uint32_t* P = reinterpret_cast<uint32_t*>(out);
+    float* S = reinterpret_cast<float*>(out + align256(rows * head_dim / 2));
+    uint32_t* Z = reinterpret_cast<uint32_t*>(out + align256(rows * head_dim / 2) + align256(rows * 4));
+    const uint32_t n = heads * (wo.rows / 8);
+    k_wo_heads<<<(n + 255) / 256, 256, 0, st>>>(wo, heads, head_dim, P, S, Z);
+    *view = QW{P, S, Z, (uint32_t)rows, head_dim};
+    return cudaGetLastError();
+}
+
+static uint32_t up16(uint32_t v) { return (v + 15) & ~15u; }
+
+// Adds a plain copy of `bytes` (a multiple of 16, 16-byte aligned source) at byte `cursor`.
+static uint32_t plan_copy(MegaSlice& S, const void* src, uint32_t bytes, uint32_t cursor) {
+    S.copy[S.ncopy++] = MegaCopy{(unsigned long long)src, bytes, cursor};
+    S.bytes += bytes;
+    return up16(cursor + bytes);
+}
+
+// Adds the copies and the compute record of rows [r0, r1) of `w` at byte `cursor` of the slot,
+// and their biases when `bias` is given (r0 and r1 multiples of 4).  bpr = scales per row (0:
+// cols / 64).
 static uint32_t plan_range(MegaSlice& S, const QW& w, int bits, uint32_t r0, uint32_t r1, uint32_t tag,
-                           uint32_t cursor) {
+                           uint32_t cursor, uint32_t bpr_override = 0, const float* bias = nullptr) {
     auto down16 = [](uint64_t v) { return v & ~uint64_t(15); };
-    auto up16 = [](uint64_t v) { return (v + 15) & ~uint64_t(15); };
+    auto up16l = [](uint64_t v) { return (v + 15) & ~uint64_t(15); };
     MegaRange& R = S.range[S.nrange++];
     R.r0 = r0;
     R.r1 = r1;
     R.tag = tag;
-    const uint64_t row_bytes = (uint64_t)w.cols * bits / 8, bpr = w.cols / kBlock, zpw = 32 / bits;
-    const uint64_t pb = r0 * row_bytes, pn = (r1 - r0) * row_bytes;  // multiple of 16 (cols % 64 == 0)
-    const uint64_t sb = down16(r0 * bpr * 4), se = up16(r1 * bpr * 4);
-    const uint64_t zb = down16((r0 * bpr / zpw) * 4), ze = up16(((r1 * bpr + zpw - 1) / zpw) * 4);
+    const uint64_t row_bytes = (uint64_t)w.cols * bits / 8, zpw = 32 / bits;
+    const uint64_t bpr = bpr_override ? bpr_override : w.cols / kBlock;
+    const uint64_t pb = r0 * row_bytes, pn = (r1 - r0) * row_bytes;  // multiple of 16 (cols % 32 == 0)
+    const uint64_t sb = down16(r0 * bpr * 4), se = up16l(r1 * bpr * 4);
+    const uint64_t zb = down16((r0 * bpr / zpw) * 4), ze = up16l(((r1 * bpr + zpw - 1) / zpw) * 4);
     R.off_p = cursor;
-    S.copy[S.ncopy++] = MegaCopy{(unsigned long long)(reinterpret_cast<const uint8_t*>(w.packed) + pb), (uint32_t)pn, cursor};
-    cursor += (uint32_t)pn;
+    cursor = plan_copy(S, reinterpret_cast<const uint8_t*>(w.packed) + pb, (uint32_t)pn, cursor);
     R.off_s = cursor;
     R.s_base = (uint32_t)(sb / 4);
-    S.copy[S.ncopy++] = MegaCopy{(unsigned long long)(reinterpret_cast<const uint8_t*>(w.scales) + sb), (uint32_t)(se - sb), cursor};
-    cursor += (uint32_t)(se - sb);
+    cursor = plan_copy(S, reinterpret_cast<const uint8_t*>(w.scales) + sb, (uint32_t)(se - sb), cursor);
     R.off_z = cursor;
     R.z_base = (uint32_t)(zb / 4);
-    S.copy[S.ncopy++] = MegaCopy{(unsigned long long)(reinterpret_cast<const uint8_t*>(w.zeros) + zb), (uint32_t)(ze - zb), cursor};
-    cursor += (uint32_t)(ze - zb);
-    S.bytes += (uint32_t)(pn + (se - sb) + (ze - zb));
-    return (uint32_t)up16(cursor);
+    cursor = plan_copy(S, reinterpret_cast<const uint8_t*>(w.zeros) + zb, (uint32_t)(ze - zb), cursor);
+    if (bias) {
+        R.off_b = cursor;
+        cursor = plan_copy(S, bias + r0, (r1 - r0) * 4, cursor);
+    }
+    return cursor;
 }
 
-void mega_build_table(const MegaArgs& A, const MegaGeometry& g, std::vector<MegaSlice>& table,
-                      std::vector<uint32_t>& counts, uint32_t& stride) {
-    const uint32_t G = g.grid, L = A.layers;
+// Head rows [r0, r1): packed codes one row per copy at a 16-byte-padded stride, then scales and
+// zero words as in plan_range.
+static void plan_head_rows(MegaSlice& S, const QW& w, int bits, uint32_t r0, uint32_t r1, uint32_t cursor) {
+    auto down16 = [](uint64_t v) { return v & ~uint64_t(15); };
+    auto up16l = [](uint64_t v) { return (v + 15) & ~uint64_t(15); };
+    MegaRange& R = S.range[S.nrange++];
+    R.r0 = r0;
+    R.r1 = r1;
+    const uint32_t row_bytes = w.cols * bits / 8, zpw = 32 / bits, bpr = w.cols / kBlock;
+    S.rows = MegaRows{(unsigned long long)(reinterpret_cast<const uint8_t*>(w.packed) + (size_t)r0 * row_bytes), r1 - r0,
+                      row_bytes, row_bytes, cursor, row_bytes + 16, 0};
+    S.bytes += (r1 - r0) * row_bytes;
+    R.off_p = cursor;
+    cursor = up16(cursor + (r1 - r0) * (row_bytes + 16));
+    const uint64_t sb = down16((uint64_t)r0 * bpr * 4), se = up16l((uint64_t)r1 * bpr * 4);
+    const uint64_t zb = down16(((uint64_t)r0 * bpr / zpw) * 4), ze = up16l((((uint64_t)r1 * bpr + zpw - 1) / zpw) * 4);
+    R.off_s = cursor;
+    R.s_base = (uint32_t)(sb / 4);
+    cursor = plan_copy(S, reinterpret_cast<const uint8_t*>(w.scales) + sb, (uint32_t)(se - sb), cursor);
+    R.off_z = cursor;
+    R.z_base = (uint32_t)(zb / 4);
+    plan_copy(S, reinterpret_cast<const uint8_t*>(w.zeros) + zb, (uint32_t)(ze - zb), cursor);
+}
+
+static uint32_t mega_att_reps(uint32_t mt, uint32_t heads, uint32_t grid) {
+    const uint32_t r = grid / (mt * heads);
+    return r > 4 ? 4 : (r < 1 ? 1 : r);
+}
+
+void mega_build_table(uint32_t mt, const MegaArgs& A, const QW* wo_heads, const MegaGeometry& g,
+                      std::vector<MegaSlice>& table, std::vector<uint32_t>& counts, uint32_t& stride) {
+    const uint32_t G = g.grid, L = A.layers, hd = A.head_dim, half = hd / 2, per_slot = half / 4;
+    const uint32_t units = (A.heads + 2 * A.kv_heads) * per_slot, R = g.att_reps;
     uint32_t max_head = 0;
     for (uint32_t c = 0; c < G; ++c) {
         const uint32_t h0 = split_lo(A.vocab, G, c, 1), h1 = split_lo(A.vocab, G, c + 1, 1);
         const uint32_t n = (h1 - h0 + g.head_chunk - 1) / g.head_chunk;
         max_head = n > max_head ? n : max_head;
     }
-    stride = 4 * L + max_head;
+    stride = 4 * L + (max_head ? max_head : 1);
     table.assign((size_t)G * stride, MegaSlice{});
     counts.assign(G, 0);
-    const uint32_t half = A.head_dim / 2, per_slot = half / 4;
-    const uint32_t units = (A.heads + 2 * A.kv_heads) * per_slot;
     for (uint32_t c = 0; c < G; ++c) {
         MegaSlice* T = table.data() + (size_t)c * stride;
+        uint32_t i = 0;
         for (uint32_t l = 0; l < L; ++l) {
             const LayerArgs& La = A.layer[l];
-            {  // S1: units of 4 RoPE pairs of one head slot of the q|k|v row space
-                MegaSlice& S = T[4 * l];
-                uint32_t cur = 0;
-                for (uint32_t u = c; u < units && S.nrange + 2 <= 4; u += G) {
+            {  // q|k|v units of 4 RoPE pairs (this CTA's share), after the input-norm gain
+                MegaSlice& S = T[i++];
+                S.off_v = 0;
+                uint32_t cur = plan_copy(S, La.norm_in, A.hidden * 4, 0);
+                for (uint32_t u = c; u < units; u += G) {
                     const uint32_t hs = u / per_slot, i0 = (u % per_slot) * 4;
                     const QW* w;
+                    const float* bias;
                     uint32_t head, kind;
-                    if (hs < A.heads) { w = &La.wq; head = hs; kind = 0; }
-                    else if (hs < A.heads + A.kv_heads) { w = &La.wk; head = hs - A.heads; kind = 1; }
-                    else { w = &La.wv; head = hs - A.heads - A.kv_heads; kind = 2; }
-                    const uint32_t b = head * A.head_dim + i0;
-                    cur = plan_range(S, *w, 4, b, b + 4, kind, cur);
-                    cur = plan_range(S, *w, 4, b + half, b + half + 4, kind, cur);
+                    if (hs < A.heads) { w = &La.wq; bias = La.bq; head = hs; kind = 0; }
+                    else if (hs < A.heads + A.kv_heads) { w = &La.wk; bias = La.bk; head = hs - A.heads; kind = 1; }
+                    else { w = &La.wv; bias = La.bv; head = hs - A.heads - A.kv_heads; kind = 2; }
+                    const uint32_t b = head * hd + i0;
+                    cur = plan_range(S, *w, 4, b, b + 4, kind, cur, 0, bias);
+                    cur = plan_range(S, *w, 4, b + half, b + half + 4, kind, cur, 0, bias);
                 }
             }
-            {
-                const uint32_t r0 = split_lo(A.hidden, G, c, 2), r1 = split_lo(A.hidden, G, c + 1, 2);
-                if (r1 > r0) plan_range(T[4 * l + 1], La.wo, 4, r0, r1, 0, 0);
+            if (c < mt * A.heads * R) {  // attention CTA: its rows of the head's o-projection columns
+                const uint32_t h = (c / R) % A.heads, rep = c % R;
+                const uint32_t r0 = split_lo(A.hidden, R, rep, 8), r1 = split_lo(A.hidden, R, rep + 1, 8);
+                plan_range(T[i++], wo_heads[l], 4, h * A.hidden + r0, h * A.hidden + r1, 3, 0, 1);
             }
             {
+                MegaSlice& S = T[i++];
+                S.off_v = 0;
+                uint32_t cur = plan_copy(S, La.norm_post, A.hidden * 4, 0);
                 const uint32_t r0 = split_lo(A.intermediate, G, c, 1), r1 = split_lo(A.intermediate, G, c + 1, 1);
                 if (r1 > r0) {
-                    const uint32_t cur = plan_range(T[4 * l + 2], La.wg, 4, r0, r1, 0, 0);
-                    plan_range(T[4 * l + 2], La.wu, 4, r0, r1, 0, cur);
+                    cur = plan_range(S, La.wg, 4, r0, r1, 0, cur);
+                    plan_range(S, La.wu, 4, r0, r1, 0, cur);
                 }
             }
             {
                 const uint32_t r0 = split_lo(A.hidden, G, c, 2), r1 = split_lo(A.hidden, G, c + 1, 2);
-                if (r1 > r0) plan_range(T[4 * l + 3], La.wd, 4, r0, r1, 0, 0);
+                if (r1 > r0) plan_range(T[i], La.wd, 4, r0, r1, 0, 0);
+                ++i;
             }
         }
         const uint32_t h0 = split_lo(A.vocab, G, c, 1), h1 = split_lo(A.vocab, G, c + 1, 1);
+        {  // the first head slice carries the final-norm gain (even when this CTA has no rows)
+            MegaSlice& S = T[i];
+            S.off_v = 0;
+            plan_copy(S, A.final_norm, A.hidden * 4, 0);
+        }
         uint32_t j = 0;
         for (uint32_t r0 = h0; r0 < h1; r0 += g.head_chunk, ++j) {
             const uint32_t r1 = r0 + g.head_chunk < h1 ? r0 + g.head_chunk : h1;
-            plan_range(T[4 * L + j], A.head, A.head_bits, r0, r1, 0, 0);
+            plan_head_rows(T[i + j], A.head, A.head_bits, r0, r1, j == 0 ? up16(A.hidden * 4) : 0);
         }
-        counts[c] = 4 * L + j;
+        counts[c] = i + (j ? j : 1);
     }
 }
 
@@ -737,25 +1007,28 @@ MegaGeometry mega_geometry(uint32_t mt, const MegaArgs& A) {
     cudaDeviceGetAttribute(&maxsm, cudaDevAttrMaxSharedMemoryPerBlockOptin, dev);
     g.grid = (uint32_t)sms;
     g.head_chunk = 32;
+    g.att_reps = mega_att_reps(mt, A.heads, g.grid);
     const uint32_t x4 = A.intermediate > A.hidden ? A.intermediate : A.hidden;
     g.x4_floats = x4;
-    auto range_bytes = [](uint32_t rows, uint32_t cols, uint32_t bits) {
-        const uint32_t bpr = cols / 64;
-        return rows * cols * bits / 8 + rows * bpr * 4 + 32 + rows * bpr * bits / 8 + 32 + 48;
+    auto range_bytes = [](uint32_t rows, uint32_t cols, uint32_t bits, uint32_t bpr) {
+        return rows * cols * bits / 8 + rows * bpr * 4 + 32 + rows * bpr * bits / 8 + 32 + 48 + rows * 4 + 16;
     };
+    const uint32_t bprH = A.hidden / 64, bprI = A.intermediate / 64, gain = A.hidden * 4 + 16;
     const uint32_t rows4 = (A.intermediate + g.grid - 1) / g.grid + 1;
     const uint32_t rows5 = ((A.hidden / 2 + g.grid - 1) / g.grid) * 2 + 2;
-    uint32_t slot = 2 * range_bytes(rows4, A.hidden, 4);
-    const uint32_t s5 = range_bytes(rows5, A.intermediate, 4);
-    const uint32_t s1 = 4 * range_bytes(4, A.hidden, 4);
-    const uint32_t hc = range_bytes(g.head_chunk, A.hidden, (uint32_t)A.head_bits);
-    if (s5 > slot) slot = s5;
-    if (s1 > slot) slot = s1;
-    if (hc > slot) slot = hc;
+    const uint32_t orows = (A.hidden + g.att_reps - 1) / g.att_reps + 8;
+    const uint32_t units = (A.heads + 2 * A.kv_heads) * (A.head_dim / 8);
+    const uint32_t upc = (units + g.grid - 1) / g.grid;  // q|k|v units per CTA
+    uint32_t slot = gain + 2 * range_bytes(rows4, A.hidden, 4, bprH);
+    const uint32_t cand[4] = {range_bytes(rows5, A.intermediate, 4, bprI), gain + upc * 2 * range_bytes(4, A.hidden, 4, bprH),
+                              range_bytes(orows, A.head_dim, 4, 1),
+                              gain + range_bytes(g.head_chunk, A.hidden, (uint32_t)A.head_bits, bprH) + 16 * g.head_chunk};
+    for (uint32_t v : cand) slot = v > slot ? v : slot;
     slot = (slot + 127) & ~127u;
     g.slot_bytes = slot;
-    const size_t fixed = 256 + (size_t)mt * x4 * 8 + (size_t)mt * A.hidden * 4 + (size_t)kKvStage * A.kv_heads * A.head_dim * 2;
-    const size_t statics = sizeof(double) * (mt + mt * kMWarps + kMaxRes * mt) + 64;
+    const size_t fixed = 256 + (size_t)mt * x4 * 8 + (((size_t)mt * A.hidden * 4 + 15) & ~size_t(15)) + (size_t)kKvHalfs * 2;
+    const size_t statics = sizeof(double) * (mt + mt * kMWarps + kMaxRes * mt + mt * kHeadDimMax) + sizeof(HeadSmem) +
+                           sizeof(MegaSlice) * kMegaSlots + 64;
     const int64_t room = (int64_t)maxsm - (int64_t)fixed - (int64_t)statics - 1024;
     int ns = room > 0 ? (int)(room / slot) : 0;
     if (ns > (int)kMegaSlots) ns = kMegaSlots;
@@ -763,11 +1036,10 @@ MegaGeometry mega_geometry(uint32_t mt, const MegaArgs& A) {
     g.smem = fixed + (size_t)g.nslots * slot;
     g.max_positions = mt * x4;  // scores of one head, as doubles, in the activation area
     // shapes the kernel's fixed per-CTA capacities cannot take: report no ring (not eligible)
-    const uint32_t s1_units = (A.heads + 2 * A.kv_heads) * (A.head_dim / 8);
-    const uint32_t rows_up = (A.intermediate + g.grid - 1) / g.grid + 1;
-    if (s1_units > 2 * g.grid || 2 * rows_up > (uint32_t)kMaxRes || rows5 > (uint32_t)kMaxRes ||
-        (size_t)mt * A.hidden > 8 * (size_t)kMConsumers ||
-        A.hidden > 2 * (uint32_t)kMConsumers || A.head_dim % 8 != 0 || A.heads / A.kv_heads > kMaxGroup)
+    if (upc > 2 || 2 * rows4 > (uint32_t)kMaxRes || rows5 > (uint32_t)kMaxRes || mt * A.heads > g.grid ||
+        (A.head_dim != 32 && A.head_dim != 64) || A.hidden % 64 != 0 || A.intermediate % 64 != 0 ||
+        A.hidden > 2 * (uint32_t)kMConsumers || A.kv_heads == 0 || A.heads % A.kv_heads != 0 ||
+        A.kv_heads * (size_t)mt > 2 * (kMegaBarWords - 8))
         g.nslots = 0;
     return g;
 }

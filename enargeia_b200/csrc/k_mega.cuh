@@ -9,7 +9,9 @@ namespace enx {
 
 constexpr uint32_t kMaxLayers = 32;
 constexpr uint32_t kMegaSlots = 8;   // upper bound on ring slots
-constexpr uint32_t kMegaStages = 5;  // grid-barrier stages per layer (qkv, attention, o, gate/up, down)
+constexpr uint32_t kMegaStages = 3;  // grid-barrier stages per layer (attention, gate/up, down)
+constexpr uint32_t kMegaTraceDetail = 8;  // extra stamps per layer inside stage A
+constexpr uint32_t kMegaBarWords = 64;    // u64 words of barrier + ready counters (zeroed per launch)
 
 // One bulk copy of a slice: global source, size, destination offset inside the slot.
 struct MegaCopy {
@@ -18,19 +20,27 @@ struct MegaCopy {
 };
 
 // A row range [r0, r1) of one quantised tensor as staged in a slot: where its packed codes,
-// scales and zero words start inside the slot, and the global scale / zero-word index of the
-// first staged scale / zero word (the copies are widened to 16-byte boundaries).
+// scales, zero words and (q|k|v units) biases start inside the slot, and the global scale /
+// zero-word index of the first staged scale / zero word (copies are widened to 16 bytes).
 struct MegaRange {
     uint32_t r0, r1;
-    uint32_t off_p, off_s, off_z;
+    uint32_t off_p, off_s, off_z, off_b;
     uint32_t s_base, z_base;
-    uint32_t tag;  // stage-specific: q/k/v kind for the q|k|v stage
+    uint32_t tag;  // q|k|v units: 0 q, 1 k, 2 v
 };
 
-// Everything one CTA needs for one slice (one stage of one layer, or one chunk of head rows).
+// Rows copied one by one to a padded stride in the slot (conflict-free row-per-lane reads).
+struct MegaRows {
+    unsigned long long src;
+    uint32_t n, bytes, src_stride, dst, dst_stride, pad;
+};
+
+// Everything one CTA needs for one slice (one weight group of one stage, or a chunk of head rows):
+// the bulk copies and, for stages that start with an RMSNorm, the slot offset of its gain vector.
 struct MegaSlice {
-    uint32_t ncopy, nrange, bytes, pad;
-    MegaCopy copy[12];
+    uint32_t ncopy, nrange, bytes, off_v;
+    MegaCopy copy[18];
+    MegaRows rows;
     MegaRange range[4];
 };
 
@@ -43,7 +53,10 @@ struct MegaArgs {
     const float* final_norm;
     StepArgs S;                   // activations, caches, RoPE table, positions
     const uint32_t* tokens;       // [MT] ids fed this step (device)
+    double* opart;                // [MT][heads][hidden] o-projection partial sums per head
     unsigned long long* bar;      // grid-barrier arrival counter, zeroed before each launch
+    uint32_t* ready;              // [MT][kv_heads] q|k|v units done (monotonic over layers), zeroed too
+    uint32_t att_reps;            // attention CTAs per (token, head): each does a share of the o rows
     uint32_t* err;                // sticky error: 1 barrier timeout, 2 copy timeout
     const MegaSlice* table;       // [grid][table_stride] slices, built on the host
     const uint32_t* nslices;      // [grid] slices per CTA
@@ -53,15 +66,22 @@ struct MegaArgs {
 };
 
 struct MegaGeometry {
-    uint32_t grid, nslots, slot_bytes, x4_floats, max_positions, head_chunk;
+    uint32_t grid, nslots, slot_bytes, x4_floats, max_positions, head_chunk, att_reps;
     size_t smem;
 };
 
-// Grid, ring and shared-memory geometry for `mt` tokens.
+// Grid, ring and shared-memory geometry for `mt` tokens; nslots < 2 means the shape is not supported.
 MegaGeometry mega_geometry(uint32_t mt, const MegaArgs& A);
-// The per-CTA slice table for that geometry (host side): table[c * stride + i], counts[c].
-void mega_build_table(const MegaArgs& A, const MegaGeometry& g, std::vector<MegaSlice>& table,
-                      std::vector<uint32_t>& counts, uint32_t& stride);
+// The per-CTA slice table for `mt` tokens (host side): table[c * stride + i], counts[c].
+// wo_heads[l] is layer l's o-projection re-laid out head-major (mega_wo_heads).
+void mega_build_table(uint32_t mt, const MegaArgs& A, const QW* wo_heads, const MegaGeometry& g,
+                      std::vector<MegaSlice>& table, std::vector<uint32_t>& counts, uint32_t& stride);
+// Bytes of one layer's head-major o-projection copy, and the kernel that writes it: head h's
+// columns [h*hd, (h+1)*hd) of every row, as rows h*hidden + r of a (heads*hidden) x hd tensor
+// with one scale and one zero-point per row.
+size_t mega_wo_heads_bytes(uint32_t hidden, uint32_t heads, uint32_t head_dim);
+cudaError_t mega_wo_heads(const QW& wo, uint32_t heads, uint32_t head_dim, uint8_t* out, QW* view,
+                          cudaStream_t st);
 cudaError_t launch_mega(uint32_t mt, const MegaArgs& A, const MegaGeometry& g, cudaStream_t st);
 
 }  // namespace enx

@@ -182,23 +182,39 @@ class Model:
         """Per-stage device times (us) of the last traced step, summed over layers: how long each
         stage waited for its barrier+weights and how long it computed (kernel-group telemetry of
         src/runtime/telemetry.ts, at stage granularity)."""
-        n = 3 * (5 * self.config.layers + 1)
+        L = self.config.layers
+        n = 3 * (3 * L + 1) + 8 * L
         buf = np.zeros(n, dtype=np.uint64)
         cnt = C.c_uint32()
         call("enx_trace", self._h, buf.ctypes.data, n, C.byref(cnt))
-        t = buf.astype(np.float64).reshape(-1, 3) / 1e3
-        names = ["qkv", "attn", "o", "gate_up", "down"]
+        t = buf[: 3 * (3 * L + 1)].astype(np.float64).reshape(-1, 3) / 1e3
+        names = ["attn", "gate_up", "down"]
         out = {f"{k}_{p}": 0.0 for k in names for p in ("wait", "weights", "compute")}
-        L = self.config.layers
-        for i in range(5 * L):
-            k = names[i % 5]
+        for i in range(3 * L):
+            k = names[i % 3]
             prev_done = t[i - 1, 2] if i > 0 else t[i, 0]
             out[f"{k}_wait"] += t[i, 0] - prev_done          # barrier after the previous stage
             out[f"{k}_weights"] += max(t[i, 1] - t[i, 0], 0.0)  # includes the activation loads/norm
             out[f"{k}_compute"] += t[i, 2] - t[i, 1]
-        out["head_wait"] = t[5 * L, 0] - t[5 * L - 1, 2]
-        out["head"] = t[5 * L, 2] - t[5 * L, 0]
-        out["total"] = t[5 * L, 2] - t[0, 0]
+        out["head_wait"] = t[3 * L, 0] - t[3 * L - 1, 2]
+        out["head"] = t[3 * L, 2] - t[3 * L, 0]
+        out["total"] = t[3 * L, 2] - t[0, 0]
+        # inside the attention stage (first CTA): weights + norm, q|k|v units, wait for the kv
+        # head's units, q and current k/v loads, attention, o weights wait, o partial, (unused)
+        d = buf[3 * (3 * L + 1):].astype(np.float64).reshape(L, 8) / 1e3
+        if d.any():
+            marks = ["norm", "units", "ready_wait", "q_load", "attention", "o_wait", "o_partial+end"]
+            d = d[:, :6]
+            starts = t[0:3 * L:3, 0]
+            ends = t[0:3 * L:3, 2]
+            seq = np.concatenate([starts[:, None], d, ends[:, None]], axis=1)
+            for j, m in enumerate(marks):
+                out[f"attn.{m}"] = float(np.sum(seq[:, j + 1] - seq[:, j]))
+            full = buf[3 * (3 * L + 1):].astype(np.float64).reshape(L, 8)[1:] / 1e3
+            t1 = t[3:3 * L:3, 1]
+            out["norm.loads"] = float(np.sum(full[:, 6] - t1))
+            out["norm.rs"] = float(np.sum(full[:, 7] - full[:, 6]))
+            out["norm.stage"] = float(np.sum(full[:, 0] - full[:, 7]))
         return out
 
     def stream_handle(self) -> int:
