@@ -322,6 +322,8 @@ struct enx_ctx {
     uint32_t table_stride[kMaxStepBatch + 1] = {};
     uint8_t* d_wo_heads = nullptr;
     std::vector<QW> wo_heads;
+    uint8_t* d_head_slices = nullptr;
+    QW head_slices{};
     double* d_opart = nullptr;
     uint32_t last_launches = 0;
     // prefill buffers (chunk-sized)
@@ -377,6 +379,7 @@ void free_graphs(enx_ctx* c) {
     }
     dfree(c->d_wo_heads);
     dfree(c->d_opart);
+    dfree(c->d_head_slices);
     c->wo_heads.clear();
 }
 
@@ -876,8 +879,12 @@ static bool mega_eligible(enx_ctx* c, uint32_t B, const StepArgs& S, MegaArgs& A
                 dfree(c->d_wo_heads);
                 return false;
             }
-        if (cudaStreamSynchronize(c->stream) != cudaSuccess) {
+        const size_t hb = mega_head_slices_bytes(C.vocab, C.hidden, c->head.bits);
+        if (dalloc(&c->d_head_slices, hb, "head by slices") != ENX_OK ||
+            mega_head_slices(c->head.embed, c->head.bits, c->d_head_slices, &c->head_slices, c->stream) != cudaSuccess ||
+            cudaStreamSynchronize(c->stream) != cudaSuccess) {
             dfree(c->d_wo_heads);
+            dfree(c->d_head_slices);
             return false;
         }
     }
@@ -885,7 +892,7 @@ static bool mega_eligible(enx_ctx* c, uint32_t B, const StepArgs& S, MegaArgs& A
         std::vector<MegaSlice> table;
         std::vector<uint32_t> counts;
         uint32_t stride = 0;
-        mega_build_table(B, A, c->wo_heads.data(), geo, table, counts, stride);
+        mega_build_table(B, A, c->wo_heads.data(), c->head_slices, geo, table, counts, stride);
         if (dalloc(&c->d_table[B], table.size(), "mega table") != ENX_OK ||
             dalloc(&c->d_nslices[B], counts.size(), "mega counts") != ENX_OK ||
             cudaMemcpy(c->d_table[B], table.data(), table.size() * sizeof(MegaSlice), cudaMemcpyHostToDevice) != cudaSuccess ||
@@ -1140,7 +1147,7 @@ extern "C" enx_status enx_set_tracing(enx_ctx* c, int on) {
     dfree(c->d_trace);
     c->trace_len = 0;
     if (on) {
-        c->trace_len = 3 * (kMegaStages * c->cfg.layers + 1) + kMegaTraceDetail * c->cfg.layers;
+        c->trace_len = 3 * (kMegaStages * c->cfg.layers + 1) + kMegaTraceDetail * c->cfg.layers + 2;
         ENX_TRY(dalloc(&c->d_trace, c->trace_len, "trace"));
         ENX_CUDA(cudaMemset(c->d_trace, 0, (size_t)c->trace_len * 8));
     }

@@ -41,6 +41,7 @@ constexpr uint32_t kSpinLimit = 1u << 24;    // bounded waits (well under a minu
 constexpr uint32_t kKvHalfs = 16384;         // f16 staging of cached K and V rows (32 KB)
 constexpr int kMaxRes = 96;                  // rows per token exchanged in shared memory (C, D)
 constexpr int kHeadDimMax = 64;
+constexpr int kMaxChunks = 192;             // chunks of a staged activation row (K <= 6144)
 
 // ---------------------------------------------------------------------------------------------
 // PTX helpers
@@ -130,11 +131,90 @@ __device__ bool grid_sync(const MegaArgs& A, uint32_t& index, volatile int* s_fa
 // ---------------------------------------------------------------------------------------------
 // dot products against staged rows
 
+// One chunk of R rows against MT tokens with biased codes: (B + q) becomes an exact double in a
+// single byte permute (B = 16 for int4, 4096 for int8, the code landing in the top mantissa
+// bits), so each element costs one DFMA; the bias comes off once per chunk as (B + z) * sum(x)
+// with the chunk sums xsum precomputed for all rows.  Products stay exact ((B + q) * x needs at
+// most 37 bits); the sums are double sums like the reference's, in another order.
+template <int BITS, int MT, int R>
+__device__ __forceinline__ void chunk_dot_b(const uint4 (&q)[R], const float (&s)[R], const uint32_t (&zc)[R],
+                                            const double2* __restrict__ XD, const double* __restrict__ xsum,
+                                            uint32_t nchunk, uint32_t c, double (&acc)[R][MT]) {
+    constexpr int F2 = Geom<BITS>::F2;
+    constexpr int NP = 4;
+    constexpr double B = BITS == 4 ? 16.0 : 4096.0;
+    uint32_t wv[R][BITS == 4 ? 8 : 4];  // int4: per word, even nibbles then odd nibbles as bytes 0x3q
+#pragma unroll
+    for (int r = 0; r < R; ++r) {
+        const uint32_t w4[4] = {q[r].x, q[r].y, q[r].z, q[r].w};
+#pragma unroll
+        for (int i = 0; i < 4; ++i) {
+            if (BITS == 4) {
+                wv[r][2 * i] = (w4[i] & 0x0F0F0F0Fu) | 0x30303030u;
+                wv[r][2 * i + 1] = ((w4[i] >> 4) & 0x0F0F0F0Fu) | 0x30303030u;
+            } else {
+                wv[r][i] = w4[i];
+            }
+        }
+    }
+#pragma unroll
+    for (int t = 0; t < MT; ++t) {
+        double part[R][NP];
+#pragma unroll
+        for (int r = 0; r < R; ++r)
+#pragma unroll
+            for (int p = 0; p < NP; ++p) part[r][p] = 0.0;
+#pragma unroll
+        for (int j = 0; j < F2; ++j) {
+            const double2 xv = XD[(t * F2 + j) * nchunk + c];
+#pragma unroll
+            for (int e = 0; e < 2; ++e) {
+                const int el = j * 2 + e;
+                const double xe = e == 0 ? xv.x : xv.y;
+#pragma unroll
+                for (int r = 0; r < R; ++r) {
+                    uint32_t hi;
+                    if (BITS == 4) {  // element el = nibble (el & 7) of word el >> 3
+                        const uint32_t src = wv[r][2 * (el >> 3) + (el & 1)];
+                        hi = __byte_perm(src, 0x40000000u, 0x7054u | ((uint32_t)((el & 7) >> 1) << 8));
+                    } else {  // element el = byte (el & 3) of word el >> 2
+                        hi = __byte_perm(wv[r][el >> 2], 0x40B00000u, 0x7604u | ((uint32_t)(el & 3) << 4));
+                    }
+                    part[r][el % NP] = fma(__hiloint2double((int)hi, 0), xe, part[r][el % NP]);
+                }
+            }
+        }
+        const double xs = xsum[t * nchunk + c];
+#pragma unroll
+        for (int r = 0; r < R; ++r) {
+            const double p = fma(-(B + (double)zc[r]), xs, (part[r][0] + part[r][1]) + (part[r][2] + part[r][3]));
+            acc[r][t] = fma(p, (double)s[r], acc[r][t]);
+        }
+    }
+}
+
+// Chunk sums of the staged activations (for chunk_dot_b): xsum[t * nchunk + c].
+template <int BITS, int MT>
+__device__ __forceinline__ void stage_xsum(const double* Xd, double* xsum, uint32_t nchunk) {
+    constexpr int F2 = Geom<BITS>::F2;
+    const double2* XD = reinterpret_cast<const double2*>(Xd);
+    for (uint32_t t = 0; t < MT; ++t)
+        for (uint32_t c = threadIdx.x; c < nchunk; c += kMConsumers) {
+            double sum = 0.0;
+#pragma unroll
+            for (int j = 0; j < F2; ++j) {
+                const double2 v = XD[(t * F2 + j) * nchunk + c];
+                sum += v.x + v.y;
+            }
+            xsum[t * nchunk + c] = sum;
+        }
+}
+
 // One staged row over chunks [c0, c1): lane l takes chunks c0+l, c0+l+32, ...
 template <int BITS, int MT>
 __device__ __forceinline__ void row_dot(const uint8_t* slot, const MegaRange& R, uint32_t row, uint32_t cols,
-                                        const double2* __restrict__ XD, uint32_t nchunk, uint32_t c0, uint32_t c1,
-                                        int lane, double (&acc)[MT]) {
+                                        const double2* __restrict__ XD, const double* __restrict__ xsum, uint32_t nchunk,
+                                        uint32_t c0, uint32_t c1, int lane, double (&acc)[MT]) {
     constexpr int CPB = Geom<BITS>::CPB;
     const uint32_t bpr = cols / kBlock;
     const uint4* P = reinterpret_cast<const uint4*>(slot + R.off_p) + (size_t)(row - R.r0) * nchunk;
@@ -149,7 +229,7 @@ __device__ __forceinline__ void row_dot(const uint8_t* slot, const MegaRange& R,
         const float s[1] = {sc[blk - R.s_base]};
         const uint32_t zc[1] = {BITS == 4 ? (zw[(blk >> 3) - R.z_base] >> ((blk & 7u) * 4u)) & 0xFu
                                           : (zw[(blk >> 2) - R.z_base] >> ((blk & 3u) * 8u)) & 0xFFu};
-        chunk_dot<BITS, MT, 1>(q, s, zc, XD, nchunk, c, a);
+        chunk_dot_b<BITS, MT, 1>(q, s, zc, XD, xsum, nchunk, c, a);
     }
 #pragma unroll
     for (int t = 0; t < MT; ++t) acc[t] = warp_sum_d(a[0][t]);
@@ -158,11 +238,11 @@ __device__ __forceinline__ void row_dot(const uint8_t* slot, const MegaRange& R,
 // Two staged rows at once (each x chunk read from shared memory serves both): acc[r][t].
 template <int BITS, int MT>
 __device__ __forceinline__ void row_dot2(const uint8_t* slot, const MegaRange& Ra, uint32_t ra, const MegaRange& Rb,
-                                         uint32_t rb, uint32_t cols, const double2* __restrict__ XD, uint32_t nchunk,
-                                         int lane, double (&acc)[2][MT]) {
+                                         uint32_t rb, uint32_t cols, const double2* __restrict__ XD,
+                                         const double* __restrict__ xsum, uint32_t nchunk, int lane, double (&acc)[2][MT]) {
     if constexpr (MT > 2) {  // register budget: one row at a time
-        row_dot<BITS, MT>(slot, Ra, ra, cols, XD, nchunk, 0, nchunk, lane, acc[0]);
-        row_dot<BITS, MT>(slot, Rb, rb, cols, XD, nchunk, 0, nchunk, lane, acc[1]);
+        row_dot<BITS, MT>(slot, Ra, ra, cols, XD, xsum, nchunk, 0, nchunk, lane, acc[0]);
+        row_dot<BITS, MT>(slot, Rb, rb, cols, XD, xsum, nchunk, 0, nchunk, lane, acc[1]);
         return;
     }
     constexpr int CPB = Geom<BITS>::CPB;
@@ -187,7 +267,7 @@ __device__ __forceinline__ void row_dot2(const uint8_t* slot, const MegaRange& R
             zc[r] = BITS == 4 ? (zw[(blk >> 3) - R.z_base] >> ((blk & 7u) * 4u)) & 0xFu
                               : (zw[(blk >> 2) - R.z_base] >> ((blk & 3u) * 8u)) & 0xFFu;
         }
-        chunk_dot<BITS, MT, 2>(q, s, zc, XD, nchunk, c, acc);
+        chunk_dot_b<BITS, MT, 2>(q, s, zc, XD, xsum, nchunk, c, acc);
     }
 #pragma unroll
     for (int r = 0; r < 2; ++r)
@@ -198,8 +278,8 @@ __device__ __forceinline__ void row_dot2(const uint8_t* slot, const MegaRange& R
 // One pass: read MT rows of x (L2 or shared), RMSNorm them in double, stage the float-rounded
 // outputs as doubles.  K <= 2 * kMConsumers.
 template <int BITS, int MT>
-__device__ void load_norm(double* Xd, const float* x, bool from_smem, uint32_t K, const float* gain, float eps,
-                          double* rs, double* red, const MegaArgs* tr = nullptr, uint32_t tl = 0) {
+__device__ void load_norm(double* Xd, double* xsum, const float* x, bool from_smem, uint32_t K, const float* gain,
+                          float eps, double* rs, double* red, const MegaArgs* tr = nullptr, uint32_t tl = 0) {
     constexpr int PER = 2;
     const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
     float v[MT][PER], gv[PER];
@@ -235,6 +315,8 @@ __device__ void load_norm(double* Xd, const float* x, bool from_smem, uint32_t K
 #pragma unroll
             for (int t = 0; t < MT; ++t) Xd[xd_index<BITS>(t, i, nchunk)] = (double)norm_value(v[t][k], rs[t], gv[k]);
     }
+    cbar();
+    stage_xsum<BITS, MT>(Xd, xsum, nchunk);
     cbar();
 }
 
@@ -376,6 +458,7 @@ __global__ void __launch_bounds__(kMThreads, 1) k_mega(const __grid_constant__ M
     __shared__ double rope_c[MT][kHeadDimMax / 2], rope_s[MT][kHeadDimMax / 2];  // this step's RoPE rows
     __shared__ HeadSmem hs;
     __shared__ uint32_t spos[MT];  // this step's positions
+    __shared__ double xsum[MT * kMaxChunks];  // chunk sums of the staged activations
     __shared__ __align__(16) MegaSlice sdesc[kMegaSlots];  // descriptors of the slices in the ring
     __shared__ volatile int s_fail;
     const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
@@ -533,9 +616,9 @@ __global__ void __launch_bounds__(kMThreads, 1) k_mega(const __grid_constant__ M
                     if (k >= o0 && k < o1) A.S.x[i] = v;
                 }
                 cbar();
-                if (work) load_norm<4, MT>(Xd, xs, true, H, gain, A.eps, rs, red);
+                if (work) load_norm<4, MT>(Xd, xsum, xs, true, H, gain, A.eps, rs, red);
             } else if (work) {
-                load_norm<4, MT>(Xd, A.S.x, false, H, gain, A.eps, rs, red, &A, l);
+                load_norm<4, MT>(Xd, xsum, A.S.x, false, H, gain, A.eps, rs, red, &A, l);
             }
             stamp_a(A, l, 0);
             // q|k|v units: ranges of 4 rows, (i0..i0+3) then (+half), a warp per row
@@ -543,7 +626,7 @@ __global__ void __launch_bounds__(kMThreads, 1) k_mega(const __grid_constant__ M
             for (uint32_t w = warp; w < nrows; w += kMWarps) {
                 const MegaRange& Rr = D.range[w / 4];
                 double acc[MT];
-                row_dot<4, MT>(slot, Rr, Rr.r0 + w % 4, H, XD, H / 32, 0, H / 32, lane, acc);
+                row_dot<4, MT>(slot, Rr, Rr.r0 + w % 4, H, XD, xsum, H / 32, 0, H / 32, lane, acc);
                 if (lane == 0)
 #pragma unroll
                     for (int t = 0; t < MT; ++t) res[w * MT + t] = acc[t];
@@ -666,14 +749,14 @@ __global__ void __launch_bounds__(kMThreads, 1) k_mega(const __grid_constant__ M
         {
             const MegaSlice& D = sdesc[slice % NS];
             const uint8_t* slot = slot_ptr();
-            load_norm<4, MT>(Xd, xs, true, H, reinterpret_cast<const float*>(slot + D.off_v), A.eps, rs, red);
+            load_norm<4, MT>(Xd, xsum, xs, true, H, reinterpret_cast<const float*>(slot + D.off_v), A.eps, rs, red);
             if (D.nrange) {
                 const MegaRange& Rg = D.range[0];
                 const MegaRange& Ru = D.range[1];
                 const uint32_t nr = Rg.r1 - Rg.r0;
                 for (uint32_t i = warp; i < nr; i += kMWarps) {  // gate row i with up row i
                     double acc[2][MT];
-                    row_dot2<4, MT>(slot, Rg, Rg.r0 + i, Ru, Ru.r0 + i, H, XD, H / 32, lane, acc);
+                    row_dot2<4, MT>(slot, Rg, Rg.r0 + i, Ru, Ru.r0 + i, H, XD, xsum, H / 32, lane, acc);
                     if (lane == 0)
 #pragma unroll
                         for (int t = 0; t < MT; ++t) {
@@ -711,6 +794,8 @@ __global__ void __launch_bounds__(kMThreads, 1) k_mega(const __grid_constant__ M
                         if (i < I) Xd[xd_index<4>(t, i, nchunk)] = (double)v[k];
                     }
                 }
+            cbar();
+            stage_xsum<4, MT>(Xd, xsum, nchunk);
         }
         if (!wait_slice()) return;
         stamp(A, 3 * (kMegaStages * l + 2) + 1);
@@ -725,7 +810,7 @@ __global__ void __launch_bounds__(kMThreads, 1) k_mega(const __grid_constant__ M
                     const uint32_t i = w / parts, p = w % parts;
                     const uint32_t c0 = nchunk * p / parts, c1 = nchunk * (p + 1) / parts;
                     double acc[MT];
-                    row_dot<4, MT>(slot, Rr, Rr.r0 + i, I, XD, nchunk, c0, c1, lane, acc);
+                    row_dot<4, MT>(slot, Rr, Rr.r0 + i, I, XD, xsum, nchunk, c0, c1, lane, acc);
                     if (lane == 0)
 #pragma unroll
                         for (int t = 0; t < MT; ++t) res[w * MT + t] = acc[t];
@@ -748,54 +833,69 @@ __global__ void __launch_bounds__(kMThreads, 1) k_mega(const __grid_constant__ M
     stamp(A, 3 * (kMegaStages * A.layers));
     const uint32_t nchunk = H / Geom<HB>::E;
     bool first = true;
+    unsigned long long tw = 0, tc = 0, tmark = 0;  // CTA 0 thread 0: time waiting / computing (trace)
+    auto now = []() { unsigned long long t; asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t)); return t; };
+    if (A.trace && c == 0 && tid == 0) tmark = now();
     while (slice < total) {
         if (!wait_slice()) return;
+        if (A.trace && c == 0 && tid == 0) { const unsigned long long t = now(); tw += t - tmark; tmark = t; }
         const MegaSlice& D = sdesc[slice % NS];
         const uint8_t* slot = slot_ptr();
         if (first) {  // the first head slice carries the final-norm gain
             const float* gain = reinterpret_cast<const float*>(slot + D.off_v);
-            load_norm<HB, MT>(Xd, A.S.x, false, H, gain, A.eps, rs, red);
+            load_norm<HB, MT>(Xd, xsum, A.S.x, false, H, gain, A.eps, rs, red);
             if (c == 0)
                 for (uint32_t i = tid; i < MT * H; i += kMConsumers)
                     A.S.normed[i] = norm_value(__ldcg(A.S.x + i), rs[i / H], gain[i % H]);
             first = false;
         }
         if (D.nrange) {
-            // a lane per row (rows at a padded stride), the chunks split over the warps, the
+            // a lane per row of the 32-row slice ([chunk][row] codes), the chunks split over the
+            // warps (every lane of a warp on the same activation chunk: broadcast reads), the
             // warps' partial sums added in a fixed order
             constexpr int CPB = Geom<HB>::CPB;
             const MegaRange& Rr = D.range[0];
-            const uint32_t nr = Rr.r1 - Rr.r0, bpr = H / kBlock, pstride = D.rows.dst_stride;
-            const uint32_t c0 = nchunk * warp / kMWarps, c1 = nchunk * (warp + 1) / kMWarps;
-            double* hpart = reinterpret_cast<double*>(kst);  // [warps][32 rows][MT]
+            const uint32_t nr = Rr.r1 - Rr.r0;
+            const uint32_t k0 = nchunk * warp / kMWarps, k1 = nchunk * (warp + 1) / kMWarps;
+            double* hpart = reinterpret_cast<double*>(kst);  // [32 rows][17 (16 warps + pad)][MT]
             if ((uint32_t)lane < nr) {
-                const uint32_t row = Rr.r0 + lane;
-                const uint8_t* prow = slot + Rr.off_p + (size_t)lane * pstride;
+                const uint4* P = reinterpret_cast<const uint4*>(slot + Rr.off_p);
                 const float* sc = reinterpret_cast<const float*>(slot + Rr.off_s);
-                const uint32_t* zw = reinterpret_cast<const uint32_t*>(slot + Rr.off_z);
+                const uint8_t* zb = slot + Rr.off_z;
                 double acc[1][MT];
 #pragma unroll
                 for (int t = 0; t < MT; ++t) acc[0][t] = 0.0;
-                for (uint32_t cc = c0; cc < c1; ++cc) {
-                    const uint4 q[1] = {*reinterpret_cast<const uint4*>(prow + cc * 16)};
-                    const uint32_t blk = row * bpr + cc / CPB;
-                    const float s[1] = {sc[blk - Rr.s_base]};
-                    const uint32_t zc[1] = {HB == 4 ? (zw[(blk >> 3) - Rr.z_base] >> ((blk & 7u) * 4u)) & 0xFu
-                                                    : (zw[(blk >> 2) - Rr.z_base] >> ((blk & 3u) * 8u)) & 0xFFu};
-                    chunk_dot<HB, MT, 1>(q, s, zc, XD, nchunk, cc, acc);
+                for (uint32_t cc = k0; cc < k1; ++cc) {
+                    const uint4 q[1] = {P[cc * kHeadSlice + lane]};
+                    const uint32_t b = cc / CPB;
+                    const float s[1] = {sc[b * kHeadSlice + lane]};
+                    const uint32_t zc[1] = {zb[b * kHeadSlice + lane]};
+                    chunk_dot_b<HB, MT, 1>(q, s, zc, XD, xsum, nchunk, cc, acc);
                 }
 #pragma unroll
-                for (int t = 0; t < MT; ++t) hpart[(warp * 32 + lane) * MT + t] = acc[0][t];
+                for (int t = 0; t < MT; ++t) hpart[(lane * 17 + warp) * MT + t] = acc[0][t];
             }
             cbar();
-            for (uint32_t e = tid; e < nr * MT; e += kMConsumers) {
-                const uint32_t i = e / MT, t = e % MT;
-                double v = 0.0;
-                for (int w = 0; w < kMWarps; ++w) v += hpart[(w * 32 + i) * MT + t];
-                A.S.logits[(size_t)t * A.vocab + Rr.r0 + i] = (float)v;
+            // 16 partials per row: thread (row i = tid / 16, warp part w = tid % 16), a 16-lane tree
+            {
+                const uint32_t i = tid >> 4, w = tid & 15;
+#pragma unroll
+                for (int t = 0; t < MT; ++t) {
+                    double v = i < nr ? hpart[(i * 17 + w) * MT + t] : 0.0;
+                    v += __shfl_xor_sync(0xffffffffu, v, 8);
+                    v += __shfl_xor_sync(0xffffffffu, v, 4);
+                    v += __shfl_xor_sync(0xffffffffu, v, 2);
+                    v += __shfl_xor_sync(0xffffffffu, v, 1);
+                    if (w == 0 && i < nr) A.S.logits[(size_t)t * A.vocab + Rr.r0 + i] = (float)v;
+                }
             }
         }
         release_slice();
+        if (A.trace && c == 0 && tid == 0) { const unsigned long long t = now(); tc += t - tmark; tmark = t; }
+    }
+    if (A.trace && c == 0 && tid == 0) {
+        A.trace[3 * (kMegaStages * A.layers + 1) + kADetail * A.layers] = tw;
+        A.trace[3 * (kMegaStages * A.layers + 1) + kADetail * A.layers + 1] = tc;
     }
     stamp(A, 3 * (kMegaStages * A.layers) + 2);
 }
@@ -814,6 +914,22 @@ __global__ void k_wo_heads(QW wo, uint32_t heads, uint32_t hd, uint32_t* P, floa
         for (uint32_t w = 0; w < hw; ++w) P[((size_t)h * H + r) * hw + w] = wo.packed[(size_t)r * wpr + h * hw + w];
     }
     Z[(size_t)h * (H / 8) + r0 / 8] = zword;
+}
+
+// Slice-major copy of the tied head (see mega_head_slices): a thread per (slice, chunk, row).
+__global__ void k_head_slices(QW head, int bits, uint32_t nslices, uint4* P, float* S, uint8_t* Z) {
+    const uint32_t H = head.cols, nchunk = H * bits / 128, bpr = H / kBlock;
+    const size_t idx = (size_t)blockIdx.x * blockDim.x + threadIdx.x;
+    if (idx >= (size_t)nslices * nchunk * kHeadSlice) return;
+    const uint32_t i = idx % kHeadSlice, cch = (idx / kHeadSlice) % nchunk, s = (uint32_t)(idx / ((size_t)kHeadSlice * nchunk));
+    const uint32_t row = s * kHeadSlice + i;
+    const bool live = row < head.rows;
+    P[idx] = live ? reinterpret_cast<const uint4*>(head.packed)[(size_t)row * nchunk + cch] : make_uint4(0, 0, 0, 0);
+    if (cch < bpr) {  // the block-th thread of the row also moves its scale and zero-point
+        const size_t o = ((size_t)s * bpr + cch) * kHeadSlice + i, blk = (size_t)row * bpr + cch;
+        S[o] = live ? head.scales[blk] : 0.f;
+        Z[o] = live ? (uint8_t)(bits == 4 ? zero_code<4>(head.zeros, (uint32_t)blk) : zero_code<8>(head.zeros, (uint32_t)blk)) : 0;
+    }
 }
 
 // ---------------------------------------------------------------------------------------------
@@ -839,6 +955,23 @@ cudaError_t mega_wo_heads(const QW& wo, uint32_t heads, uint32_t head_dim, uint8
     const uint32_t n = heads * (wo.rows / 8);
     k_wo_heads<<<(n + 255) / 256, 256, 0, st>>>(wo, heads, head_dim, P, S, Z);
     *view = QW{P, S, Z, (uint32_t)rows, head_dim};
+    return cudaGetLastError();
+}
+
+size_t mega_head_slices_bytes(uint32_t vocab, uint32_t hidden, int bits) {
+    const size_t ns = (vocab + kHeadSlice - 1) / kHeadSlice, rows = ns * kHeadSlice;
+    return align256(rows * hidden * bits / 8) + align256(rows * (hidden / kBlock) * 4) + align256(rows * (hidden / kBlock));
+}
+
+cudaError_t mega_head_slices(const QW& head, int bits, uint8_t* out, QW* view, cudaStream_t st) {
+    const uint32_t ns = (head.rows + kHeadSlice - 1) / kHeadSlice, rows = ns * kHeadSlice;
+    const uint32_t nchunk = head.cols * bits / 128, bpr = head.cols / kBlock;
+    uint4* P = reinterpret_cast<uint4*>(out);
+    float* S = reinterpret_cast<float*>(out + align256((size_t)rows * head.cols * bits / 8));
+    uint8_t* Z = out + align256((size_t)rows * head.cols * bits / 8) + align256((size_t)rows * bpr * 4);
+    const size_t n = (size_t)ns * nchunk * kHeadSlice;
+    k_head_slices<<<(unsigned)((n + 255) / 256), 256, 0, st>>>(head, bits, ns, P, S, Z);
+    *view = QW{reinterpret_cast<const uint32_t*>(P), S, reinterpret_cast<const uint32_t*>(Z), head.rows, head.cols};
     return cudaGetLastError();
 }
 
@@ -882,45 +1015,17 @@ static uint32_t plan_range(MegaSlice& S, const QW& w, int bits, uint32_t r0, uin
     return cursor;
 }
 
-// Head rows [r0, r1): packed codes one row per copy at a 16-byte-padded stride, then scales and
-// zero words as in plan_range.
-static void plan_head_rows(MegaSlice& S, const QW& w, int bits, uint32_t r0, uint32_t r1, uint32_t cursor) {
-    auto down16 = [](uint64_t v) { return v & ~uint64_t(15); };
-    auto up16l = [](uint64_t v) { return (v + 15) & ~uint64_t(15); };
-    MegaRange& R = S.range[S.nrange++];
-    R.r0 = r0;
-    R.r1 = r1;
-    const uint32_t row_bytes = w.cols * bits / 8, zpw = 32 / bits, bpr = w.cols / kBlock;
-    S.rows = MegaRows{(unsigned long long)(reinterpret_cast<const uint8_t*>(w.packed) + (size_t)r0 * row_bytes), r1 - r0,
-                      row_bytes, row_bytes, cursor, row_bytes + 16, 0};
-    S.bytes += (r1 - r0) * row_bytes;
-    R.off_p = cursor;
-    cursor = up16(cursor + (r1 - r0) * (row_bytes + 16));
-    const uint64_t sb = down16((uint64_t)r0 * bpr * 4), se = up16l((uint64_t)r1 * bpr * 4);
-    const uint64_t zb = down16(((uint64_t)r0 * bpr / zpw) * 4), ze = up16l((((uint64_t)r1 * bpr + zpw - 1) / zpw) * 4);
-    R.off_s = cursor;
-    R.s_base = (uint32_t)(sb / 4);
-    cursor = plan_copy(S, reinterpret_cast<const uint8_t*>(w.scales) + sb, (uint32_t)(se - sb), cursor);
-    R.off_z = cursor;
-    R.z_base = (uint32_t)(zb / 4);
-    plan_copy(S, reinterpret_cast<const uint8_t*>(w.zeros) + zb, (uint32_t)(ze - zb), cursor);
-}
-
 static uint32_t mega_att_reps(uint32_t mt, uint32_t heads, uint32_t grid) {
     const uint32_t r = grid / (mt * heads);
     return r > 4 ? 4 : (r < 1 ? 1 : r);
 }
 
-void mega_build_table(uint32_t mt, const MegaArgs& A, const QW* wo_heads, const MegaGeometry& g,
+void mega_build_table(uint32_t mt, const MegaArgs& A, const QW* wo_heads, const QW& head_slices, const MegaGeometry& g,
                       std::vector<MegaSlice>& table, std::vector<uint32_t>& counts, uint32_t& stride) {
     const uint32_t G = g.grid, L = A.layers, hd = A.head_dim, half = hd / 2, per_slot = half / 4;
     const uint32_t units = (A.heads + 2 * A.kv_heads) * per_slot, R = g.att_reps;
-    uint32_t max_head = 0;
-    for (uint32_t c = 0; c < G; ++c) {
-        const uint32_t h0 = split_lo(A.vocab, G, c, 1), h1 = split_lo(A.vocab, G, c + 1, 1);
-        const uint32_t n = (h1 - h0 + g.head_chunk - 1) / g.head_chunk;
-        max_head = n > max_head ? n : max_head;
-    }
+    const uint32_t nsl = (A.vocab + kHeadSlice - 1) / kHeadSlice;
+    const uint32_t max_head = (nsl + G - 1) / G;
     stride = 4 * L + (max_head ? max_head : 1);
     table.assign((size_t)G * stride, MegaSlice{});
     counts.assign(G, 0);
@@ -967,16 +1072,27 @@ void mega_build_table(uint32_t mt, const MegaArgs& A, const QW* wo_heads, const 
                 ++i;
             }
         }
-        const uint32_t h0 = split_lo(A.vocab, G, c, 1), h1 = split_lo(A.vocab, G, c + 1, 1);
+        const uint32_t s0 = split_lo(nsl, G, c, 1), s1 = split_lo(nsl, G, c + 1, 1);
         {  // the first head slice carries the final-norm gain (even when this CTA has no rows)
             MegaSlice& S = T[i];
             S.off_v = 0;
             plan_copy(S, A.final_norm, A.hidden * 4, 0);
         }
         uint32_t j = 0;
-        for (uint32_t r0 = h0; r0 < h1; r0 += g.head_chunk, ++j) {
-            const uint32_t r1 = r0 + g.head_chunk < h1 ? r0 + g.head_chunk : h1;
-            plan_head_rows(T[i + j], A.head, A.head_bits, r0, r1, j == 0 ? up16(A.hidden * 4) : 0);
+        const uint32_t nchunk = A.hidden * A.head_bits / 128, bpr = A.hidden / kBlock;
+        for (uint32_t sl = s0; sl < s1; ++sl, ++j) {  // 32-row slices of the slice-major head copy
+            MegaSlice& S = T[i + j];
+            MegaRange& R = S.range[S.nrange++];
+            R.r0 = sl * kHeadSlice;
+            R.r1 = R.r0 + kHeadSlice < A.vocab ? R.r0 + kHeadSlice : A.vocab;
+            uint32_t cur = j == 0 ? up16(A.hidden * 4) : 0;
+            R.off_p = cur;
+            cur = plan_copy(S, reinterpret_cast<const uint8_t*>(head_slices.packed) + (size_t)sl * nchunk * kHeadSlice * 16,
+                            nchunk * kHeadSlice * 16, cur);
+            R.off_s = cur;
+            cur = plan_copy(S, head_slices.scales + (size_t)sl * bpr * kHeadSlice, bpr * kHeadSlice * 4, cur);
+            R.off_z = cur;
+            plan_copy(S, reinterpret_cast<const uint8_t*>(head_slices.zeros) + (size_t)sl * bpr * kHeadSlice, bpr * kHeadSlice, cur);
         }
         counts[c] = i + (j ? j : 1);
     }
@@ -1022,13 +1138,13 @@ MegaGeometry mega_geometry(uint32_t mt, const MegaArgs& A) {
     uint32_t slot = gain + 2 * range_bytes(rows4, A.hidden, 4, bprH);
     const uint32_t cand[4] = {range_bytes(rows5, A.intermediate, 4, bprI), gain + upc * 2 * range_bytes(4, A.hidden, 4, bprH),
                               range_bytes(orows, A.head_dim, 4, 1),
-                              gain + range_bytes(g.head_chunk, A.hidden, (uint32_t)A.head_bits, bprH) + 16 * g.head_chunk};
+                              gain + range_bytes(g.head_chunk, A.hidden, (uint32_t)A.head_bits, bprH)};
     for (uint32_t v : cand) slot = v > slot ? v : slot;
     slot = (slot + 127) & ~127u;
     g.slot_bytes = slot;
     const size_t fixed = 256 + (size_t)mt * x4 * 8 + (((size_t)mt * A.hidden * 4 + 15) & ~size_t(15)) + (size_t)kKvHalfs * 2;
     const size_t statics = sizeof(double) * (mt + mt * kMWarps + kMaxRes * mt + mt * kHeadDimMax) + sizeof(HeadSmem) +
-                           sizeof(MegaSlice) * kMegaSlots + 64;
+                           sizeof(MegaSlice) * kMegaSlots + sizeof(double) * mt * kMaxChunks + 64;
     const int64_t room = (int64_t)maxsm - (int64_t)fixed - (int64_t)statics - 1024;
     int ns = room > 0 ? (int)(room / slot) : 0;
     if (ns > (int)kMegaSlots) ns = kMegaSlots;
@@ -1036,7 +1152,7 @@ MegaGeometry mega_geometry(uint32_t mt, const MegaArgs& A) {
     g.smem = fixed + (size_t)g.nslots * slot;
     g.max_positions = mt * x4;  // scores of one head, as doubles, in the activation area
     // shapes the kernel's fixed per-CTA capacities cannot take: report no ring (not eligible)
-    if (upc > 2 || 2 * rows4 > (uint32_t)kMaxRes || rows5 > (uint32_t)kMaxRes || mt * A.heads > g.grid ||
+    if (upc > 2 || A.intermediate / 32 > (uint32_t)kMaxChunks || A.hidden / 16 > (uint32_t)kMaxChunks || 2 * rows4 > (uint32_t)kMaxRes || rows5 > (uint32_t)kMaxRes || mt * A.heads > g.grid ||
         (A.head_dim != 32 && A.head_dim != 64) || A.hidden % 64 != 0 || A.intermediate % 64 != 0 ||
         A.hidden > 2 * (uint32_t)kMConsumers || A.kv_heads == 0 || A.heads % A.kv_heads != 0 ||
         A.kv_heads * (size_t)mt > 2 * (kMegaBarWords - 8))

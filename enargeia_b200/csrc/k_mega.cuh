@@ -74,7 +74,7 @@ struct MegaGeometry {
 MegaGeometry mega_geometry(uint32_t mt, const MegaArgs& A);
 // The per-CTA slice table for `mt` tokens (host side): table[c * stride + i], counts[c].
 // wo_heads[l] is layer l's o-projection re-laid out head-major (mega_wo_heads).
-void mega_build_table(uint32_t mt, const MegaArgs& A, const QW* wo_heads, const MegaGeometry& g,
+void mega_build_table(uint32_t mt, const MegaArgs& A, const QW* wo_heads, const QW& head_slices, const MegaGeometry& g,
                       std::vector<MegaSlice>& table, std::vector<uint32_t>& counts, uint32_t& stride);
 // Bytes of one layer's head-major o-projection copy, and the kernel that writes it: head h's
 // columns [h*hd, (h+1)*hd) of every row, as rows h*hidden + r of a (heads*hidden) x hd tensor
@@ -82,6 +82,13 @@ void mega_build_table(uint32_t mt, const MegaArgs& A, const QW* wo_heads, const 
 size_t mega_wo_heads_bytes(uint32_t hidden, uint32_t heads, uint32_t head_dim);
 cudaError_t mega_wo_heads(const QW& wo, uint32_t heads, uint32_t head_dim, uint8_t* out, QW* view,
                           cudaStream_t st);
+// Bytes of the tied head re-laid out in slices of 32 rows, and the kernel that writes it: slice
+// s holds, chunk-major, the 16-byte code chunks of its 32 rows ([chunk][row]), then its scales
+// ([block][row] floats) and zero-points ([block][row] bytes).  A lane per row then reads its
+// codes free of bank conflicts while every lane reads the same activation chunk.
+constexpr uint32_t kHeadSlice = 32;
+size_t mega_head_slices_bytes(uint32_t vocab, uint32_t hidden, int bits);
+cudaError_t mega_head_slices(const QW& head, int bits, uint8_t* out, QW* view, cudaStream_t st);
 cudaError_t launch_mega(uint32_t mt, const MegaArgs& A, const MegaGeometry& g, cudaStream_t st);
 
 }  // namespace enx
