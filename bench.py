@@ -227,30 +227,26 @@ def run_enx(args, rank, world, local_rank):
     e2e_value = world * args.steps / (e2e_ms / 1e3)
     consistent = api_ids == loop_ids
 
-    # --- roofline: the tied int8 head, the largest kernel of the step ------------------------
-    tv = m.tensor_view("model.embed_tokens.weight")
-    x = torch.randn(cfg.hidden, device=dev)
-    logits = torch.empty(cfg.vocab, device=dev)
-    flush = torch.empty(256 << 20, dtype=torch.uint8, device=dev)  # 256 MB > 126 MB L2
-    import ctypes as C
+    # --- roofline: the persistent decode kernel (the step's dominant kernel) ------------------
+    # One decode step at position PROMPT + 1, then the kernel alone, `reps` times back to back on
+    # the context stream (enx_launch_step_kernel: no sampler, no host copies), timed with events
+    # on that stream.  Each launch streams every weight once (351 MB > 126 MB L2).
+    restart_tok = restart()
+    Session(m, GREEDY).decode_step(restart_tok)
+    torch.cuda.synchronize()
+    from enargeia_b200._lib import call
 
-    from enargeia_b200._lib import EmbeddingDims, call
-
-    d = EmbeddingDims(1, cfg.hidden, 0, cfg.vocab, 64, cfg.hidden // 64, 0, 0, 0, 0, 0, 0)
-    head_ms = []
-    cur = torch.cuda.current_stream()
-    for i in range(args.warmup + 20):
-        flush.zero_()
-        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-        e0.record(cur)
-        call("enx_lm_head_q8", C.c_void_p(x.data_ptr()), C.c_void_p(tv["packed"]), C.c_void_p(tv["scales"]),
-             C.c_void_p(tv["zeros"]), C.c_void_p(logits.data_ptr()), C.byref(d), C.c_void_p(cur.cuda_stream))
-        e1.record(cur)
-        torch.cuda.synchronize()
-        if i >= args.warmup:
-            head_ms.append(e0.elapsed_time(e1))
-    head_algo = head_bytes + cfg.hidden * 4 + cfg.vocab * 4
-    head_avg = sum(head_ms) / len(head_ms)
+    reps = 50
+    call("enx_launch_step_kernel", m.handle, 1, 3)  # warm
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record(stream)
+    call("enx_launch_step_kernel", m.handle, 1, reps)
+    e1.record(stream)
+    torch.cuda.synchronize()
+    kern_us = e0.elapsed_time(e1) / reps * 1e3
+    kv_positions = PROMPT + 2  # positions attended by the step at position PROMPT + 1
+    kern_bytes = weight_bytes + cfg.layers * 2 * kv_positions * cfg.kv_dim * 2
     peaks = {}
     try:
         peaks = json.loads((ROOT / "MEASURED_PEAKS.json").read_text())
@@ -258,14 +254,14 @@ def run_enx(args, rank, world, local_rank):
         pass
     hbm = float(peaks.get("hbm_gbs", 6650.0))
     peak_src = "measured" if "hbm_gbs" in peaks else "fallback"
-    achieved = head_algo / (head_avg / 1e3) / 1e9
+    achieved = kern_bytes / (kern_us / 1e6) / 1e9
     step_bytes = weight_bytes  # plus KV reads, added below at the mean position
     mean_pos = PROMPT + GEN / 2
     kv_bytes = cfg.layers * 2 * int(mean_pos) * cfg.kv_dim * 2
     step_achieved = (step_bytes + kv_bytes) / (ms_total / args.steps / 1e3) / 1e9
 
     traffic = None
-    tf = ROOT / "profiles" / "lm_head_q8_traffic.json"
+    tf = ROOT / "profiles" / "k_mega_decode_traffic.json"
     if tf.exists():
         traffic = json.loads(tf.read_text()).get("dram_bytes_per_launch")
 
@@ -289,10 +285,10 @@ def run_enx(args, rank, world, local_rank):
                    "step_bytes": step_bytes + kv_bytes},
         "e2e": {"value": round(e2e_value, 2), "unit": "tok/s", "h2d_bytes_per_step": 116, "d2h_bytes_per_step": 4,
                 "api": "Session.decode_step -> enx_decode_step (pinned step block in, 4-byte id out)"},
-        "roofline": {"kernel": "k_head<8,1> (final RMSNorm + tied int8 LM head, 151936x896)", "bound": "hbm",
-                     "achieved": round(achieved, 1), "peak": hbm, "unit": "GB/s",
+        "roofline": {"kernel": "k_mega<1,8> (persistent decode step: 24 layers + tied int8 head, batch 1)",
+                     "bound": "hbm", "achieved": round(achieved, 1), "peak": hbm, "unit": "GB/s",
                      "frac": round(achieved / hbm, 4), "traffic": traffic,
-                     "algorithmic_bytes_per_launch": head_algo, "launch_us": round(head_avg * 1e3, 2),
+                     "algorithmic_bytes_per_launch": kern_bytes, "launch_us": round(kern_us, 2),
                      "peak_source": f"{peak_src} MEASURED_PEAKS.json hbm_gbs (burst copy)"},
         "step_roofline": {"bound": "hbm", "bytes_per_step": step_bytes + kv_bytes,
                           "achieved": round(step_achieved, 1), "peak": hbm, "unit": "GB/s",

@@ -828,9 +828,10 @@ extern "C" enx_status enx_sample_prefill(enx_ctx* c, uint32_t seq, const enx_sam
     return ENX_OK;
 }
 
-// The persistent step kernel runs when it fits: 1, 2 or 4 tokens, attention scores for every
-// cached position fit its shared-memory area (it recomputes attention in every CTA), and
-// ENX_DECODE_PATH is not "kernels".  Otherwise the five-launches-per-layer path runs.
+// The persistent step kernel runs when it fits: its ring gets at least two slots in shared memory
+// for this many tokens (in practice 1 or 2 for config 0), the scores of every cached position fit
+// its activation area, the shape is within its fixed capacities (mega_geometry), and
+// ENX_DECODE_PATH is not "kernels".  Otherwise the six-launches-per-layer path runs.
 static bool mega_eligible(enx_ctx* c, uint32_t B, const StepArgs& S, MegaArgs& A, MegaGeometry& geo) {
     const char* env = std::getenv("ENX_DECODE_PATH");
     if (env && std::string(env) == "kernels") return false;
@@ -1174,5 +1175,22 @@ extern "C" enx_status enx_stream(enx_ctx* c, void** stream) {
 extern "C" enx_status enx_step_launches(enx_ctx* c, uint32_t* launches) {
     CHECK_ARG(c && launches, "enx_step_launches: null pointer");
     *launches = c->last_launches;
+    return ENX_OK;
+}
+
+extern "C" enx_status enx_launch_step_kernel(enx_ctx* c, uint32_t batch, uint32_t count) {
+    CHECK_ARG(c, "enx_launch_step_kernel: null context");
+    if (batch == 0 || batch > kMaxStepBatch || !c->d_step || !(c->graph_mega[batch] || c->loop_mega[batch]))
+        return fail(ENX_ERR_STATE, "enx_launch_step_kernel: no decode step of this batch ran on the persistent kernel");
+    DeviceGuard g(c->device);
+    StepArgs S = step_args(c);
+    S.pos = c->d_step->pos;
+    MegaArgs A;
+    MegaGeometry geo{};
+    if (!mega_eligible(c, batch, S, A, geo)) return fail(ENX_ERR_STATE, "enx_launch_step_kernel: not eligible");
+    for (uint32_t i = 0; i < count; ++i) {
+        ENX_CUDA(cudaMemsetAsync(c->d_bar, 0, kMegaBarWords * sizeof(unsigned long long), c->stream));
+        ENX_CUDA(launch_mega(batch, A, geo, c->stream));
+    }
     return ENX_OK;
 }

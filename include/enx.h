@@ -273,10 +273,11 @@ ENX_API enx_status enx_tensor_view(enx_ctx* ctx, const char* name, int32_t* dtyp
 /* Stage telemetry (Session.setInstrumented + the per-kernel timestamp queries of
  * src/runtime/session.ts:162-308).  With tracing on, the persistent decode kernel stamps the
  * device clock (ns) three times per stage: when the stage starts (its barrier released), when its
- * weights have landed in shared memory, and when its compute is done; stages are 4 per layer
- * (qkv, attention+o, gate/up, down) then the head.  enx_trace copies the stamps of the last step
- * (3 * (4*layers + 1) values; unused slots are 0).  Turning tracing on or off re-captures the
- * decode graphs on the next step. */
+ * weights have landed in shared memory, and when its compute is done; stages are 3 per layer
+ * (q|k|v + attention + o partial, gate/up, down) then the head.  After those 3 * (3*layers + 1)
+ * values come 8 per layer inside the attention stage and 2 head totals (waiting, computing), all
+ * of the first CTA.  enx_trace copies the stamps of the last step (unused slots are 0).  Turning
+ * tracing on or off re-captures the decode graphs on the next step. */
 ENX_API enx_status enx_set_tracing(enx_ctx* ctx, int on);
 ENX_API enx_status enx_trace(enx_ctx* ctx, uint64_t* out, uint32_t capacity, uint32_t* count);
 
@@ -285,6 +286,12 @@ ENX_API enx_status enx_stream(enx_ctx* ctx, void** stream);
 
 /* Kernel launches issued by the last enx_decode_step (the captured step's node count). */
 ENX_API enx_status enx_step_launches(enx_ctx* ctx, uint32_t* launches);
+
+/* Measurement hook: enqueue on the context stream, `count` times, the persistent decode kernel
+ * alone (with its barrier reset) for the `batch` tokens and positions of the last decode step,
+ * without the sampler or any host copy.  Re-running a step rewrites the same cache rows and
+ * logits.  ENX_ERR_STATE if no step ran yet or the step did not use the persistent kernel. */
+ENX_API enx_status enx_launch_step_kernel(enx_ctx* ctx, uint32_t batch, uint32_t count);
 
 #ifdef __cplusplus
 }
