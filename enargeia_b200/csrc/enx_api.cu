@@ -298,7 +298,7 @@ struct enx_ctx {
     std::vector<uint32_t> filled;
     // decode step buffers
     float *x = nullptr, *q = nullptr, *gated = nullptr, *logits = nullptr, *normed = nullptr,
-          *scores = nullptr, *attn_out = nullptr;
+          *scores = nullptr, *attn_out = nullptr, *x_mid = nullptr;
     StepBlock* d_step = nullptr;
     StepBlock* h_step = nullptr;
     cudaGraphExec_t graph[kMaxStepBatch + 1] = {};
@@ -320,11 +320,8 @@ struct enx_ctx {
     MegaSlice* d_table[kMaxStepBatch + 1] = {};
     uint32_t* d_nslices[kMaxStepBatch + 1] = {};
     uint32_t table_stride[kMaxStepBatch + 1] = {};
-    uint8_t* d_wo_heads = nullptr;
-    std::vector<QW> wo_heads;
     uint8_t* d_head_slices = nullptr;
     QW head_slices{};
-    double* d_opart = nullptr;
     uint32_t last_launches = 0;
     // prefill buffers (chunk-sized)
     uint32_t pf_chunk = 0;
@@ -377,10 +374,7 @@ void free_graphs(enx_ctx* c) {
         dfree(c->d_nslices[b]);
         c->table_stride[b] = 0;
     }
-    dfree(c->d_wo_heads);
-    dfree(c->d_opart);
     dfree(c->d_head_slices);
-    c->wo_heads.clear();
 }
 
 void free_prefill(enx_ctx* c) {
@@ -394,7 +388,7 @@ void free_kv(enx_ctx* c) {
     free_graphs(c);
     free_prefill(c);
     dfree(c->kcache); dfree(c->vcache); dfree(c->rope_cos); dfree(c->rope_sin); dfree(c->history);
-    dfree(c->x); dfree(c->q); dfree(c->gated); dfree(c->logits); dfree(c->normed); dfree(c->scores); dfree(c->attn_out);
+    dfree(c->x); dfree(c->q); dfree(c->gated); dfree(c->logits); dfree(c->normed); dfree(c->scores); dfree(c->attn_out); dfree(c->x_mid);
     dfree(c->d_step);
     if (c->h_step) cudaFreeHost(c->h_step);
     c->h_step = nullptr;
@@ -665,6 +659,7 @@ extern "C" enx_status enx_kv_alloc(enx_ctx* c, uint32_t max_context, uint32_t ba
     ENX_TRY(dalloc(&c->normed, (size_t)batch * C.hidden, "normed"));
     ENX_TRY(dalloc(&c->scores, (size_t)B * splits_for(max_context) * kAttnChunk * C.heads, "attention scores"));
     ENX_TRY(dalloc(&c->attn_out, (size_t)B * C.hidden, "attention output"));
+    ENX_TRY(dalloc(&c->x_mid, (size_t)B * C.hidden, "residual after attention"));
     ENX_TRY(dalloc(&c->d_step, 1, "step block"));
     if (cudaMallocHost(&c->h_step, sizeof(StepBlock)) != cudaSuccess) return fail(ENX_ERR_NOMEM, "pinned step block");
     std::memset(c->h_step, 0, sizeof(StepBlock));
@@ -856,6 +851,8 @@ static bool mega_eligible(enx_ctx* c, uint32_t B, const StepArgs& S, MegaArgs& A
     A.tokens = c->d_step->tokens;
     A.bar = c->d_bar;
     A.ready = reinterpret_cast<uint32_t*>(c->d_bar + 8);
+    A.done = A.ready + 64;
+    A.x_mid = c->x_mid;
     A.err = &c->d_step->err;
     A.trace = c->d_trace;
     geo = mega_geometry(B, A);
@@ -863,28 +860,11 @@ static bool mega_eligible(enx_ctx* c, uint32_t B, const StepArgs& S, MegaArgs& A
     A.nslots = geo.nslots;
     A.slot_bytes = geo.slot_bytes;
     A.x4_floats = geo.x4_floats;
-    A.att_reps = geo.att_reps;
-    if (!c->d_wo_heads) {
-        // head-major copy of every o-projection and the per-head partial sums (built once)
-        const size_t per = mega_wo_heads_bytes(C.hidden, C.heads, C.head_dim);
-        if (dalloc(&c->d_wo_heads, per * C.layers, "o-projection by head") != ENX_OK ||
-            dalloc(&c->d_opart, (size_t)kMaxStepBatch * C.heads * C.hidden, "o partials") != ENX_OK) {
-            dfree(c->d_wo_heads);
-            dfree(c->d_opart);
-            return false;
-        }
-        c->wo_heads.assign(C.layers, QW{});
-        for (uint32_t l = 0; l < C.layers; ++l)
-            if (mega_wo_heads(c->layers[l].wo, C.heads, C.head_dim, c->d_wo_heads + per * l, &c->wo_heads[l], c->stream) !=
-                cudaSuccess) {
-                dfree(c->d_wo_heads);
-                return false;
-            }
+    if (!c->d_head_slices) {  // slice-major copy of the tied head (built once)
         const size_t hb = mega_head_slices_bytes(C.vocab, C.hidden, c->head.bits);
         if (dalloc(&c->d_head_slices, hb, "head by slices") != ENX_OK ||
             mega_head_slices(c->head.embed, c->head.bits, c->d_head_slices, &c->head_slices, c->stream) != cudaSuccess ||
             cudaStreamSynchronize(c->stream) != cudaSuccess) {
-            dfree(c->d_wo_heads);
             dfree(c->d_head_slices);
             return false;
         }
@@ -893,7 +873,7 @@ static bool mega_eligible(enx_ctx* c, uint32_t B, const StepArgs& S, MegaArgs& A
         std::vector<MegaSlice> table;
         std::vector<uint32_t> counts;
         uint32_t stride = 0;
-        mega_build_table(B, A, c->wo_heads.data(), c->head_slices, geo, table, counts, stride);
+        mega_build_table(B, A, c->head_slices, geo, table, counts, stride);
         if (dalloc(&c->d_table[B], table.size(), "mega table") != ENX_OK ||
             dalloc(&c->d_nslices[B], counts.size(), "mega counts") != ENX_OK ||
             cudaMemcpy(c->d_table[B], table.data(), table.size() * sizeof(MegaSlice), cudaMemcpyHostToDevice) != cudaSuccess ||
@@ -904,7 +884,6 @@ static bool mega_eligible(enx_ctx* c, uint32_t B, const StepArgs& S, MegaArgs& A
         }
         c->table_stride[B] = stride;
     }
-    A.opart = c->d_opart;
     A.table = c->d_table[B];
     A.nslices = c->d_nslices[B];
     A.table_stride = c->table_stride[B];

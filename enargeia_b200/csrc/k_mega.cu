@@ -11,18 +11,17 @@
 // A grid barrier costs ~1.9 us on this part (measured), so each layer has three of them:
 //   A  every CTA: RMSNorm(x) -> its units of q|k|v rows (4 RoPE pairs each) + bias + RoPE; q to
 //      global, k/v into the f16 cache; then it bumps the ready counter of the unit's kv head.
-//      Attention CTAs, att_reps per (token, query head), wait (bounded) for their kv head's
-//      counter instead of a grid barrier, run attention over the cached positions (history
-//      prefetched with cp.async at the start of the stage) and the o-projection restricted to
-//      this head's columns for their share of the rows, in double, into opart[t][h][:].
-//   C  every CTA: x += float(sum over heads of opart) (fixed head order, all rows, kept in
-//      shared memory) -> RMSNorm -> its gate|up rows -> SiLU(gate)*up into `gated`
-//   D  every CTA: its down-projection rows + residual (from shared memory) into x
+//      One attention CTA per (token, query head) waits (bounded) for its kv head's counter
+//      instead of a grid barrier, runs attention over the cached positions (history prefetched
+//      with cp.async at the start of the stage), writes its head's output and bumps the token's
+//      done counter.  Every CTA then waits for the done counters and computes its rows of the
+//      o-projection + residual into x_mid (a second buffer: a CTA still reading x for its norm
+//      must not see it change).
+//   C  every CTA: RMSNorm(x) -> its gate|up rows -> SiLU(gate)*up into `gated`
+//   D  every CTA: its down-projection rows + residual into x (the rows it also owns in A)
 // then the final RMSNorm and this CTA's slice of the tied head rows, streamed in chunks.  Norm
 // gains and q|k|v biases travel in the slices with the weights.
-// Arithmetic is the faithful double-sum, float-store scheme of k_matvec.cuh.  Splitting the
-// o-projection sum by head and adding the per-head doubles in a fixed order only reorders f64
-// additions before the single rounding to float.
+// Arithmetic is the faithful double-sum, float-store scheme of k_matvec.cuh.
 //
 // Grid barriers are a monotonic 64-bit arrival counter (zeroed by a memset node before each
 // launch).  Every wait is bounded and reports through `err` instead of hanging; the producer
@@ -279,7 +278,8 @@ __device__ __forceinline__ void row_dot2(const uint8_t* slot, const MegaRange& R
 // outputs as doubles.  K <= 2 * kMConsumers.
 template <int BITS, int MT>
 __device__ void load_norm(double* Xd, double* xsum, const float* x, bool from_smem, uint32_t K, const float* gain,
-                          float eps, double* rs, double* red, const MegaArgs* tr = nullptr, uint32_t tl = 0) {
+                          float eps, double* rs, double* red, float* keep = nullptr, const MegaArgs* tr = nullptr,
+                          uint32_t tl = 0) {
     constexpr int PER = 2;
     const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
     float v[MT][PER], gv[PER];
@@ -290,6 +290,12 @@ __device__ void load_norm(double* Xd, double* xsum, const float* x, bool from_sm
 #pragma unroll
         for (int t = 0; t < MT; ++t) v[t][k] = i < K ? (from_smem ? x[t * K + i] : __ldcg(x + t * K + i)) : 0.f;
     }
+    if (keep)  // a copy of the raw rows (the residual) in shared memory
+#pragma unroll
+        for (int k = 0; k < PER; ++k)
+#pragma unroll
+            for (int t = 0; t < MT; ++t)
+                if (tid + k * kMConsumers < K) keep[t * K + tid + k * kMConsumers] = v[t][k];
 #pragma unroll
     for (int t = 0; t < MT; ++t) {
         double ss = 0.0;
@@ -479,10 +485,9 @@ __global__ void __launch_bounds__(kMThreads, 1) k_mega(const __grid_constant__ M
 
     const MegaSlice* T = A.table + (size_t)c * A.table_stride;
     const uint32_t total = A.nslices[c];
-    // attention role: (token, head, replica) for the first MT * heads * att_reps CTAs
-    const uint32_t R = A.att_reps;
-    const bool att = c < MT * A.heads * R;
-    const uint32_t at = att ? c / (A.heads * R) : 0, ah = att ? (c / R) % A.heads : 0, arep = att ? c % R : 0;
+    // attention role: (token, query head) for the first MT * heads CTAs
+    const bool att = c < MT * A.heads;
+    const uint32_t at = att ? c / A.heads : 0, ah = att ? c % A.heads : 0;
     const uint32_t ag = ah / group;
     const uint32_t units_per_group = (group + 2) * (hd / 8);
 
@@ -600,10 +605,8 @@ __global__ void __launch_bounds__(kMThreads, 1) k_mega(const __grid_constant__ M
             const MegaSlice& D = sdesc[slice % NS];
             const uint8_t* slot = slot_ptr();
             const float* gain = reinterpret_cast<const float*>(slot + D.off_v);
-            const bool work = D.nrange != 0;  // CTAs without q|k|v units skip the norm
             if (l == 0) {
-                // embedding rows of the tied table; this CTA also starts its share of the residual
-                const uint32_t o0 = (uint32_t)(((uint64_t)H * c) / gridDim.x), o1 = (uint32_t)(((uint64_t)H * (c + 1)) / gridDim.x);
+                // embedding rows of the tied table (every CTA: the residual of its o rows)
                 const uint32_t bpr = H / kBlock;
                 for (uint32_t i = tid; i < MT * H; i += kMConsumers) {
                     const uint32_t t = i / H, k = i % H, row = A.tokens[t];
@@ -613,12 +616,11 @@ __global__ void __launch_bounds__(kMThreads, 1) k_mega(const __grid_constant__ M
                     const uint32_t blk = row * bpr + k / kBlock;
                     const float v = ((float)q - (float)zero_code<HB>(A.head.zeros, blk)) * A.head.scales[blk];
                     xs[i] = v;
-                    if (k >= o0 && k < o1) A.S.x[i] = v;
                 }
                 cbar();
-                if (work) load_norm<4, MT>(Xd, xsum, xs, true, H, gain, A.eps, rs, red);
-            } else if (work) {
-                load_norm<4, MT>(Xd, xsum, A.S.x, false, H, gain, A.eps, rs, red, &A, l);
+                load_norm<4, MT>(Xd, xsum, xs, true, H, gain, A.eps, rs, red);
+            } else {
+                load_norm<4, MT>(Xd, xsum, A.S.x, false, H, gain, A.eps, rs, red, xs, &A, l);
             }
             stamp_a(A, l, 0);
             // q|k|v units: ranges of 4 rows, (i0..i0+3) then (+half), a warp per row
@@ -699,57 +701,72 @@ __global__ void __launch_bounds__(kMThreads, 1) k_mega(const __grid_constant__ M
             cbar();
             stamp_a(A, l, 3);
             attend(A, l, at, ag, apos, Xd, kst, vst, cap, hs);
+            for (uint32_t d = tid; d < hd; d += kMConsumers) A.S.attn_out[(size_t)at * H + ah * hd + d] = (float)hs.ad[d];
+            cbar();
+            if (tid == 0) asm volatile("red.release.gpu.global.add.u32 [%0], 1;" ::"l"(A.done + at) : "memory");
             stamp_a(A, l, 4);
-            // this head's share of the o-projection for rows [R.r0, R.r1) of the head-major copy
-            if (!wait_slice()) return;
-            stamp_a(A, l, 5);
-            {
-                const MegaRange& Rr = sdesc[slice % NS].range[0];
-                const uint8_t* slot = slot_ptr();
-                const uint32_t cpr = hd / 32;  // 32-element chunks per row of the head slice
-                const uint4* P = reinterpret_cast<const uint4*>(slot + Rr.off_p);
-                const float* sc = reinterpret_cast<const float*>(slot + Rr.off_s);
-                const uint32_t* zw = reinterpret_cast<const uint32_t*>(slot + Rr.off_z);
-                double* out = A.opart + ((size_t)at * A.heads + ah) * H;
-                for (uint32_t row = Rr.r0 + tid; row < Rr.r1; row += kMConsumers) {
-                    const double zd = magic_d((zw[(row >> 3) - Rr.z_base] >> ((row & 7u) * 4u)) & 0xFu);
-                    const double s = (double)sc[row - Rr.s_base];
-                    double acc = 0.0;
-                    for (uint32_t cc = 0; cc < cpr; ++cc) {
-                        const uint4 q = P[(size_t)(row - Rr.r0) * cpr + cc];
-                        const uint32_t w4[4] = {q.x, q.y, q.z, q.w};
-                        double p0 = 0.0, p1 = 0.0;
-#pragma unroll
-                        for (int e = 0; e < 32; e += 2) {
-                            const uint32_t wd = w4[e >> 3];
-                            p0 = fma(magic_d((wd >> ((e & 7) * 4)) & 0xFu) - zd, hs.ad[cc * 32 + e], p0);
-                            p1 = fma(magic_d((wd >> (((e + 1) & 7) * 4)) & 0xFu) - zd, hs.ad[cc * 32 + e + 1], p1);
-                        }
-                        acc = fma(p0 + p1, s, acc);
+        }
+        // every CTA: wait for all heads' attention (bounded), then its rows of the o-projection
+        if (tid == 0) {
+            const uint32_t target = A.heads * (l + 1);
+            for (uint32_t t = 0; t < MT && !s_fail; ++t)
+                for (uint32_t it = 0;; ++it) {
+                    uint32_t v;
+                    asm volatile("ld.acquire.gpu.global.u32 %0, [%1];" : "=r"(v) : "l"(A.done + t) : "memory");
+                    if (v >= target) break;
+                    if (it > kSpinLimit) {
+                        atomicMax(A.err, 1u);
+                        s_fail = 1;
+                        break;
                     }
-                    out[row - ah * H] = acc;
+                }
+        }
+        cbar();
+        if (s_fail) return;
+        stamp_a(A, l, 5);
+        for (uint32_t t = 0; t < MT; ++t)
+            for (uint32_t k = tid; k < H; k += kMConsumers) Xd[xd_index<4>(t, k, H / 32)] = (double)__ldcg(A.S.attn_out + t * H + k);
+        cbar();
+        stage_xsum<4, MT>(Xd, xsum, H / 32);
+        if (!wait_slice()) return;
+        {
+            const MegaSlice& D = sdesc[slice % NS];
+            if (D.nrange) {
+                const MegaRange& Rr = D.range[0];
+                const uint8_t* slot = slot_ptr();
+                const uint32_t nr = Rr.r1 - Rr.r0, nchunk = H / 32;
+                const uint32_t parts = nr >= (uint32_t)kMWarps ? 1 : kMWarps / nr;  // split K across warps
+                for (uint32_t w = warp; w < nr * parts; w += kMWarps) {
+                    const uint32_t i = w / parts, p = w % parts;
+                    const uint32_t c0 = nchunk * p / parts, c1 = nchunk * (p + 1) / parts;
+                    double acc[MT];
+                    row_dot<4, MT>(slot, Rr, Rr.r0 + i, H, XD, xsum, nchunk, c0, c1, lane, acc);
+                    if (lane == 0)
+#pragma unroll
+                        for (int t = 0; t < MT; ++t) res[w * MT + t] = acc[t];
+                }
+                cbar();
+                for (uint32_t e = tid; e < nr * MT; e += kMConsumers) {
+                    const uint32_t i = e / MT, t = e % MT;
+                    double v = 0.0;
+                    for (uint32_t p = 0; p < parts; ++p) v += res[(i * parts + p) * MT + t];  // fixed order
+                    A.x_mid[(size_t)t * H + Rr.r0 + i] = xs[(size_t)t * H + Rr.r0 + i] + (float)v;
                 }
             }
-            release_slice();
         }
+        release_slice();
+        stamp_a(A, l, 6);
         stamp(A, 3 * (kMegaStages * l + 0) + 2);
         if (!grid_sync(A, bar_index, &s_fail)) return;
 
         // ---------------- C: residual + RMSNorm + gate|up + SiLU ----------------------------
         stamp(A, 3 * (kMegaStages * l + 1));
-        for (uint32_t t = 0; t < MT; ++t)
-            for (uint32_t r = tid; r < H; r += kMConsumers) {
-                const double* p = A.opart + (size_t)t * A.heads * H + r;
-                double o = 0.0;
-                for (uint32_t h = 0; h < A.heads; ++h) o += __ldcg(p + (size_t)h * H);  // fixed head order
-                xs[t * H + r] = __ldcg(A.S.x + t * H + r) + (float)o;
-            }
         if (!wait_slice()) return;
         stamp(A, 3 * (kMegaStages * l + 1) + 1);
         {
             const MegaSlice& D = sdesc[slice % NS];
             const uint8_t* slot = slot_ptr();
-            load_norm<4, MT>(Xd, xsum, xs, true, H, reinterpret_cast<const float*>(slot + D.off_v), A.eps, rs, red);
+            load_norm<4, MT>(Xd, xsum, A.x_mid, false, H, reinterpret_cast<const float*>(slot + D.off_v), A.eps, rs, red, xs);
             if (D.nrange) {
                 const MegaRange& Rg = D.range[0];
                 const MegaRange& Ru = D.range[1];
@@ -900,22 +917,6 @@ __global__ void __launch_bounds__(kMThreads, 1) k_mega(const __grid_constant__ M
     stamp(A, 3 * (kMegaStages * A.layers) + 2);
 }
 
-// Head-major copy of an o-projection (see mega_wo_heads): a thread per (head, 8 rows).
-__global__ void k_wo_heads(QW wo, uint32_t heads, uint32_t hd, uint32_t* P, float* S, uint32_t* Z) {
-    const uint32_t H = wo.rows, wpr = wo.cols / 8, hw = hd / 8, bpr = wo.cols / kBlock;
-    const uint32_t idx = blockIdx.x * blockDim.x + threadIdx.x;
-    if (idx >= heads * (H / 8)) return;
-    const uint32_t h = idx / (H / 8), r0 = (idx % (H / 8)) * 8;
-    uint32_t zword = 0;
-    for (uint32_t k = 0; k < 8; ++k) {
-        const uint32_t r = r0 + k, blk = r * bpr + (h * hd) / kBlock;
-        S[(size_t)h * H + r] = wo.scales[blk];
-        zword |= zero_code<4>(wo.zeros, blk) << (4 * k);
-        for (uint32_t w = 0; w < hw; ++w) P[((size_t)h * H + r) * hw + w] = wo.packed[(size_t)r * wpr + h * hw + w];
-    }
-    Z[(size_t)h * (H / 8) + r0 / 8] = zword;
-}
-
 // Slice-major copy of the tied head (see mega_head_slices): a thread per (slice, chunk, row).
 __global__ void k_head_slices(QW head, int bits, uint32_t nslices, uint4* P, float* S, uint8_t* Z) {
     const uint32_t H = head.cols, nchunk = H * bits / 128, bpr = H / kBlock;
@@ -941,22 +942,6 @@ static uint32_t split_lo(uint32_t total, uint32_t parts, uint32_t i, uint32_t gr
 }
 
 static size_t align256(size_t v) { return (v + 255) & ~size_t(255); }
-
-size_t mega_wo_heads_bytes(uint32_t hidden, uint32_t heads, uint32_t head_dim) {
-    const size_t rows = (size_t)heads * hidden;
-    return align256(rows * head_dim / 2) + align256(rows * 4) + align256(rows / 2);
-}
-
-cudaError_t mega_wo_heads(const QW& wo, uint32_t heads, uint32_t head_dim, uint8_t* out, QW* view, cudaStream_t st) {
-    const size_t rows = (size_t)heads * wo.rows;
-    uint32_t* P = reinterpret_cast<uint32_t*>(out);
-    float* S = reinterpret_cast<float*>(out + align256(rows * head_dim / 2));
-    uint32_t* Z = reinterpret_cast<uint32_t*>(out + align256(rows * head_dim / 2) + align256(rows * 4));
-    const uint32_t n = heads * (wo.rows / 8);
-    k_wo_heads<<<(n + 255) / 256, 256, 0, st>>>(wo, heads, head_dim, P, S, Z);
-    *view = QW{P, S, Z, (uint32_t)rows, head_dim};
-    return cudaGetLastError();
-}
 
 size_t mega_head_slices_bytes(uint32_t vocab, uint32_t hidden, int bits) {
     const size_t ns = (vocab + kHeadSlice - 1) / kHeadSlice, rows = ns * kHeadSlice;
@@ -1015,15 +1000,10 @@ static uint32_t plan_range(MegaSlice& S, const QW& w, int bits, uint32_t r0, uin
     return cursor;
 }
 
-static uint32_t mega_att_reps(uint32_t mt, uint32_t heads, uint32_t grid) {
-    const uint32_t r = grid / (mt * heads);
-    return r > 4 ? 4 : (r < 1 ? 1 : r);
-}
-
-void mega_build_table(uint32_t mt, const MegaArgs& A, const QW* wo_heads, const QW& head_slices, const MegaGeometry& g,
+void mega_build_table(uint32_t mt, const MegaArgs& A, const QW& head_slices, const MegaGeometry& g,
                       std::vector<MegaSlice>& table, std::vector<uint32_t>& counts, uint32_t& stride) {
     const uint32_t G = g.grid, L = A.layers, hd = A.head_dim, half = hd / 2, per_slot = half / 4;
-    const uint32_t units = (A.heads + 2 * A.kv_heads) * per_slot, R = g.att_reps;
+    const uint32_t units = (A.heads + 2 * A.kv_heads) * per_slot;
     const uint32_t nsl = (A.vocab + kHeadSlice - 1) / kHeadSlice;
     const uint32_t max_head = (nsl + G - 1) / G;
     stride = 4 * L + (max_head ? max_head : 1);
@@ -1051,10 +1031,10 @@ void mega_build_table(uint32_t mt, const MegaArgs& A, const QW* wo_heads, const 
                     cur = plan_range(S, *w, 4, b + half, b + half + 4, kind, cur, 0, bias);
                 }
             }
-            if (c < mt * A.heads * R) {  // attention CTA: its rows of the head's o-projection columns
-                const uint32_t h = (c / R) % A.heads, rep = c % R;
-                const uint32_t r0 = split_lo(A.hidden, R, rep, 8), r1 = split_lo(A.hidden, R, rep + 1, 8);
-                plan_range(T[i++], wo_heads[l], 4, h * A.hidden + r0, h * A.hidden + r1, 3, 0, 1);
+            {  // this CTA's rows of the o-projection (the rows it owns in D too)
+                const uint32_t r0 = split_lo(A.hidden, G, c, 2), r1 = split_lo(A.hidden, G, c + 1, 2);
+                if (r1 > r0) plan_range(T[i], La.wo, 4, r0, r1, 0, 0);
+                ++i;
             }
             {
                 MegaSlice& S = T[i++];
@@ -1123,7 +1103,6 @@ MegaGeometry mega_geometry(uint32_t mt, const MegaArgs& A) {
     cudaDeviceGetAttribute(&maxsm, cudaDevAttrMaxSharedMemoryPerBlockOptin, dev);
     g.grid = (uint32_t)sms;
     g.head_chunk = 32;
-    g.att_reps = mega_att_reps(mt, A.heads, g.grid);
     const uint32_t x4 = A.intermediate > A.hidden ? A.intermediate : A.hidden;
     g.x4_floats = x4;
     auto range_bytes = [](uint32_t rows, uint32_t cols, uint32_t bits, uint32_t bpr) {
@@ -1132,12 +1111,11 @@ MegaGeometry mega_geometry(uint32_t mt, const MegaArgs& A) {
     const uint32_t bprH = A.hidden / 64, bprI = A.intermediate / 64, gain = A.hidden * 4 + 16;
     const uint32_t rows4 = (A.intermediate + g.grid - 1) / g.grid + 1;
     const uint32_t rows5 = ((A.hidden / 2 + g.grid - 1) / g.grid) * 2 + 2;
-    const uint32_t orows = (A.hidden + g.att_reps - 1) / g.att_reps + 8;
     const uint32_t units = (A.heads + 2 * A.kv_heads) * (A.head_dim / 8);
     const uint32_t upc = (units + g.grid - 1) / g.grid;  // q|k|v units per CTA
     uint32_t slot = gain + 2 * range_bytes(rows4, A.hidden, 4, bprH);
     const uint32_t cand[4] = {range_bytes(rows5, A.intermediate, 4, bprI), gain + upc * 2 * range_bytes(4, A.hidden, 4, bprH),
-                              range_bytes(orows, A.head_dim, 4, 1),
+                              range_bytes(rows5, A.hidden, 4, bprH),
                               gain + range_bytes(g.head_chunk, A.hidden, (uint32_t)A.head_bits, bprH)};
     for (uint32_t v : cand) slot = v > slot ? v : slot;
     slot = (slot + 127) & ~127u;
@@ -1155,7 +1133,7 @@ MegaGeometry mega_geometry(uint32_t mt, const MegaArgs& A) {
     if (upc > 2 || A.intermediate / 32 > (uint32_t)kMaxChunks || A.hidden / 16 > (uint32_t)kMaxChunks || 2 * rows4 > (uint32_t)kMaxRes || rows5 > (uint32_t)kMaxRes || mt * A.heads > g.grid ||
         (A.head_dim != 32 && A.head_dim != 64) || A.hidden % 64 != 0 || A.intermediate % 64 != 0 ||
         A.hidden > 2 * (uint32_t)kMConsumers || A.kv_heads == 0 || A.heads % A.kv_heads != 0 ||
-        A.kv_heads * (size_t)mt > 2 * (kMegaBarWords - 8))
+        A.kv_heads * (size_t)mt > 64)
         g.nslots = 0;
     return g;
 }

@@ -53,10 +53,10 @@ struct MegaArgs {
     const float* final_norm;
     StepArgs S;                   // activations, caches, RoPE table, positions
     const uint32_t* tokens;       // [MT] ids fed this step (device)
-    double* opart;                // [MT][heads][hidden] o-projection partial sums per head
     unsigned long long* bar;      // grid-barrier arrival counter, zeroed before each launch
     uint32_t* ready;              // [MT][kv_heads] q|k|v units done (monotonic over layers), zeroed too
-    uint32_t att_reps;            // attention CTAs per (token, head): each does a share of the o rows
+    uint32_t* done;               // [MT] attention heads done (monotonic over layers), zeroed too
+    float* x_mid;                 // [MT][hidden] residual after attention (x stays readable meanwhile)
     uint32_t* err;                // sticky error: 1 barrier timeout, 2 copy timeout
     const MegaSlice* table;       // [grid][table_stride] slices, built on the host
     const uint32_t* nslices;      // [grid] slices per CTA
@@ -66,22 +66,16 @@ struct MegaArgs {
 };
 
 struct MegaGeometry {
-    uint32_t grid, nslots, slot_bytes, x4_floats, max_positions, head_chunk, att_reps;
+    uint32_t grid, nslots, slot_bytes, x4_floats, max_positions, head_chunk;
     size_t smem;
 };
 
 // Grid, ring and shared-memory geometry for `mt` tokens; nslots < 2 means the shape is not supported.
 MegaGeometry mega_geometry(uint32_t mt, const MegaArgs& A);
 // The per-CTA slice table for `mt` tokens (host side): table[c * stride + i], counts[c].
-// wo_heads[l] is layer l's o-projection re-laid out head-major (mega_wo_heads).
-void mega_build_table(uint32_t mt, const MegaArgs& A, const QW* wo_heads, const QW& head_slices, const MegaGeometry& g,
+// head_slices is the slice-major copy of the tied head (mega_head_slices).
+void mega_build_table(uint32_t mt, const MegaArgs& A, const QW& head_slices, const MegaGeometry& g,
                       std::vector<MegaSlice>& table, std::vector<uint32_t>& counts, uint32_t& stride);
-// Bytes of one layer's head-major o-projection copy, and the kernel that writes it: head h's
-// columns [h*hd, (h+1)*hd) of every row, as rows h*hidden + r of a (heads*hidden) x hd tensor
-// with one scale and one zero-point per row.
-size_t mega_wo_heads_bytes(uint32_t hidden, uint32_t heads, uint32_t head_dim);
-cudaError_t mega_wo_heads(const QW& wo, uint32_t heads, uint32_t head_dim, uint8_t* out, QW* view,
-                          cudaStream_t st);
 // Bytes of the tied head re-laid out in slices of 32 rows, and the kernel that writes it: slice
 // s holds, chunk-major, the 16-byte code chunks of its 32 rows ([chunk][row]), then its scales
 // ([block][row] floats) and zero-points ([block][row] bytes).  A lane per row then reads its

@@ -200,10 +200,10 @@ class Model:
         out["head"] = t[3 * L, 2] - t[3 * L, 0]
         out["total"] = t[3 * L, 2] - t[0, 0]
         # inside the attention stage (first CTA): weights + norm, q|k|v units, wait for the kv
-        # head's units, q and current k/v loads, attention, o weights wait, o partial, (unused)
+        # head's units, q and current k/v loads, attention, wait for every head, o rows
         d = buf[3 * (3 * L + 1):3 * (3 * L + 1) + 8 * L].astype(np.float64).reshape(L, 8) / 1e3
         if d.any():
-            marks = ["norm", "units", "ready_wait", "q_load", "attention", "o_wait", "o_partial+end"]
+            marks = ["norm", "units", "ready_wait", "q_load", "attention", "done_wait", "o_rows+end"]
             d = d[:, :6]
             starts = t[0:3 * L:3, 0]
             ends = t[0:3 * L:3, 2]
