@@ -10,10 +10,12 @@
 #include <map>
 #include <memory>
 #include <string>
+#include <mutex>
 #include <vector>
 
 #include "enx_internal.cuh"
 #include "k_decode.cuh"
+#include "k_gemm_tc.cuh"
 #include "k_mega.cuh"
 #include "k_small.cuh"
 #include "json_lite.h"
@@ -52,6 +54,40 @@ extern "C" const char* enx_version(void) { return "enx 0.1 sm_100a"; }
 // ---------------------------------------------------------------------------------------------
 // raw kernels
 
+// Tensor-core GEMMs (M >= kTcMinTokens) need a workspace for the activation limbs.  The raw entry
+// points keep one per device, grown on demand (a call that grows it synchronises the device through
+// cudaMalloc), with a device error word that a bounded wait raises.
+constexpr uint32_t kTcMinTokens = 16;
+static std::mutex g_tc_mu;
+struct TcWorkspace {
+    uint8_t* ptr = nullptr;
+    size_t bytes = 0;
+    uint32_t* err = nullptr;
+};
+static std::vector<TcWorkspace> g_tc_ws;
+
+static enx_status tc_workspace(size_t bytes, uint8_t** ws, uint32_t** err) {
+    int dev = 0;
+    ENX_CUDA(cudaGetDevice(&dev));
+    std::lock_guard<std::mutex> lock(g_tc_mu);
+    if ((size_t)dev >= g_tc_ws.size()) g_tc_ws.resize((size_t)dev + 1);
+    TcWorkspace& W = g_tc_ws[dev];
+    if (!W.err) {
+        ENX_CUDA(cudaMalloc(&W.err, sizeof(uint32_t)));
+        ENX_CUDA(cudaMemset(W.err, 0, sizeof(uint32_t)));
+    }
+    if (W.bytes < bytes) {
+        if (W.ptr) cudaFree(W.ptr);
+        W.ptr = nullptr;
+        W.bytes = 0;
+        ENX_CUDA(cudaMalloc(&W.ptr, bytes));
+        W.bytes = bytes;
+    }
+    *ws = W.ptr;
+    *err = W.err;
+    return ENX_OK;
+}
+
 extern "C" enx_status enx_matmul_q4(const float* x, const uint32_t* packed, const float* scales,
                                     const uint32_t* zeros, const float* bias, float* out,
                                     const enx_matmul_q4_dims* d, void* stream) {
@@ -62,6 +98,14 @@ extern "C" enx_status enx_matmul_q4(const float* x, const uint32_t* packed, cons
     CHECK_ARG(!d->use_bias || bias, "enx_matmul_q4: use_bias set without a bias");
     if (d->m == 0 || d->n == 0) return ENX_OK;
     QW w{packed, scales, zeros, d->n, d->k};
+    if (d->m >= kTcMinTokens) {  // tensor cores (exact limb GEMM), library-owned workspace
+        uint8_t* ws = nullptr;
+        uint32_t* err = nullptr;
+        ENX_TRY(tc_workspace(gemm_tc_workspace_bytes(d->m, d->k), &ws, &err));
+        ENX_CUDA(launch_gemm_tc(4, x, d->k, w, d->use_bias ? bias : nullptr, out, d->m, d->out_stride, d->out_offset, ws,
+                                err, as_stream(stream)));
+        return ENX_OK;
+    }
     ENX_CUDA(launch_matmul(4, x, w, d->use_bias ? bias : nullptr, out, d->m, d->out_stride, d->out_offset,
                            as_stream(stream), false));
     return ENX_OK;
@@ -328,6 +372,7 @@ struct enx_ctx {
     float *pf_x = nullptr, *pf_n = nullptr, *pf_q = nullptr, *pf_q2 = nullptr, *pf_k = nullptr,
           *pf_k2 = nullptr, *pf_v = nullptr, *pf_att = nullptr, *pf_t = nullptr, *pf_g = nullptr,
           *pf_u = nullptr, *pf_part = nullptr;
+    uint8_t* pf_ws = nullptr;  // tensor-core GEMM workspace (activation limbs) for prefill chunks
     uint32_t* pf_ids = nullptr;
 };
 
@@ -381,6 +426,7 @@ void free_prefill(enx_ctx* c) {
     dfree(c->pf_x); dfree(c->pf_n); dfree(c->pf_q); dfree(c->pf_q2); dfree(c->pf_k); dfree(c->pf_k2);
     dfree(c->pf_v); dfree(c->pf_att); dfree(c->pf_t); dfree(c->pf_g); dfree(c->pf_u); dfree(c->pf_part);
     dfree(c->pf_ids);
+    dfree(c->pf_ws);
     c->pf_chunk = 0;
 }
 
@@ -722,6 +768,14 @@ static StepArgs step_args(enx_ctx* c) {
     return S;
 }
 
+// A projection of m prefill rows: tensor cores for m >= kTcMinTokens, CUDA cores below.
+static cudaError_t proj(enx_ctx* c, int bits, const float* x, const QW& w, const float* bias, float* out, uint32_t m,
+                        uint32_t stride, uint32_t offset, cudaStream_t st) {
+    if (m >= kTcMinTokens && c->pf_ws)
+        return launch_gemm_tc(bits, x, w.cols, w, bias, out, m, stride, offset, c->pf_ws, &c->d_step->err, st);
+    return launch_matmul(bits, x, w, bias, out, m, stride, offset, st, false);
+}
+
 static enx_status ensure_prefill(enx_ctx* c, uint32_t chunk) {
     if (c->pf_chunk >= chunk) return ENX_OK;
     free_prefill(c);
@@ -740,6 +794,8 @@ static enx_status ensure_prefill(enx_ctx* c, uint32_t chunk) {
     ENX_TRY(dalloc(&c->pf_u, chunk * I, "prefill up"));
     ENX_TRY(dalloc(&c->pf_part, (size_t)chunk * splits_for(c->max_ctx) * kAttnChunk * C.heads, "prefill scores"));
     ENX_TRY(dalloc(&c->pf_ids, chunk, "prefill ids"));
+    if (chunk >= kTcMinTokens)
+        ENX_TRY(dalloc(&c->pf_ws, gemm_tc_workspace_bytes(chunk, (uint32_t)(I > H ? I : H)), "prefill GEMM workspace"));
     c->pf_chunk = chunk;
     return ENX_OK;
 }
@@ -777,21 +833,21 @@ extern "C" enx_status enx_prefill(enx_ctx* c, uint32_t seq, const uint32_t* ids,
         for (uint32_t l = 0; l < C.layers; ++l) {
             const LayerArgs& L = c->layers[l];
             ENX_CUDA(launch_rmsnorm(c->pf_x, L.norm_in, c->pf_n, m, H, C.rms_norm_eps, st));
-            ENX_CUDA(launch_matmul(4, c->pf_n, L.wq, L.bq, c->pf_q, m, H, 0, st, false));
-            ENX_CUDA(launch_matmul(4, c->pf_n, L.wk, L.bk, c->pf_k, m, kv, 0, st, false));
-            ENX_CUDA(launch_matmul(4, c->pf_n, L.wv, L.bv, c->pf_v, m, kv, 0, st, false));
+            ENX_CUDA(proj(c, 4, c->pf_n, L.wq, L.bq, c->pf_q, m, H, 0, st));
+            ENX_CUDA(proj(c, 4, c->pf_n, L.wk, L.bk, c->pf_k, m, kv, 0, st));
+            ENX_CUDA(proj(c, 4, c->pf_n, L.wv, L.bv, c->pf_v, m, kv, 0, st));
             ENX_CUDA(launch_rope_d(c->pf_q, c->pf_q2, c->rope_cos, c->rope_sin, m, C.heads, C.head_dim, begin, 0, st));
             ENX_CUDA(launch_rope_d(c->pf_k, c->pf_k2, c->rope_cos, c->rope_sin, m, C.kv_heads, C.head_dim, begin, 0, st));
             ENX_CUDA(launch_cache_pack(c->pf_k2, c->kcache + S.cache_offset(seq, l, begin), m * kv, 0, st));
             ENX_CUDA(launch_cache_pack(c->pf_v, c->vcache + S.cache_offset(seq, l, begin), m * kv, 0, st));
             ENX_CUDA(launch_attn(S, l, m, c->pf_att, st, false));
-            ENX_CUDA(launch_matmul(4, c->pf_att, L.wo, nullptr, c->pf_t, m, H, 0, st, false));
+            ENX_CUDA(proj(c, 4, c->pf_att, L.wo, nullptr, c->pf_t, m, H, 0, st));
             ENX_CUDA(launch_add(c->pf_x, c->pf_t, c->pf_x, m * H, st));
             ENX_CUDA(launch_rmsnorm(c->pf_x, L.norm_post, c->pf_n, m, H, C.rms_norm_eps, st));
-            ENX_CUDA(launch_matmul(4, c->pf_n, L.wg, nullptr, c->pf_g, m, I, 0, st, false));
-            ENX_CUDA(launch_matmul(4, c->pf_n, L.wu, nullptr, c->pf_u, m, I, 0, st, false));
+            ENX_CUDA(proj(c, 4, c->pf_n, L.wg, nullptr, c->pf_g, m, I, 0, st));
+            ENX_CUDA(proj(c, 4, c->pf_n, L.wu, nullptr, c->pf_u, m, I, 0, st));
             ENX_CUDA(launch_silu_mul(c->pf_g, c->pf_u, c->pf_g, m * I, st));
-            ENX_CUDA(launch_matmul(4, c->pf_g, L.wd, nullptr, c->pf_t, m, H, 0, st, false));
+            ENX_CUDA(proj(c, 4, c->pf_g, L.wd, nullptr, c->pf_t, m, H, 0, st));
             ENX_CUDA(launch_add(c->pf_x, c->pf_t, c->pf_x, m * H, st));
         }
         c->filled[seq] += m;
