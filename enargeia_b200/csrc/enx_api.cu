@@ -320,6 +320,51 @@ __global__ void k_loop_post(LoopState* L, const StepBlock* blk, uint32_t* ids, u
     if (b == 0) L->i = i + 1;
 }
 
+// Batched decode (more than kMaxStepBatch sequences per step): one block of u32 arrays for
+// `cap` sequences (cap a multiple of 4), offsets below; SampleRow entries are 4 words.
+struct BatchLayout {
+    uint32_t cap;
+    __host__ __device__ uint32_t tok() const { return 0; }
+    __host__ __device__ uint32_t pos() const { return cap; }
+    __host__ __device__ uint32_t hist() const { return 2 * cap; }
+    __host__ __device__ uint32_t rows() const { return 3 * cap; }
+    __host__ __device__ uint32_t out() const { return 7 * cap; }
+    __host__ __device__ uint32_t err() const { return 8 * cap; }
+    __host__ __device__ uint32_t step() const { return 8 * cap + 1; }
+    __host__ __device__ uint32_t base() const { return 8 * cap + 4; }
+    __host__ __device__ uint32_t first() const { return 9 * cap + 4; }
+    __host__ __device__ uint32_t params() const { return 10 * cap + 4; }
+    __host__ __device__ uint32_t words() const { return 14 * cap + 4; }
+};
+
+__global__ void k_batch_prep(uint32_t* blk, BatchLayout Lb, uint32_t* history, uint32_t max_ctx, uint32_t batch) {
+    for (uint32_t b = threadIdx.x; b < batch; b += blockDim.x)
+        history[(size_t)b * max_ctx + blk[Lb.pos() + b]] = blk[Lb.tok() + b];
+}
+
+__global__ void k_batch_loop_prep(uint32_t* blk, BatchLayout Lb, const float* randoms, const uint32_t* ids,
+                                  uint32_t* history, uint32_t max_ctx, uint32_t batch) {
+    const uint32_t i = blk[Lb.step()];
+    for (uint32_t b = threadIdx.x; b < batch; b += blockDim.x) {
+        const uint32_t tok = i == 0 ? blk[Lb.first() + b] : ids[(size_t)(i - 1) * batch + b];
+        const uint32_t pos = blk[Lb.base() + b] + i;
+        blk[Lb.tok() + b] = tok;
+        blk[Lb.pos() + b] = pos;
+        blk[Lb.hist() + b] = pos + 1;
+        SampleRow r = reinterpret_cast<const SampleRow*>(blk + Lb.params())[b];
+        r.random = randoms[(size_t)i * batch + b];
+        reinterpret_cast<SampleRow*>(blk + Lb.rows())[b] = r;
+        history[(size_t)b * max_ctx + pos] = tok;
+    }
+}
+
+__global__ void k_batch_loop_post(uint32_t* blk, BatchLayout Lb, uint32_t* ids, uint32_t batch) {
+    const uint32_t i = blk[Lb.step()];
+    for (uint32_t b = threadIdx.x; b < batch; b += blockDim.x) ids[(size_t)i * batch + b] = blk[Lb.out() + b];
+    __syncthreads();
+    if (threadIdx.x == 0) blk[Lb.step()] = i + 1;
+}
+
 }  // namespace
 
 struct enx_ctx {
@@ -373,6 +418,17 @@ struct enx_ctx {
           *pf_k2 = nullptr, *pf_v = nullptr, *pf_att = nullptr, *pf_t = nullptr, *pf_g = nullptr,
           *pf_u = nullptr, *pf_part = nullptr;
     uint8_t* pf_ws = nullptr;  // tensor-core GEMM workspace (activation limbs) for prefill chunks
+    // batched decode: more than kMaxStepBatch sequences per step (the tensor-core GEMM path)
+    BatchLayout bl{};
+    uint32_t* d_bb = nullptr;  // BatchLayout block
+    uint32_t* h_bb = nullptr;  // pinned mirror
+    float *b_x = nullptr, *b_xn = nullptr, *b_q = nullptr, *b_k = nullptr, *b_v = nullptr, *b_att = nullptr,
+          *b_t = nullptr, *b_g = nullptr, *b_u = nullptr, *b_scores = nullptr, *b_rand = nullptr;
+    uint32_t* b_ids = nullptr;
+    uint8_t* b_ws = nullptr;
+    std::map<uint32_t, cudaGraphExec_t> b_graph, b_loop_graph;
+    std::map<uint32_t, uint32_t> b_launches;
+    bool loop_batched = false;  // the last enx_decode_loop ran the batched path
     uint32_t* pf_ids = nullptr;
 };
 
@@ -414,6 +470,10 @@ void free_graphs(enx_ctx* c) {
         if (g) cudaGraphExecDestroy(g);
         g = nullptr;
     }
+    for (auto& kv : c->b_graph) cudaGraphExecDestroy(kv.second);
+    for (auto& kv : c->b_loop_graph) cudaGraphExecDestroy(kv.second);
+    c->b_graph.clear();
+    c->b_loop_graph.clear();
     for (uint32_t b = 0; b <= kMaxStepBatch; ++b) {
         dfree(c->d_table[b]);
         dfree(c->d_nslices[b]);
@@ -444,6 +504,11 @@ void free_kv(enx_ctx* c) {
     c->h_loop = nullptr;
     c->h_loop_ids = nullptr;
     c->loop_cap = c->loop_count = 0;
+    dfree(c->d_bb); dfree(c->b_x); dfree(c->b_xn); dfree(c->b_q); dfree(c->b_k); dfree(c->b_v); dfree(c->b_att);
+    dfree(c->b_t); dfree(c->b_g); dfree(c->b_u); dfree(c->b_scores); dfree(c->b_rand); dfree(c->b_ids); dfree(c->b_ws);
+    if (c->h_bb) cudaFreeHost(c->h_bb);
+    c->h_bb = nullptr;
+    c->bl = BatchLayout{};
     c->max_ctx = c->batch = 0;
     c->filled.clear();
 }
@@ -718,6 +783,27 @@ extern "C" enx_status enx_kv_alloc(enx_ctx* c, uint32_t max_context, uint32_t ba
     ENX_TRY(dalloc(&c->d_loop_ids, c->loop_cap, "loop ids"));
     if (cudaMallocHost(&c->h_loop, sizeof(LoopState)) != cudaSuccess) return fail(ENX_ERR_NOMEM, "pinned loop state");
     if (cudaMallocHost(&c->h_loop_ids, (size_t)c->loop_cap * 4) != cudaSuccess) return fail(ENX_ERR_NOMEM, "pinned loop ids");
+    if (batch > kMaxStepBatch) {  // batched decode buffers
+        const size_t Bn = batch, H = C.hidden, kvd = (size_t)C.kv_heads * C.head_dim, I = C.intermediate;
+        c->bl.cap = (batch + 3) & ~3u;
+        ENX_TRY(dalloc(&c->d_bb, c->bl.words(), "batch block"));
+        ENX_CUDA(cudaMemset(c->d_bb, 0, (size_t)c->bl.words() * 4));
+        if (cudaMallocHost(&c->h_bb, (size_t)c->bl.words() * 4) != cudaSuccess) return fail(ENX_ERR_NOMEM, "pinned batch block");
+        std::memset(c->h_bb, 0, (size_t)c->bl.words() * 4);
+        ENX_TRY(dalloc(&c->b_x, Bn * H, "batch x"));
+        ENX_TRY(dalloc(&c->b_xn, Bn * H, "batch normed"));
+        ENX_TRY(dalloc(&c->b_q, Bn * H, "batch q"));
+        ENX_TRY(dalloc(&c->b_k, Bn * kvd, "batch k"));
+        ENX_TRY(dalloc(&c->b_v, Bn * kvd, "batch v"));
+        ENX_TRY(dalloc(&c->b_att, Bn * H, "batch attention"));
+        ENX_TRY(dalloc(&c->b_t, Bn * H, "batch projection"));
+        ENX_TRY(dalloc(&c->b_g, Bn * I, "batch gate"));
+        ENX_TRY(dalloc(&c->b_u, Bn * I, "batch up"));
+        ENX_TRY(dalloc(&c->b_scores, Bn * splits_for(max_context) * kAttnChunk * C.heads, "batch scores"));
+        ENX_TRY(dalloc(&c->b_rand, Bn * max_context, "batch loop randoms"));
+        ENX_TRY(dalloc(&c->b_ids, Bn * max_context, "batch loop ids"));
+        ENX_TRY(dalloc(&c->b_ws, gemm_tc_workspace_bytes(batch, (uint32_t)(I > H ? I : H)), "batch GEMM workspace"));
+    }
     ENX_CUDA(cudaStreamSynchronize(c->stream));
     c->max_ctx = max_context;
     c->batch = batch;
@@ -946,6 +1032,171 @@ static bool mega_eligible(enx_ctx* c, uint32_t B, const StepArgs& S, MegaArgs& A
     return true;
 }
 
+// A projection of B batched tokens: tensor cores from kTcMinTokens tokens, CUDA cores below.
+static cudaError_t proj_b(enx_ctx* c, int bits, const float* x, const QW& w, const float* bias, float* out, uint32_t B,
+                          uint32_t stride, cudaStream_t st) {
+    if (B >= kTcMinTokens)
+        return launch_gemm_tc(bits, x, w.cols, w, bias, out, B, stride, 0, c->b_ws, c->d_bb + c->bl.err(), st);
+    return launch_matmul(bits, x, w, bias, out, B, stride, 0, st, false);
+}
+
+// One batched decode step of sequences 0..B-1 (each at its own position) as graph nodes: embed,
+// per layer RMSNorm, q|k|v projections, RoPE + cache rows, attention over each sequence's cache,
+// o projection + residual, RMSNorm, gate/up, SiLU, down + residual; final norm, tied head and the
+// batched sampler.  The reference runs each sequence through the same per-token step.
+static cudaError_t batch_body(enx_ctx* c, uint32_t B, cudaStream_t st) {
+    const enx_model_config& C = c->cfg;
+    const uint32_t H = C.hidden, kvd = C.kv_heads * C.head_dim, I = C.intermediate;
+    uint32_t* blk = c->d_bb;
+    StepArgs S = step_args(c);
+    S.q = c->b_q;
+    S.scores = c->b_scores;
+    S.pos = blk + c->bl.pos();
+    cudaError_t e = launch_embed(blk + c->bl.tok(), c->head.embed, c->head.bits, c->b_x, B, 0, C.vocab, H, st, false);
+    for (uint32_t l = 0; l < C.layers && e == cudaSuccess; ++l) {
+        const LayerArgs& L = c->layers[l];
+        e = launch_rmsnorm(c->b_x, L.norm_in, c->b_xn, B, H, C.rms_norm_eps, st);
+        if (e == cudaSuccess) e = proj_b(c, 4, c->b_xn, L.wq, L.bq, c->b_q, B, H, st);
+        if (e == cudaSuccess) e = proj_b(c, 4, c->b_xn, L.wk, L.bk, c->b_k, B, kvd, st);
+        if (e == cudaSuccess) e = proj_b(c, 4, c->b_xn, L.wv, L.bv, c->b_v, B, kvd, st);
+        if (e == cudaSuccess) e = launch_rope_cache_batch(S, l, c->b_q, c->b_k, c->b_v, B, st);
+        if (e == cudaSuccess) e = launch_attn(S, l, B, c->b_att, st, false);
+        if (e == cudaSuccess) e = proj_b(c, 4, c->b_att, L.wo, nullptr, c->b_t, B, H, st);
+        if (e == cudaSuccess) e = launch_add(c->b_x, c->b_t, c->b_x, B * H, st);
+        if (e == cudaSuccess) e = launch_rmsnorm(c->b_x, L.norm_post, c->b_xn, B, H, C.rms_norm_eps, st);
+        if (e == cudaSuccess) e = proj_b(c, 4, c->b_xn, L.wg, nullptr, c->b_g, B, I, st);
+        if (e == cudaSuccess) e = proj_b(c, 4, c->b_xn, L.wu, nullptr, c->b_u, B, I, st);
+        if (e == cudaSuccess) e = launch_silu_mul(c->b_g, c->b_u, c->b_g, B * I, st);
+        if (e == cudaSuccess) e = proj_b(c, 4, c->b_g, L.wd, nullptr, c->b_t, B, H, st);
+        if (e == cudaSuccess) e = launch_add(c->b_x, c->b_t, c->b_x, B * H, st);
+    }
+    if (e == cudaSuccess) e = launch_rmsnorm(c->b_x, c->head.norm, c->normed, B, H, C.rms_norm_eps, st);
+    if (e == cudaSuccess) e = proj_b(c, c->head.bits, c->normed, c->head.embed, nullptr, c->logits, B, C.vocab, st);
+    if (e == cudaSuccess)
+        e = launch_sample(c->logits, C.vocab, B, c->history, c->max_ctx, blk + c->bl.hist(),
+                          reinterpret_cast<const SampleRow*>(blk + c->bl.rows()), false, SampleRow{}, blk + c->bl.out(), st,
+                          false);
+    return e;
+}
+
+static enx_status capture_batch(enx_ctx* c, uint32_t B, bool loop) {
+    cudaStream_t st = c->stream;
+    const BatchLayout& Lb = c->bl;
+    ENX_CUDA(cudaStreamBeginCapture(st, cudaStreamCaptureModeThreadLocal));
+    cudaError_t e = cudaSuccess;
+    if (loop) {
+        k_batch_loop_prep<<<1, 256, 0, st>>>(c->d_bb, Lb, c->b_rand, c->b_ids, c->history, c->max_ctx, B);
+        e = cudaGetLastError();
+    } else {
+        // this step's inputs: B entries of each array (ids, positions, history lengths, sampling rows)
+        const uint32_t offs[3] = {Lb.tok(), Lb.pos(), Lb.hist()};
+        for (uint32_t k = 0; k < 3 && e == cudaSuccess; ++k)
+            e = cudaMemcpyAsync(c->d_bb + offs[k], c->h_bb + offs[k], (size_t)B * 4, cudaMemcpyHostToDevice, st);
+        if (e == cudaSuccess)
+            e = cudaMemcpyAsync(c->d_bb + Lb.rows(), c->h_bb + Lb.rows(), (size_t)B * 16, cudaMemcpyHostToDevice, st);
+        if (e == cudaSuccess) {
+            k_batch_prep<<<1, 256, 0, st>>>(c->d_bb, Lb, c->history, c->max_ctx, B);
+            e = cudaGetLastError();
+        }
+    }
+    if (e == cudaSuccess) e = batch_body(c, B, st);
+    if (e == cudaSuccess) {
+        if (loop) {
+            k_batch_loop_post<<<1, 256, 0, st>>>(c->d_bb, Lb, c->b_ids, B);
+            e = cudaGetLastError();
+        } else {
+            e = cudaMemcpyAsync(c->h_bb + Lb.out(), c->d_bb + Lb.out(), (size_t)B * 4, cudaMemcpyDeviceToHost, st);
+            if (e == cudaSuccess)
+                e = cudaMemcpyAsync(c->h_bb + Lb.err(), c->d_bb + Lb.err(), 4, cudaMemcpyDeviceToHost, st);
+        }
+    }
+    cudaGraph_t graph = nullptr;
+    cudaError_t e2 = cudaStreamEndCapture(st, &graph);
+    if (e == cudaSuccess) e = e2;
+    if (e != cudaSuccess) {
+        if (graph) cudaGraphDestroy(graph);
+        return cuda_fail(e, "capturing the batched decode step");
+    }
+    size_t nodes = 0;
+    cudaGraphGetNodes(graph, nullptr, &nodes);
+    cudaGraphExec_t exec = nullptr;
+    e = cudaGraphInstantiate(&exec, graph, 0);
+    cudaGraphDestroy(graph);
+    if (e != cudaSuccess) return cuda_fail(e, "instantiating the batched decode step");
+    (loop ? c->b_loop_graph : c->b_graph)[B] = exec;
+    c->b_launches[B] = (uint32_t)nodes;
+    return ENX_OK;
+}
+
+static enx_status batch_error(enx_ctx* c, uint32_t code) {
+    c->h_bb[c->bl.err()] = 0;
+    cudaMemsetAsync(c->d_bb + c->bl.err(), 0, 4, c->stream);
+    return fail(ENX_ERR_TIMEOUT, "batched decode: a bounded device wait gave up (code " + std::to_string(code) + ")");
+}
+
+// enx_decode_step for more than kMaxStepBatch sequences.
+static enx_status decode_batch(enx_ctx* c, uint32_t B, const uint32_t* tokens, const enx_sampling* params,
+                               uint32_t params_count, const float* randoms, uint32_t* out_ids) {
+    if (!c->d_bb) return fail(ENX_ERR_STATE, "batched decode: enx_kv_alloc with more than 4 sequences first");
+    auto it = c->b_graph.find(B);
+    if (it == c->b_graph.end()) {
+        ENX_TRY(capture_batch(c, B, false));
+        it = c->b_graph.find(B);
+    }
+    uint32_t* h = c->h_bb;
+    const BatchLayout& Lb = c->bl;
+    for (uint32_t b = 0; b < B; ++b) {
+        const enx_sampling& p = params[params_count == 1 ? 0 : b];
+        h[Lb.tok() + b] = tokens[b];
+        h[Lb.pos() + b] = c->filled[b];
+        h[Lb.hist() + b] = c->filled[b] + 1;
+        reinterpret_cast<SampleRow*>(h + Lb.rows())[b] = SampleRow{p.temperature, p.top_p, p.repetition_penalty, randoms[b]};
+    }
+    ENX_CUDA(cudaGraphLaunch(it->second, c->stream));
+    ENX_CUDA(cudaStreamSynchronize(c->stream));
+    if (h[Lb.err()]) return batch_error(c, h[Lb.err()]);
+    for (uint32_t b = 0; b < B; ++b) {
+        out_ids[b] = h[Lb.out() + b];
+        c->filled[b] += 1;
+    }
+    c->last_launches = c->b_launches[B];
+    return ENX_OK;
+}
+
+// enx_decode_loop for more than kMaxStepBatch sequences.
+static enx_status decode_batch_loop(enx_ctx* c, uint32_t B, const uint32_t* first, const enx_sampling* params,
+                                    uint32_t params_count, uint32_t steps, const float* randoms, uint32_t* out_ids,
+                                    int sync) {
+    if (!c->d_bb) return fail(ENX_ERR_STATE, "batched decode: enx_kv_alloc with more than 4 sequences first");
+    auto it = c->b_loop_graph.find(B);
+    if (it == c->b_loop_graph.end()) {
+        ENX_TRY(capture_batch(c, B, true));
+        it = c->b_loop_graph.find(B);
+    }
+    uint32_t* h = c->h_bb;
+    const BatchLayout& Lb = c->bl;
+    h[Lb.step()] = 0;
+    for (uint32_t b = 0; b < B; ++b) {
+        const enx_sampling& p = params[params_count == 1 ? 0 : b];
+        h[Lb.base() + b] = c->filled[b];
+        h[Lb.first() + b] = first[b];
+        reinterpret_cast<SampleRow*>(h + Lb.params())[b] = SampleRow{p.temperature, p.top_p, p.repetition_penalty, 0.f};
+    }
+    ENX_CUDA(cudaMemcpyAsync(c->d_bb + Lb.step(), h + Lb.step(), ((size_t)Lb.words() - Lb.step()) * 4,
+                             cudaMemcpyHostToDevice, c->stream));
+    ENX_CUDA(cudaMemcpyAsync(c->b_rand, randoms, (size_t)steps * B * 4, cudaMemcpyHostToDevice, c->stream));
+    for (uint32_t i = 0; i < steps; ++i) ENX_CUDA(cudaGraphLaunch(it->second, c->stream));
+    for (uint32_t b = 0; b < B; ++b) c->filled[b] += steps;
+    c->loop_count = steps * B;
+    c->last_launches = c->b_launches[B];
+    if (!sync) return ENX_OK;
+    ENX_CUDA(cudaMemcpyAsync(out_ids, c->b_ids, (size_t)steps * B * 4, cudaMemcpyDeviceToHost, c->stream));
+    ENX_CUDA(cudaMemcpyAsync(h + Lb.err(), c->d_bb + Lb.err(), 4, cudaMemcpyDeviceToHost, c->stream));
+    ENX_CUDA(cudaStreamSynchronize(c->stream));
+    if (h[Lb.err()]) return batch_error(c, h[Lb.err()]);
+    return ENX_OK;
+}
+
 static enx_status capture_step(enx_ctx* c, uint32_t B, bool loop) {
     cudaStream_t st = c->stream;
     StepArgs S = step_args(c);
@@ -1026,8 +1277,6 @@ extern "C" enx_status enx_decode_step(enx_ctx* c, uint32_t batch, const uint32_t
     if (!c->kcache) return fail(ENX_ERR_STATE, "enx_decode_step: call enx_kv_alloc first");
     if (batch == 0) return ENX_OK;
     if (batch > c->batch) return fail(ENX_ERR_RANGE, "enx_decode_step: batch exceeds the allocated sequences");
-    if (batch > kMaxStepBatch)
-        return fail(ENX_ERR_RANGE, "enx_decode_step: at most " + std::to_string(kMaxStepBatch) + " sequences per step");
     CHECK_ARG(params_count == 1 || params_count == batch, "enx_decode_step: params_count must be 1 or batch");
     for (uint32_t b = 0; b < batch; ++b) {
         if (tokens[b] >= c->cfg.vocab) return fail(ENX_ERR_INVALID, "token id outside the vocabulary");
@@ -1036,6 +1285,7 @@ extern "C" enx_status enx_decode_step(enx_ctx* c, uint32_t batch, const uint32_t
                                            std::to_string(c->max_ctx));
     }
     DeviceGuard g(c->device);
+    if (batch > kMaxStepBatch) return decode_batch(c, batch, tokens, params, params_count, randoms, out_ids);
     if (!c->graph[batch]) ENX_TRY(capture_step(c, batch, false));
     StepBlock* h = c->h_step;
     for (uint32_t b = 0; b < batch; ++b) {
@@ -1072,7 +1322,7 @@ extern "C" enx_status enx_decode_loop(enx_ctx* c, uint32_t batch, const uint32_t
     if (!c->loaded) return fail(ENX_ERR_STATE, "enx_decode_loop: no model loaded");
     if (!c->kcache) return fail(ENX_ERR_STATE, "enx_decode_loop: call enx_kv_alloc first");
     if (batch == 0 || steps == 0) return ENX_OK;
-    if (batch > c->batch || batch > kMaxStepBatch) return fail(ENX_ERR_RANGE, "enx_decode_loop: batch too large");
+    if (batch > c->batch) return fail(ENX_ERR_RANGE, "enx_decode_loop: batch too large");
     CHECK_ARG(params_count == 1 || params_count == batch, "enx_decode_loop: params_count must be 1 or batch");
     for (uint32_t b = 0; b < batch; ++b) {
         if (first_tokens[b] >= c->cfg.vocab) return fail(ENX_ERR_INVALID, "token id outside the vocabulary");
@@ -1081,6 +1331,9 @@ extern "C" enx_status enx_decode_loop(enx_ctx* c, uint32_t batch, const uint32_t
                                            std::to_string(steps) + " exceeds " + std::to_string(c->max_ctx));
     }
     DeviceGuard g(c->device);
+    c->loop_batched = batch > kMaxStepBatch;
+    if (batch > kMaxStepBatch)
+        return decode_batch_loop(c, batch, first_tokens, params, params_count, steps, randoms, out_ids, sync);
     if (!c->loop_graph[batch]) ENX_TRY(capture_step(c, batch, true));
     ENX_CUDA(cudaStreamSynchronize(c->stream));  // the pinned loop state may still be in flight
     LoopState* L = c->h_loop;
@@ -1121,12 +1374,23 @@ extern "C" enx_status enx_synchronize(enx_ctx* c) {
     CHECK_ARG(c, "enx_synchronize: null context");
     DeviceGuard g(c->device);
     ENX_CUDA(cudaStreamSynchronize(c->stream));
+    if (c->d_bb) {
+        uint32_t code = 0;
+        ENX_CUDA(cudaMemcpy(&code, c->d_bb + c->bl.err(), 4, cudaMemcpyDeviceToHost));
+        if (code) return batch_error(c, code);
+    }
     return c->d_step ? device_error(c) : ENX_OK;
 }
 
 extern "C" enx_status enx_loop_ids(enx_ctx* c, uint32_t* out_ids, uint32_t count) {
     CHECK_ARG(c && out_ids, "enx_loop_ids: null pointer");
     if (count > c->loop_count) return fail(ENX_ERR_RANGE, "enx_loop_ids: more ids than the last loop produced");
+    if (c->loop_batched) {  // the batched loop leaves its ids on the device
+        DeviceGuard g(c->device);
+        ENX_CUDA(cudaMemcpyAsync(out_ids, c->b_ids, (size_t)count * 4, cudaMemcpyDeviceToHost, c->stream));
+        ENX_CUDA(cudaStreamSynchronize(c->stream));
+        return ENX_OK;
+    }
     std::memcpy(out_ids, c->h_loop_ids, (size_t)count * 4);
     return ENX_OK;
 }

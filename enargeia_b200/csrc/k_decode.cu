@@ -472,6 +472,45 @@ static cudaError_t launch_layer_mt(const LayerArgs& L, const StepArgs& S, cudaSt
                   (size_t)MT * S.intermediate * 8, st, true, L, S);
 }
 
+// Batched decode, after the q|k|v projections of B tokens (token t is sequence t, at position
+// S.pos_of(t)): RoPE of q in place and of k, then k and v rounded to f16 into the token's own cache
+// row (test/reference/ops.ts:103-109, src/kernels/cache_variants.ts:269-301).
+__global__ void k_rope_cache_batch(StepArgs S, uint32_t layer, float* __restrict__ q, const float* __restrict__ k,
+                                   const float* __restrict__ v, uint32_t B) {
+    const uint32_t hd = S.head_dim, half = hd / 2, kvd = S.kv_heads * hd;
+    const uint32_t qp = S.heads * half, kp = S.kv_heads * half, per = qp + kp + kvd;
+    for (uint32_t g = blockIdx.x * blockDim.x + threadIdx.x; g < B * per; g += gridDim.x * blockDim.x) {
+        const uint32_t t = g / per, r = g % per, pos = S.pos_of(t);
+        if (r < qp + kp) {
+            const bool isq = r < qp;
+            const uint32_t r2 = isq ? r : r - qp, h = r2 / half, i = r2 % half;
+            const size_t base = isq ? (size_t)t * S.hidden + h * hd : (size_t)t * kvd + h * hd;
+            float a = isq ? q[base + i] : k[base + i], b = isq ? q[base + i + half] : k[base + i + half];
+            rope_pair(a, b, S.rope_cos[(size_t)pos * half + i], S.rope_sin[(size_t)pos * half + i]);
+            if (isq) {
+                q[base + i] = a;
+                q[base + i + half] = b;
+            } else {
+                uint16_t* row = S.kcache + S.cache_offset(S.seq_of(t), layer, pos) + h * hd;
+                row[i] = __half_as_ushort(__float2half_rn(a));
+                row[i + half] = __half_as_ushort(__float2half_rn(b));
+            }
+        } else {
+            const uint32_t e = r - qp - kp;
+            S.vcache[S.cache_offset(S.seq_of(t), layer, pos) + e] = __half_as_ushort(__float2half_rn(v[(size_t)t * kvd + e]));
+        }
+    }
+}
+
+cudaError_t launch_rope_cache_batch(const StepArgs& S, uint32_t layer, float* q, const float* k, const float* v,
+                                    uint32_t B, cudaStream_t st) {
+    const uint32_t per = S.heads * (S.head_dim / 2) + S.kv_heads * (S.head_dim / 2) + S.kv_heads * S.head_dim;
+    const uint32_t n = B * per;
+    if (n == 0) return cudaSuccess;
+    k_rope_cache_batch<<<(n + 255) / 256 < 4096 ? (n + 255) / 256 : 4096, 256, 0, st>>>(S, layer, q, k, v, B);
+    return cudaGetLastError();
+}
+
 cudaError_t launch_layer(uint32_t mt, const LayerArgs& L, const StepArgs& S, cudaStream_t st) {
     switch (mt) {
         case 1: return launch_layer_mt<1>(L, S, st);
