@@ -113,6 +113,7 @@ SIGNATURES = {
     "enx_stream": (C.c_int32, [P, C.POINTER(P)]),
     "enx_step_launches": (C.c_int32, [P, C.POINTER(U32)]),
     "enx_launch_step_kernel": (C.c_int32, [P, U32, U32]),
+    "enx_batch_profile": (C.c_int32, [P, U32, C.POINTER(C.c_float), U32]),
 }
 
 _lib = None

@@ -166,6 +166,8 @@ extern "C" enx_status enx_sample_batched(float* logits, uint32_t vocab, uint32_t
 }
 
 static uint32_t splits_for(uint32_t positions) { return (positions + kAttnChunk - 1) / kAttnChunk; }
+// Score row stride of the many-token attention path: a multiple of kAttnSplit.
+static uint32_t split_stride(uint32_t positions) { return (positions + kAttnSplit - 1) / kAttnSplit * kAttnSplit; }
 
 extern "C" size_t enx_attn_decode_workspace_bytes(uint32_t max_context, uint32_t heads, uint32_t head_dim) {
     return (size_t)splits_for(max_context) * kAttnChunk * heads * sizeof(float);
@@ -417,11 +419,13 @@ struct enx_ctx {
     float *pf_x = nullptr, *pf_n = nullptr, *pf_q = nullptr, *pf_q2 = nullptr, *pf_k = nullptr,
           *pf_k2 = nullptr, *pf_v = nullptr, *pf_att = nullptr, *pf_t = nullptr, *pf_g = nullptr,
           *pf_u = nullptr, *pf_part = nullptr;
+    double* pf_apart = nullptr;  // split partial sums of the many-token attention
     uint8_t* pf_ws = nullptr;  // tensor-core GEMM workspace (activation limbs) for prefill chunks
     // batched decode: more than kMaxStepBatch sequences per step (the tensor-core GEMM path)
     BatchLayout bl{};
     uint32_t* d_bb = nullptr;  // BatchLayout block
     uint32_t* h_bb = nullptr;  // pinned mirror
+    double* b_part = nullptr;  // split partial sums of the many-token attention
     float *b_x = nullptr, *b_xn = nullptr, *b_q = nullptr, *b_k = nullptr, *b_v = nullptr, *b_att = nullptr,
           *b_t = nullptr, *b_g = nullptr, *b_u = nullptr, *b_scores = nullptr, *b_rand = nullptr;
     uint32_t* b_ids = nullptr;
@@ -484,7 +488,7 @@ void free_graphs(enx_ctx* c) {
 
 void free_prefill(enx_ctx* c) {
     dfree(c->pf_x); dfree(c->pf_n); dfree(c->pf_q); dfree(c->pf_q2); dfree(c->pf_k); dfree(c->pf_k2);
-    dfree(c->pf_v); dfree(c->pf_att); dfree(c->pf_t); dfree(c->pf_g); dfree(c->pf_u); dfree(c->pf_part);
+    dfree(c->pf_v); dfree(c->pf_att); dfree(c->pf_t); dfree(c->pf_g); dfree(c->pf_u); dfree(c->pf_part); dfree(c->pf_apart);
     dfree(c->pf_ids);
     dfree(c->pf_ws);
     c->pf_chunk = 0;
@@ -505,7 +509,7 @@ void free_kv(enx_ctx* c) {
     c->h_loop_ids = nullptr;
     c->loop_cap = c->loop_count = 0;
     dfree(c->d_bb); dfree(c->b_x); dfree(c->b_xn); dfree(c->b_q); dfree(c->b_k); dfree(c->b_v); dfree(c->b_att);
-    dfree(c->b_t); dfree(c->b_g); dfree(c->b_u); dfree(c->b_scores); dfree(c->b_rand); dfree(c->b_ids); dfree(c->b_ws);
+    dfree(c->b_t); dfree(c->b_g); dfree(c->b_u); dfree(c->b_scores); dfree(c->b_rand); dfree(c->b_ids); dfree(c->b_ws); dfree(c->b_part);
     if (c->h_bb) cudaFreeHost(c->h_bb);
     c->h_bb = nullptr;
     c->bl = BatchLayout{};
@@ -799,7 +803,8 @@ extern "C" enx_status enx_kv_alloc(enx_ctx* c, uint32_t max_context, uint32_t ba
         ENX_TRY(dalloc(&c->b_t, Bn * H, "batch projection"));
         ENX_TRY(dalloc(&c->b_g, Bn * I, "batch gate"));
         ENX_TRY(dalloc(&c->b_u, Bn * I, "batch up"));
-        ENX_TRY(dalloc(&c->b_scores, Bn * splits_for(max_context) * kAttnChunk * C.heads, "batch scores"));
+        ENX_TRY(dalloc(&c->b_scores, Bn * split_stride(max_context) * C.heads, "batch scores"));
+        ENX_TRY(dalloc(&c->b_part, Bn * (split_stride(max_context) / kAttnSplit) * H, "batch attention splits"));
         ENX_TRY(dalloc(&c->b_rand, Bn * max_context, "batch loop randoms"));
         ENX_TRY(dalloc(&c->b_ids, Bn * max_context, "batch loop ids"));
         ENX_TRY(dalloc(&c->b_ws, gemm_tc_workspace_bytes(batch, (uint32_t)(I > H ? I : H)), "batch GEMM workspace"));
@@ -878,7 +883,8 @@ static enx_status ensure_prefill(enx_ctx* c, uint32_t chunk) {
     ENX_TRY(dalloc(&c->pf_t, chunk * H, "prefill tmp"));
     ENX_TRY(dalloc(&c->pf_g, chunk * I, "prefill gate"));
     ENX_TRY(dalloc(&c->pf_u, chunk * I, "prefill up"));
-    ENX_TRY(dalloc(&c->pf_part, (size_t)chunk * splits_for(c->max_ctx) * kAttnChunk * C.heads, "prefill scores"));
+    ENX_TRY(dalloc(&c->pf_part, (size_t)chunk * split_stride(c->max_ctx) * C.heads, "prefill scores"));
+    ENX_TRY(dalloc(&c->pf_apart, (size_t)chunk * (split_stride(c->max_ctx) / kAttnSplit) * H, "prefill attention splits"));
     ENX_TRY(dalloc(&c->pf_ids, chunk, "prefill ids"));
     if (chunk >= kTcMinTokens)
         ENX_TRY(dalloc(&c->pf_ws, gemm_tc_workspace_bytes(chunk, (uint32_t)(I > H ? I : H)), "prefill GEMM workspace"));
@@ -908,6 +914,8 @@ extern "C" enx_status enx_prefill(enx_ctx* c, uint32_t seq, const uint32_t* ids,
     S.seq_fixed = seq;
     S.q = c->pf_q2;
     S.scores = c->pf_part;
+    S.score_stride = split_stride(c->max_ctx);
+    S.attn_part = c->pf_apart;
     for (uint32_t begin0 = 0; begin0 < n; begin0 += chunk) {
         const uint32_t m = n - begin0 < chunk ? n - begin0 : chunk;
         const uint32_t begin = c->filled[seq];
@@ -1051,6 +1059,8 @@ static cudaError_t batch_body(enx_ctx* c, uint32_t B, cudaStream_t st) {
     StepArgs S = step_args(c);
     S.q = c->b_q;
     S.scores = c->b_scores;
+    S.score_stride = split_stride(c->max_ctx);
+    S.attn_part = c->b_part;
     S.pos = blk + c->bl.pos();
     cudaError_t e = launch_embed(blk + c->bl.tok(), c->head.embed, c->head.bits, c->b_x, B, 0, C.vocab, H, st, false);
     for (uint32_t l = 0; l < C.layers && e == cudaSuccess; ++l) {
@@ -1077,6 +1087,73 @@ static cudaError_t batch_body(enx_ctx* c, uint32_t B, cudaStream_t st) {
                           reinterpret_cast<const SampleRow*>(blk + c->bl.rows()), false, SampleRow{}, blk + c->bl.out(), st,
                           false);
     return e;
+}
+
+// The batched step body once, outside any graph, with events between its sections; adds each
+// section's time (ms) to ms[k]: 0 embed, 1 RMSNorms, 2 q|k|v GEMMs, 3 RoPE + cache rows,
+// 4 attention, 5 o GEMM + residual, 6 gate/up GEMMs + SiLU, 7 down GEMM + residual, 8 head GEMM,
+// 9 sampler.  It reruns the last step's rows (same cache rows and logits).
+static enx_status batch_profile(enx_ctx* c, uint32_t B, float* ms) {
+    const enx_model_config& C = c->cfg;
+    const uint32_t H = C.hidden, kvd = C.kv_heads * C.head_dim, I = C.intermediate;
+    cudaStream_t st = c->stream;
+    uint32_t* blk = c->d_bb;
+    StepArgs S = step_args(c);
+    S.q = c->b_q;
+    S.scores = c->b_scores;
+    S.score_stride = split_stride(c->max_ctx);
+    S.attn_part = c->b_part;
+    S.pos = blk + c->bl.pos();
+    cudaEvent_t ev[2];
+    ENX_CUDA(cudaEventCreate(&ev[0]));
+    ENX_CUDA(cudaEventCreate(&ev[1]));
+    auto section = [&](int k, auto&& work) -> cudaError_t {
+        cudaEventRecord(ev[0], st);
+        cudaError_t e = work();
+        cudaEventRecord(ev[1], st);
+        cudaEventSynchronize(ev[1]);
+        float t = 0.f;
+        cudaEventElapsedTime(&t, ev[0], ev[1]);
+        ms[k] += t;
+        return e;
+    };
+    cudaError_t e = section(0, [&] { return launch_embed(blk + c->bl.tok(), c->head.embed, c->head.bits, c->b_x, B, 0, C.vocab, H, st, false); });
+    for (uint32_t l = 0; l < C.layers && e == cudaSuccess; ++l) {
+        const LayerArgs& L = c->layers[l];
+        e = section(1, [&] { return launch_rmsnorm(c->b_x, L.norm_in, c->b_xn, B, H, C.rms_norm_eps, st); });
+        if (e == cudaSuccess) e = section(2, [&] {
+            cudaError_t r = proj_b(c, 4, c->b_xn, L.wq, L.bq, c->b_q, B, H, st);
+            if (r == cudaSuccess) r = proj_b(c, 4, c->b_xn, L.wk, L.bk, c->b_k, B, kvd, st);
+            return r == cudaSuccess ? proj_b(c, 4, c->b_xn, L.wv, L.bv, c->b_v, B, kvd, st) : r;
+        });
+        if (e == cudaSuccess) e = section(3, [&] { return launch_rope_cache_batch(S, l, c->b_q, c->b_k, c->b_v, B, st); });
+        if (e == cudaSuccess) e = section(4, [&] { return launch_attn(S, l, B, c->b_att, st, false); });
+        if (e == cudaSuccess) e = section(5, [&] {
+            cudaError_t r = proj_b(c, 4, c->b_att, L.wo, nullptr, c->b_t, B, H, st);
+            return r == cudaSuccess ? launch_add(c->b_x, c->b_t, c->b_x, B * H, st) : r;
+        });
+        if (e == cudaSuccess) e = section(1, [&] { return launch_rmsnorm(c->b_x, L.norm_post, c->b_xn, B, H, C.rms_norm_eps, st); });
+        if (e == cudaSuccess) e = section(6, [&] {
+            cudaError_t r = proj_b(c, 4, c->b_xn, L.wg, nullptr, c->b_g, B, I, st);
+            if (r == cudaSuccess) r = proj_b(c, 4, c->b_xn, L.wu, nullptr, c->b_u, B, I, st);
+            return r == cudaSuccess ? launch_silu_mul(c->b_g, c->b_u, c->b_g, B * I, st) : r;
+        });
+        if (e == cudaSuccess) e = section(7, [&] {
+            cudaError_t r = proj_b(c, 4, c->b_g, L.wd, nullptr, c->b_t, B, H, st);
+            return r == cudaSuccess ? launch_add(c->b_x, c->b_t, c->b_x, B * H, st) : r;
+        });
+    }
+    if (e == cudaSuccess) e = section(1, [&] { return launch_rmsnorm(c->b_x, c->head.norm, c->normed, B, H, C.rms_norm_eps, st); });
+    if (e == cudaSuccess) e = section(8, [&] { return proj_b(c, c->head.bits, c->normed, c->head.embed, nullptr, c->logits, B, C.vocab, st); });
+    if (e == cudaSuccess) e = section(9, [&] {
+        return launch_sample(c->logits, C.vocab, B, c->history, c->max_ctx, blk + c->bl.hist(),
+                             reinterpret_cast<const SampleRow*>(blk + c->bl.rows()), false, SampleRow{}, blk + c->bl.out(), st,
+                             false);
+    });
+    cudaEventDestroy(ev[0]);
+    cudaEventDestroy(ev[1]);
+    if (e != cudaSuccess) return cuda_fail(e, "batched step profile");
+    return ENX_OK;
 }
 
 static enx_status capture_batch(enx_ctx* c, uint32_t B, bool loop) {
@@ -1492,4 +1569,14 @@ extern "C" enx_status enx_launch_step_kernel(enx_ctx* c, uint32_t batch, uint32_
         ENX_CUDA(launch_mega(batch, A, geo, c->stream));
     }
     return ENX_OK;
+}
+
+extern "C" enx_status enx_batch_profile(enx_ctx* c, uint32_t batch, float* ms, uint32_t count) {
+    CHECK_ARG(c && ms && count >= 10, "enx_batch_profile: need room for 10 section times");
+    if (!c->d_bb || batch <= kMaxStepBatch || batch > c->batch)
+        return fail(ENX_ERR_STATE, "enx_batch_profile: needs a batched context and a batch above 4");
+    DeviceGuard g(c->device);
+    for (uint32_t i = 0; i < count; ++i) ms[i] = 0.f;
+    ENX_CUDA(cudaStreamSynchronize(c->stream));
+    return batch_profile(c, batch, ms);
 }

@@ -443,10 +443,205 @@ cudaError_t launch_matmul(int bits, const float* x, const QW& w, const float* bi
                      : launch_matmul_bits<4>(x, w, bias, out, m, out_stride, out_offset, st, pdl);
 }
 
+// Stages n rows of hd f16 values (rows `stride` halfs apart in global memory) into shared memory
+// as doubles, rows dst_stride doubles apart, zero rows from n to nmax: 16-byte loads, eight in
+// flight per thread before any is converted.
+__device__ __forceinline__ void stage_rows_f16_to_f64(double* dst, uint32_t dst_stride, const uint16_t* src,
+                                                      uint32_t stride, uint32_t n, uint32_t nmax, uint32_t hd) {
+    const uint32_t row8 = hd / 8, total = nmax * row8;
+    for (uint32_t base = threadIdx.x; base < total; base += 8 * blockDim.x) {
+        uint4 v[8];
+#pragma unroll
+        for (int k = 0; k < 8; ++k) {
+            const uint32_t i = base + k * blockDim.x;
+            v[k] = make_uint4(0, 0, 0, 0);
+            if (i < total && i / row8 < n)
+                v[k] = __ldcg(reinterpret_cast<const uint4*>(src + (size_t)(i / row8) * stride) + i % row8);
+        }
+#pragma unroll
+        for (int k = 0; k < 8; ++k) {
+            const uint32_t i = base + k * blockDim.x;
+            if (i >= total) break;
+            const __half2* h2 = reinterpret_cast<const __half2*>(&v[k]);
+            double* d = dst + (size_t)(i / row8) * dst_stride + (i % row8) * 8;
+#pragma unroll
+            for (int e = 0; e < 4; ++e) {
+                const float2 f = __half22float2(h2[e]);
+                d[2 * e] = (double)f.x;
+                d[2 * e + 1] = (double)f.y;
+            }
+        }
+    }
+}
+
+// Many-token attention scores: one CTA per (kv head, 128-position split, token), a thread per
+// position holding all the group's heads (kMaxGroupSplit accumulators), so each K pair read from
+// shared memory feeds every head and the q pairs are warp-wide broadcasts.  The split's K rows are
+// widened to double once, row stride hd + 2 doubles (an odd number of 16-byte units: conflict-free
+// 16-byte reads).  scores[t][h][j] = float(sum_d q[h][d] * K[j][d] / sqrt(hd))
+// (test/reference/ops.ts:123-151).
+constexpr uint32_t kMaxGroupSplit = 8;
+__global__ void __launch_bounds__(kAttnSplit) k_attn_scores_split(StepArgs S, uint32_t layer) {
+    pdl_launch_dependents();
+    pdl_wait();
+    const uint32_t g = blockIdx.x, sp = blockIdx.y, t = blockIdx.z;
+    const uint32_t hd = S.head_dim, group = S.heads / S.kv_heads, kvd = S.kv_heads * hd;
+    const uint32_t npos = S.pos_of(t) + 1, j0 = sp * kAttnSplit;
+    if (j0 >= npos) return;
+    const uint32_t n = min(kAttnSplit, npos - j0), ks = hd + 2;
+    extern __shared__ double kd[];             // [kAttnSplit][hd + 2]
+    double* qd = kd + (size_t)kAttnSplit * ks;  // [group][hd]
+    const uint16_t* K = S.kcache + S.cache_offset(S.seq_of(t), layer, j0) + g * hd;
+    for (uint32_t i = threadIdx.x; i < group * hd; i += blockDim.x)
+        qd[i] = (double)__ldcg(S.q + (size_t)t * S.hidden + g * group * hd + i);
+    stage_rows_f16_to_f64(kd, ks, K, kvd, n, n, hd);
+    __syncthreads();
+    const uint32_t j = threadIdx.x;
+    if (j >= n) return;
+    double acc[kMaxGroupSplit];
+#pragma unroll
+    for (int h = 0; h < (int)kMaxGroupSplit; ++h) acc[h] = 0.0;
+    const double2* kr = reinterpret_cast<const double2*>(kd + j * ks);
+    for (uint32_t d2 = 0; d2 < hd / 2; ++d2) {
+        const double2 kv = kr[d2];
+#pragma unroll
+        for (int h = 0; h < (int)kMaxGroupSplit; ++h) {
+            if (h < (int)group) {
+                const double2 qv = reinterpret_cast<const double2*>(qd + h * hd)[d2];
+                acc[h] = fma(qv.y, kv.y, fma(qv.x, kv.x, acc[h]));
+            }
+        }
+    }
+    const double scale = 1.0 / sqrt((double)hd);
+#pragma unroll
+    for (int h = 0; h < (int)kMaxGroupSplit; ++h)
+        if (h < (int)group) S.scores[((size_t)t * S.heads + g * group + h) * S.score_stride + j0 + j] = (float)(acc[h] * scale);
+}
+
+// Many-token attention, after k_attn_scores: the softmax of every (token, head) row in place --
+// w = float(float(exp(score - max)) / sum), the exps and their sum in double
+// (test/reference/ops.ts:161-178) -- by one CTA per row.
+__global__ void __launch_bounds__(kThreads) k_attn_stats(StepArgs S) {
+    pdl_launch_dependents();
+    pdl_wait();
+    const uint32_t h = blockIdx.x, t = blockIdx.y;
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+    const uint32_t npos = S.pos_of(t) + 1;
+    float* sc = S.scores + ((size_t)t * S.heads + h) * S.score_stride;
+    __shared__ float fred[kWarps];
+    __shared__ double dred[kWarps];
+    float m = -INFINITY;
+    for (uint32_t j = threadIdx.x; j < npos; j += blockDim.x) m = fmaxf(m, sc[j]);
+    m = warp_max(m);
+    if (lane == 0) fred[warp] = m;
+    __syncthreads();
+    m = -INFINITY;
+    for (int w = 0; w < kWarps; ++w) m = fmaxf(m, fred[w]);
+    double sum = 0.0;
+    for (uint32_t j = threadIdx.x; j < npos; j += blockDim.x) {
+        const double e = exp((double)sc[j] - (double)m);
+        sc[j] = (float)e;
+        sum += e;
+    }
+    sum = warp_sum_d(sum);
+    if (lane == 0) dred[warp] = sum;
+    __syncthreads();
+    sum = 0.0;
+    for (int w = 0; w < kWarps; ++w) sum += dred[w];  // fixed order
+    for (uint32_t j = threadIdx.x; j < npos; j += blockDim.x) sc[j] = (float)((double)sc[j] / sum);
+}
+
+// Weighted V over one split of kAttnSplit positions for the query heads of one kv head, in double
+// (test/reference/ops.ts:181-204): attn_part[t][split][h][d].  A thread per (dimension pair,
+// quarter of the positions) holds every head of the group, so each V pair read from shared memory
+// feeds all heads and the weight pairs are broadcasts; the quarters meet in fixed order.
+// grid = (kv_heads, splits, ntok), 4 warps.
+__global__ void __launch_bounds__(128) k_attn_apply_split(StepArgs S, uint32_t layer) {
+    pdl_launch_dependents();
+    pdl_wait();
+    const uint32_t g = blockIdx.x, sp = blockIdx.y, t = blockIdx.z;
+    const uint32_t hd = S.head_dim, group = S.heads / S.kv_heads, kvd = S.kv_heads * hd;
+    const uint32_t npos = S.pos_of(t) + 1, j0 = sp * kAttnSplit;
+    if (j0 >= npos) return;
+    const uint32_t n = min(kAttnSplit, npos - j0);
+    extern __shared__ double vs[];                  // [kAttnSplit][hd]
+    double* ws = vs + (size_t)kAttnSplit * hd;       // [group][kAttnSplit]
+    double* red = ws + (size_t)kMaxGroupSplit * kAttnSplit;  // [4][group][hd]
+    const uint16_t* V = S.vcache + S.cache_offset(S.seq_of(t), layer, j0) + g * hd;
+    stage_rows_f16_to_f64(vs, hd, V, kvd, n, kAttnSplit, hd);
+    for (uint32_t i = threadIdx.x; i < group * kAttnSplit; i += blockDim.x) {
+        const uint32_t h = i / kAttnSplit, j = i % kAttnSplit;
+        ws[i] = j < n ? (double)S.scores[((size_t)t * S.heads + g * group + h) * S.score_stride + j0 + j] : 0.0;
+    }
+    __syncthreads();
+    const uint32_t lane = threadIdx.x & 31, q4 = threadIdx.x >> 5;  // dimension pair, position quarter
+    const uint32_t pairs = hd / 2;
+    if (lane < pairs) {
+        double ax[kMaxGroupSplit], ay[kMaxGroupSplit];
+#pragma unroll
+        for (int h = 0; h < (int)kMaxGroupSplit; ++h) ax[h] = ay[h] = 0.0;
+        const uint32_t jb = q4 * (kAttnSplit / 4), je = jb + kAttnSplit / 4;
+        for (uint32_t j = jb; j < je; j += 2) {  // zero weights past n keep the tail exact
+            const double2 v0 = reinterpret_cast<const double2*>(vs + (size_t)j * hd)[lane];
+            const double2 v1 = reinterpret_cast<const double2*>(vs + (size_t)(j + 1) * hd)[lane];
+#pragma unroll
+            for (int h = 0; h < (int)kMaxGroupSplit; ++h) {
+                if (h < (int)group) {
+                    const double2 w = reinterpret_cast<const double2*>(ws + h * kAttnSplit)[j >> 1];
+                    ax[h] = fma(w.y, v1.x, fma(w.x, v0.x, ax[h]));
+                    ay[h] = fma(w.y, v1.y, fma(w.x, v0.y, ay[h]));
+                }
+            }
+        }
+#pragma unroll
+        for (int h = 0; h < (int)kMaxGroupSplit; ++h) {
+            if (h < (int)group) {
+                red[((size_t)q4 * group + h) * hd + 2 * lane] = ax[h];
+                red[((size_t)q4 * group + h) * hd + 2 * lane + 1] = ay[h];
+            }
+        }
+    }
+    __syncthreads();
+    double* part = S.attn_part + (((size_t)t * (S.score_stride / kAttnSplit) + sp) * S.heads + g * group) * hd;
+    for (uint32_t o = threadIdx.x; o < group * hd; o += blockDim.x) {
+        double v = 0.0;
+        for (uint32_t k = 0; k < 4; ++k) v += red[(size_t)k * group * hd + o];  // quarters in order
+        part[o] = v;
+    }
+}
+
+// out[t][h*hd + d] = float(sum over the token's splits of attn_part), splits in order.
+__global__ void k_attn_combine(StepArgs S, float* out) {
+    pdl_launch_dependents();
+    pdl_wait();
+    const uint32_t t = blockIdx.x, nsp = (S.pos_of(t) + kAttnSplit) / kAttnSplit, stride = S.score_stride / kAttnSplit;
+    const double* part = S.attn_part + (size_t)t * stride * S.hidden;
+    for (uint32_t o = threadIdx.x; o < S.hidden; o += blockDim.x) {
+        double v = 0.0;
+        for (uint32_t sp = 0; sp < nsp; ++sp) v += part[(size_t)sp * S.hidden + o];
+        out[(size_t)t * S.hidden + o] = (float)v;
+    }
+}
+
 cudaError_t launch_attn(const StepArgs& S, uint32_t layer, uint32_t ntok, float* out, cudaStream_t st, bool pdl) {
     const uint32_t group = S.heads / S.kv_heads;
-    cudaError_t e = launch(k_attn_scores, dim3(S.kv_heads, S.score_stride / kAttnChunk, ntok), dim3(kThreads), 0, st,
-                           pdl, S, layer);
+    cudaError_t e;
+    if (S.attn_part && ntok >= 8 && S.score_stride % kAttnSplit == 0 && group <= kMaxGroupSplit && S.head_dim <= 64 &&
+        S.head_dim % 2 == 0) {
+        // many tokens: scores over position splits, softmax rows, V over position splits, then
+        // the fixed-order combine
+        e = launch(k_attn_scores_split, dim3(S.kv_heads, S.score_stride / kAttnSplit, ntok), dim3(kAttnSplit),
+                   (size_t)(kAttnSplit * (S.head_dim + 2) + group * S.head_dim) * 8, st, pdl, S, layer);
+        if (e != cudaSuccess) return e;
+        e = launch(k_attn_stats, dim3(S.heads, ntok), dim3(kThreads), 0, st, pdl, S);
+        if (e != cudaSuccess) return e;
+        e = launch(k_attn_apply_split, dim3(S.kv_heads, S.score_stride / kAttnSplit, ntok), dim3(128),
+                   ((size_t)kAttnSplit * (S.head_dim + kMaxGroupSplit) + 4 * (size_t)group * S.head_dim) * 8, st, pdl, S,
+                   layer);
+        if (e != cudaSuccess) return e;
+        return launch(k_attn_combine, dim3(ntok), dim3(kThreads), 0, st, pdl, S, out);
+    }
+    e = launch(k_attn_scores, dim3(S.kv_heads, S.score_stride / kAttnChunk, ntok), dim3(kThreads), 0, st, pdl, S, layer);
     if (e != cudaSuccess) return e;
     return launch(k_attn_apply, dim3(S.kv_heads, ntok), dim3(kThreads), (size_t)group * S.score_stride * 4, st, pdl,
                   S, layer, out);

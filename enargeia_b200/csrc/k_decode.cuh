@@ -6,6 +6,7 @@
 namespace enx {
 
 constexpr uint32_t kAttnChunk = 64;  // positions per attention-score split
+constexpr uint32_t kAttnSplit = 128; // positions per weighted-V split (many-token attention)
 
 // Buffers and geometry of one decode step (shared by every layer of the step).
 struct StepArgs {
@@ -19,6 +20,7 @@ struct StepArgs {
     float* scores;         // [MT][heads][score_stride] attention scores (workspace)
     float* attn_out;       // [MT][hidden] attention output
     uint32_t score_stride; // >= positions attended (a multiple of kAttnChunk)
+    double* attn_part;     // [MT][score_stride/kAttnSplit][heads][head_dim] split partial sums, or null
     const uint32_t* pos;   // [MT] position written this step (device), or null: pos_base + t
     uint32_t pos_base;
     uint32_t seq_fixed;    // sequence of every token, or 0xFFFFFFFF: token t is sequence t

@@ -290,16 +290,28 @@ __global__ void __cluster_dims__(kCluster, 1, 1) __launch_bounds__(kSThreads, 1)
             double ta = block_sum_d(sm, above);
             if (threadIdx.x == 0) { sm.bucket[0] += tb; sm.bucket[255] += ta; }
             cluster.sync();
-            if (threadIdx.x == 0) {
-                // cluster bucket totals, in rank order; then suffix sums mass(p >= thr[j])
-                double* tot = sm.suffix;
-                for (int b = 0; b < 256; ++b) tot[b] = 0.0;
-                for (int r = 0; r < kCluster; ++r) {
-                    SampleSmem* o = cluster.map_shared_rank(&sm, r);
-                    for (int b = 0; b < 256; ++b) tot[b] += o->bucket[b];
+            // cluster bucket totals (a thread per bucket, ranks in order), then suffix sums
+            // mass(p >= thr[j]): within each warp of 32 buckets, then the warps above added on
+            if (threadIdx.x < 256) {
+                double t = 0.0;
+                for (int r = 0; r < kCluster; ++r) t += cluster.map_shared_rank(&sm, r)->bucket[threadIdx.x];
+                double v = t;
+#pragma unroll
+                for (int o = 1; o < 32; o <<= 1) {
+                    const double n = __shfl_down_sync(0xffffffffu, v, o);
+                    if (lane + o < 32) v += n;
                 }
-                double acc = 0.0;
-                for (int j = 255; j >= 0; --j) { acc += tot[j]; sm.suffix[j] = acc; }
+                sm.suffix[threadIdx.x] = v;
+                if (lane == 0) sm.wred[threadIdx.x >> 5] = v;
+            }
+            __syncthreads();
+            if (threadIdx.x < 256) {
+                double add = 0.0;
+                for (int w = (threadIdx.x >> 5) + 1; w < 8; ++w) add += sm.wred[w];
+                sm.suffix[threadIdx.x] += add;
+            }
+            __syncthreads();
+            if (threadIdx.x == 0) {
                 float l = lo, h = hi;
                 int n = 1;
                 for (int step = 0; step < 8; ++step) {

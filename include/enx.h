@@ -293,6 +293,13 @@ ENX_API enx_status enx_step_launches(enx_ctx* ctx, uint32_t* launches);
  * logits.  ENX_ERR_STATE if no step ran yet or the step did not use the persistent kernel. */
 ENX_API enx_status enx_launch_step_kernel(enx_ctx* ctx, uint32_t batch, uint32_t count);
 
+/* Measurement hook for batched decode (more than 4 sequences): runs the last batched step's body
+ * once, outside its graph, with CUDA events between sections, and writes each section's total
+ * time in ms to ms[0..9]: embed, RMSNorms, q|k|v GEMMs, RoPE + cache rows, attention, o GEMM +
+ * residual, gate/up GEMMs + SiLU, down GEMM + residual, head GEMM, sampler.  It rewrites the same
+ * cache rows and logits.  count must be at least 10. */
+ENX_API enx_status enx_batch_profile(enx_ctx* ctx, uint32_t batch, float* ms, uint32_t count);
+
 #ifdef __cplusplus
 }
 #endif
