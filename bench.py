@@ -443,6 +443,192 @@ def run_batched(args, rank, world, local_rank):
 
 
 # ---------------------------------------------------------------------------------------------
+# config 2: tied int8 LM head + sampling, vocab-sharded across GPUs (bench.py --workload config2)
+
+HEAD_VOCAB, HEAD_HIDDEN, HEAD_HIST = 151936, 896, 2048
+HEAD_METRIC = ("LM head + sampling rows/s (int8 151936x896 tied head, T 0.7 / top-p 0.9 / rp 1.1, "
+               "2048-id history)")
+
+
+def head_table():
+    from enargeia_b200.format import quantize_tensor
+
+    rng = np.random.default_rng(SEED + 2)
+    w = rng.standard_normal((HEAD_VOCAB, HEAD_HIDDEN), dtype=np.float32) * np.float32(0.02)
+    return quantize_tensor("model.embed_tokens.weight", w, 8)
+
+
+def run_head(args, rank, world, local_rank):
+    """Each rank holds the contiguous row range of the table its shard owns; one step computes the
+    logits of B hidden states on every shard and samples B ids.  N = 1: the fused single-GPU
+    sampler (one cluster per row); N > 1: the sharded sampler's phases with an NCCL allgather of
+    the per-shard candidates / sums / top-p bucket masses / kept masses / picks between them.
+    Total work is fixed as N grows (strong scaling)."""
+    import torch
+    import torch.distributed as dist
+
+    from enargeia_b200 import build, kernels as K
+    from enargeia_b200.vocab_shard import ShardedHead, ShardedSampler, ShardInputs, run_distributed, \
+        sampling_rows_tensor
+
+    build.build()
+    torch.cuda.set_device(local_rank)
+    dev = torch.device("cuda", local_rank)
+    table = head_table()
+    head = ShardedHead(table, HEAD_VOCAB, rank, world, dev)
+    shard_bytes = head.packed.numel() * 4 + head.scales.numel() * 4 + head.zeros.numel() * 4
+    stream = torch.cuda.current_stream()
+
+    def barrier():
+        if world > 1:
+            dist.barrier()
+        torch.cuda.synchronize()
+
+    def max_over_ranks(x):
+        if world == 1:
+            return x
+        t = torch.tensor([x], dtype=torch.float64, device=dev)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        return float(t.item())
+
+    peaks = {}
+    try:
+        peaks = json.loads((ROOT / "MEASURED_PEAKS.json").read_text())
+    except (OSError, ValueError):
+        pass
+    hbm = float(peaks.get("hbm_gbs", 6650.0))
+    peak_src = "measured" if "hbm_gbs" in peaks else "fallback"
+
+    def one_batch(B, steps, warmup, clocks=None):
+        rng = np.random.default_rng(7000 + B)  # same inputs on every rank
+        total = steps + warmup
+        xs_host = torch.from_numpy(rng.standard_normal((total, B, HEAD_HIDDEN)).astype(np.float32)).pin_memory()
+        xs = xs_host.to(dev)
+        history = torch.from_numpy(rng.integers(0, HEAD_VOCAB, (B, HEAD_HIST)).astype(np.int32)).to(dev)
+        hlen = torch.full((B,), HEAD_HIST, dtype=torch.int32, device=dev)
+        params = [[(0.7, 0.9, 1.1, float(np.float32(v))) for v in rng.random(B)] for _ in range(total)]
+        params_dev = [sampling_rows_tensor(p, dev) for p in params]
+        logits = torch.empty((B, head.n), dtype=torch.float32, device=dev)
+        out = torch.empty(B, dtype=torch.int32, device=dev)
+        sampler = ShardedSampler(HEAD_VOCAB, rank, world, B, dev) if world > 1 else None
+
+        def step(i, x, prow_dev):
+            head.logits(x, logits)
+            if sampler is None:
+                K.sample_batched(logits, history, hlen, prow_dev, out)
+                return out
+            return run_distributed(sampler, ShardInputs(logits, history, hlen, params[i]), params_dev=prow_dev)
+
+        for i in range(warmup):
+            step(i, xs[i], params_dev[i])
+        barrier()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record(stream)
+        for i in range(warmup, total):
+            step(i, xs[i], params_dev[i])
+        e1.record(stream)
+        barrier()
+        ms = max_over_ranks(e0.elapsed_time(e1)) / steps
+        # e2e: hidden states and sampling rows copied in from pinned host memory, ids read back,
+        # every step
+        prow_host = [torch.frombuffer(bytearray(p.cpu().numpy().tobytes()), dtype=torch.uint8).pin_memory()
+                     for p in params_dev]
+        xbuf = torch.empty((B, HEAD_HIDDEN), dtype=torch.float32, device=dev)
+        pbuf = torch.empty_like(params_dev[0])
+        barrier()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record(stream)
+        for i in range(warmup, total):
+            xbuf.copy_(xs_host[i], non_blocking=True)
+            pbuf.copy_(prow_host[i], non_blocking=True)
+            ids = step(i, xbuf, pbuf).cpu()
+        e1.record(stream)
+        barrier()
+        e2e_ms = max_over_ranks(e0.elapsed_time(e1)) / steps
+        # the head GEMM/matvec alone: R launches back to back on this rank's shard
+        reps = 20
+        head.logits(xs[0], logits)
+        torch.cuda.synchronize()
+        e0.record(stream)
+        for _ in range(reps):
+            head.logits(xs[0], logits)
+        e1.record(stream)
+        torch.cuda.synchronize()
+        head_us = e0.elapsed_time(e1) / reps * 1e3
+        head_bytes = shard_bytes + B * HEAD_HIDDEN * 4 + B * head.n * 4
+        achieved = head_bytes / (head_us / 1e6) / 1e9
+        head_launches = 2 if B >= 16 else 1
+        launches = head_launches + (1 if sampler is None else 9)
+        del ids
+        return {"rows": B, "value": round(B / (ms / 1e3), 1), "ms_per_step": round(ms, 4),
+                "e2e": {"value": round(B / (e2e_ms / 1e3), 1), "unit": "rows/s",
+                        "h2d_bytes_per_step": B * HEAD_HIDDEN * 4 + B * 16, "d2h_bytes_per_step": B * 4,
+                        "api": "ShardedHead.logits (enx_lm_head_q8) + enx_sample_batched / enx_shard_* phases"},
+                "head_roofline": {"kernel": "enx_lm_head_q8 over this rank's rows"
+                                            + (" (tcgen05 limb GEMM)" if B >= 16 else " (CUDA-core matvec)"),
+                                  "bound": "hbm", "achieved": round(achieved, 1), "peak": hbm, "unit": "GB/s",
+                                  "frac": round(achieved / hbm, 4), "traffic": None,
+                                  "algorithmic_bytes_per_launch": int(head_bytes), "launch_us": round(head_us, 2),
+                                  "peak_source": f"{peak_src} MEASURED_PEAKS.json hbm_gbs (burst copy)"},
+                "sampler_ms_per_step": round(ms - head_us / 1e3, 4),
+                "gpu_launches": launches * steps, "launches_per_step": launches}
+
+    steps = min(args.steps, 200)
+    small = one_batch(1, steps, args.warmup)
+    with ClockSampler(local_rank) as clocks:
+        big = one_batch(args.batch if args.batch != 256 else 64, steps, args.warmup)
+    out = {
+        "metric": HEAD_METRIC,
+        "value": big["value"],
+        "unit": "rows/s",
+        "n_gpus": world,
+        "steps": steps,
+        "warmup": args.warmup,
+        "ms_per_step": big["ms_per_step"],
+        "higher_is_better": True,
+        "scaling": "strong",
+        "vs_baseline": None,
+        "dtype": "int8 table x f32 hidden (exact block sums, f64 accumulate), f64 sampling",
+        "data": "synthetic: seeded int8-quantised normal(0,0.02) table, hidden N(0,1), 2048 uniform random history ids",
+        "config": {"workload": f"config 2: tied int8 LM head + sampling, batch {big['rows']} (batch 1 below), "
+                               f"vocab {HEAD_VOCAB} x hidden {HEAD_HIDDEN}", "rows": big["rows"],
+                   "parallelism": f"vocab-sharded x{world}" if world > 1 else "one GPU",
+                   "rows_per_gpu": head.n, "l2": "inputs larger than L2: 137 MB table per step at N=1"},
+        "e2e": big["e2e"],
+        "roofline": big["head_roofline"],
+        "sampler_ms_per_step": big["sampler_ms_per_step"],
+        "gpu_launches": big["gpu_launches"],
+        "launches_per_step": big["launches_per_step"],
+        "batch_1": small,
+        "clocks": clocks.summary(),
+    }
+    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+        out["cpu_baseline"] = head_cpu_baseline(table, budget_s=args.cpu_budget)
+    if rank == 0:
+        print(json.dumps(out), flush=True)
+
+
+def head_cpu_baseline(table, budget_s=15.0):
+    from oracle import oracle as O
+
+    O.build()
+    cores = O.max_threads()
+    rng = np.random.default_rng(99)
+    hist = rng.integers(0, HEAD_VOCAB, HEAD_HIST).astype(np.uint32)
+    n = 0
+    t0 = time.perf_counter()
+    while n < 2 or time.perf_counter() - t0 < budget_s:
+        x = rng.standard_normal(HEAD_HIDDEN).astype(np.float32)
+        logits = O.linear_q(table, x)
+        O.sample(logits, hist, 0.7, 0.9, 1.1, float(np.float32(rng.random())))
+        n += 1
+    dt = time.perf_counter() - t0
+    return {"value": round(n / dt, 3), "unit": "rows/s", "cores": cores, "kind": "port",
+            "sample": f"{n} rows: oracle int8 head (f64 accumulate, OpenMP over vocab rows) + oracle sampler, "
+                      f"{dt:.1f} s"}
+
+
+# ---------------------------------------------------------------------------------------------
 # CPU legs (the oracle: a restatement of the reference's CPU path; the reference itself is
 # TypeScript and cannot run on this box)
 
@@ -522,9 +708,11 @@ def main():
     ap.add_argument("--impl", choices=["enx", "reference"], default="enx")
     ap.add_argument("--cpu-budget", type=float, default=15.0)
     ap.add_argument("--no-cpu-baseline", action="store_true")
-    ap.add_argument("--workload", choices=["config0", "config4"], default="config0",
-                    help="config0: greedy batch-1 decode (the headline); config4: batched sampled decode")
-    ap.add_argument("--batch", type=int, default=256, help="config4: total sequences over all GPUs")
+    ap.add_argument("--workload", choices=["config0", "config2", "config4"], default="config0",
+                    help="config0: greedy batch-1 decode (the headline); config2: vocab-sharded LM head + "
+                         "sampling; config4: batched sampled decode")
+    ap.add_argument("--batch", type=int, default=256,
+                    help="config4: total sequences over all GPUs; config2: rows per step (default 64)")
     args = ap.parse_args()
     if args.warmup < 3:
         raise SystemExit("--warmup must be at least 3")
@@ -543,7 +731,9 @@ def main():
         torch.cuda.set_device(local_rank)
         dist.init_process_group("nccl", device_id=torch.device("cuda", local_rank))
     try:
-        if args.workload == "config4":
+        if args.workload == "config2":
+            run_head(args, rank, world, local_rank)
+        elif args.workload == "config4":
             if args.steps == 2016:
                 args.steps = BATCH_CTX - BATCH_PROMPT
             run_batched(args, rank, world, local_rank)

@@ -114,6 +114,13 @@ SIGNATURES = {
     "enx_step_launches": (C.c_int32, [P, C.POINTER(U32)]),
     "enx_launch_step_kernel": (C.c_int32, [P, U32, U32]),
     "enx_batch_profile": (C.c_int32, [P, U32, C.POINTER(C.c_float), U32]),
+    "enx_shard_state_bytes": (C.c_size_t, [U32]),
+    "enx_shard_prepare": (C.c_int32, [P, U32, U32, U32, U32, P, U32, P, P, P, P]),
+    "enx_shard_probs": (C.c_int32, [P, U32, U32, U32, U32, P, P, P, P, P, P]),
+    "enx_shard_buckets": (C.c_int32, [U32, U32, U32, U32, U32, P, P, P, P, P, P, P]),
+    "enx_shard_kept": (C.c_int32, [U32, U32, U32, U32, U32, P, P, P, P, P, P, P]),
+    "enx_shard_pick": (C.c_int32, [U32, U32, U32, U32, U32, U32, P, P, P, P, P, P]),
+    "enx_shard_finish": (C.c_int32, [U32, U32, U32, P, P, P, P, P, P]),
 }
 
 _lib = None

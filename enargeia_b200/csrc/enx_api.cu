@@ -115,12 +115,21 @@ extern "C" enx_status enx_lm_head_q8(const float* x, const uint32_t* packed, con
                                      const uint32_t* zeros, float* out, const enx_embedding_dims* d,
                                      void* stream) {
     CHECK_ARG(d && x && packed && scales && zeros && out, "enx_lm_head_q8: null pointer");
-    CHECK_ARG(d->seq == 1, "enx_lm_head_q8: seq must be 1 (decode-shaped head)");
     CHECK_ARG(d->block_size == 64 && d->hidden % 64 == 0 && d->blocks_per_row == d->hidden / 64,
               "enx_lm_head_q8: hidden must be a multiple of 64 with block_size 64");
-    if (d->row_count == 0) return ENX_OK;
+    if (d->row_count == 0 || d->seq == 0) return ENX_OK;
+    const uint32_t stride = d->out_stride ? d->out_stride : d->row_count;
+    CHECK_ARG(d->seq == 1 || stride >= d->row_count, "enx_lm_head_q8: out_stride below row_count");
     QW w{packed, scales, zeros, d->row_count, d->hidden};
-    ENX_CUDA(launch_matmul(8, x, w, nullptr, out, 1, d->row_count, d->out_offset, as_stream(stream), false));
+    if (d->seq >= kTcMinTokens) {
+        uint8_t* ws = nullptr;
+        uint32_t* err = nullptr;
+        ENX_TRY(tc_workspace(gemm_tc_workspace_bytes(d->seq, d->hidden), &ws, &err));
+        ENX_CUDA(launch_gemm_tc(8, x, d->hidden, w, nullptr, out, d->seq, stride, d->out_offset, ws, err,
+                                as_stream(stream)));
+        return ENX_OK;
+    }
+    ENX_CUDA(launch_matmul(8, x, w, nullptr, out, d->seq, stride, d->out_offset, as_stream(stream), false));
     return ENX_OK;
 }
 

@@ -49,7 +49,7 @@ __device__ __forceinline__ double pick_d(const double (&a)[MT], int t) {
 }
 
 // ---------------------------------------------------------------------------------------------
-// embedding gather (embed_gather_q8 / _q4, src/kernels/embedding_variants.ts:291-317)
+// embedding gather (embed_gather_q8 / _q4, src/kernels/embedding_variants.ts:100-130)
 
 template <int BITS>
 __global__ void k_embed(const uint32_t* __restrict__ ids, QW table, float* __restrict__ out,

@@ -47,14 +47,14 @@ def matmul_q4(x, packed, scales, zeros, bias, out, m, n, k, out_stride=None, out
 
 
 def lm_head_q8(x, packed, scales, zeros, out, rows, hidden, row_begin=0, out_offset=0, stream=None):
-    """lm_head_q8 (src/kernels/embedding_variants.ts:326-370)."""
+    """lm_head_q8 (src/kernels/embedding_variants.ts:135-180)."""
     d = EmbeddingDims(1, hidden, row_begin, rows, 64, hidden // 64, 0, out_offset, min(rows, 65535), 0, 0, 0)
     call("enx_lm_head_q8", _ptr(x), _u32(packed), _ptr(scales), _u32(zeros), _ptr(out), C.byref(d), _stream(stream))
     return out
 
 
 def embed_gather_q8(ids, packed, scales, zeros, out, hidden, row_begin, row_count, stream=None):
-    """embed_gather_q8 (src/kernels/embedding_variants.ts:291-317)."""
+    """embed_gather_q8 (src/kernels/embedding_variants.ts:100-130)."""
     d = EmbeddingDims(ids.numel(), hidden, row_begin, row_count, 64, hidden // 64, 0, 0, 0, 0, 0, 0)
     call("enx_embed_gather_q8", _u32(ids), _u32(packed), _ptr(scales), _u32(zeros), _ptr(out), C.byref(d),
          _stream(stream))

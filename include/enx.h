@@ -72,7 +72,7 @@ ENX_API enx_status enx_matmul_q4(const float* x, const uint32_t* packed, const f
                          const uint32_t* zeros, const float* bias, float* out,
                          const enx_matmul_q4_dims* dims, void* stream);
 
-/* embeddingDims, 48 bytes (src/kernels/embedding_variants.ts:398-412). */
+/* embeddingDims, 48 bytes (src/kernels/embedding_variants.ts:76-90, 207-221). */
 typedef struct {
     uint32_t seq, hidden, row_begin, row_count;
     uint32_t block_size, blocks_per_row, out_stride, out_offset;
@@ -80,14 +80,17 @@ typedef struct {
 } enx_embedding_dims;
 
 /* Tied LM head over the int8 table: out[col + out_offset] = sum_k x[k] * W[col, k] for
- * col < row_count (lm_head_q8, src/kernels/embedding_variants.ts:326-370).  seq must be 1.
+ * col < row_count (lm_head_q8, src/kernels/embedding_variants.ts:135-180).  `packed`, `scales`
+ * and `zeros` are the rows of this call (a vocab shard passes its own rows).  seq > 1 is this
+ * library's batched extension: row s of x (hidden floats) goes to out + s*out_stride
+ * (out_stride 0 means row_count); from 16 rows it runs on the tensor-core GEMM.
  * Bindings: x, packed, scales, zeros, out, dims. */
 ENX_API enx_status enx_lm_head_q8(const float* x, const uint32_t* packed, const float* scales,
                           const uint32_t* zeros, float* out, const enx_embedding_dims* dims,
                           void* stream);
 
 /* out[s, :] = dequant(table[ids[s] - row_begin, :]) for ids inside [row_begin, row_begin +
- * row_count) (embed_gather_q8, src/kernels/embedding_variants.ts:291-317).  Bindings: ids,
+ * row_count) (embed_gather_q8, src/kernels/embedding_variants.ts:100-130).  Bindings: ids,
  * packed, scales, zeros, out, dims. */
 ENX_API enx_status enx_embed_gather_q8(const uint32_t* ids, const uint32_t* packed, const float* scales,
                                const uint32_t* zeros, float* out, const enx_embedding_dims* dims,
@@ -299,6 +302,48 @@ ENX_API enx_status enx_launch_step_kernel(enx_ctx* ctx, uint32_t batch, uint32_t
  * residual, gate/up GEMMs + SiLU, down GEMM + residual, head GEMM, sampler.  It rewrites the same
  * cache rows and logits.  count must be at least 10. */
 ENX_API enx_status enx_batch_profile(enx_ctx* ctx, uint32_t batch, float* ms, uint32_t count);
+
+/* ------------------------------------------------------------------------------------------
+ * Vocab-sharded sampling (the sampler of src/kernels/sample.wgsl:143-332 over a head split by
+ * contiguous id ranges across GPUs; the reference samples one unsplit vocabulary).
+ *
+ * Rank r of `world` holds logits [rows][n] for ids [row_begin, row_begin + n); ranks' ranges are
+ * in ascending id order.  `split` CTAs per row each own a contiguous part of the shard; a "unit"
+ * is (rank, cta) and units in rank-major order cover the vocabulary in id order.  Each phase
+ * writes a send buffer of one record per (row, cta) - [rows][split] - and the caller allgathers
+ * every rank's send buffer into [world][rows][split] (rank-major: NCCL all_gather_into_tensor)
+ * before the next phase reads it:
+ *   prepare -> cand u32[4]  | probs -> sum f64 | buckets x4 -> bucket f64[256] | kept -> kept f64
+ *   | pick -> pick u32 | finish -> out[rows]
+ * With topp_rounds 0 (no row has top_p < 1) the bucket phases are skipped and kept normalises.
+ * `state` (enx_shard_state_bytes(rows), device) and `probs` (f64 [rows][n], device) stay on the
+ * rank between phases.  Every rank computes the same ids in `out`.  All pointers device.
+ * ---------------------------------------------------------------------------------------- */
+ENX_API size_t enx_shard_state_bytes(uint32_t rows);
+ENX_API enx_status enx_shard_prepare(float* logits, uint32_t n, uint32_t row_begin, uint32_t rows,
+                                     uint32_t split, const uint32_t* history, uint32_t history_stride,
+                                     const uint32_t* history_length, const enx_sampling_row* params,
+                                     uint32_t* cand, void* stream);
+ENX_API enx_status enx_shard_probs(const float* logits, uint32_t n, uint32_t rows, uint32_t split,
+                                   uint32_t world, const enx_sampling_row* params,
+                                   const uint32_t* cand_all, void* state, double* probs, double* sum,
+                                   void* stream);
+ENX_API enx_status enx_shard_buckets(uint32_t n, uint32_t rows, uint32_t split, uint32_t world,
+                                     uint32_t round, const enx_sampling_row* params,
+                                     const double* sum_all, const double* bucket_prev, void* state,
+                                     double* probs, double* bucket, void* stream);
+ENX_API enx_status enx_shard_kept(uint32_t n, uint32_t rows, uint32_t split, uint32_t world,
+                                  uint32_t topp_rounds, const enx_sampling_row* params,
+                                  const double* sum_all, const double* bucket_last, void* state,
+                                  double* probs, double* kept, void* stream);
+ENX_API enx_status enx_shard_pick(uint32_t n, uint32_t row_begin, uint32_t rows, uint32_t split,
+                                  uint32_t world, uint32_t rank, const enx_sampling_row* params,
+                                  const double* kept_all, const void* state, const double* probs,
+                                  uint32_t* pick, void* stream);
+ENX_API enx_status enx_shard_finish(uint32_t rows, uint32_t split, uint32_t world,
+                                    const enx_sampling_row* params, const uint32_t* cand_all,
+                                    const uint32_t* pick_all, const void* state, uint32_t* out,
+                                    void* stream);
 
 #ifdef __cplusplus
 }
