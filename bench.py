@@ -443,6 +443,170 @@ def run_batched(args, rank, world, local_rank):
 
 
 # ---------------------------------------------------------------------------------------------
+# config 1: isolated int4 matvec / GEMM sweep (bench.py --workload config1)
+
+SWEEP_SHAPES = [("q/o", 896, 896), ("k/v", 128, 896), ("gate/up", 4864, 896), ("down", 896, 4864)]  # (n, k)
+SWEEP_M = [1, 8, 64, 256]
+SWEEP_METRIC = "int4 matvec HBM GB/s at M=1 over the projection shapes (q/o, k/v, gate/up, down)"
+L2_BYTES = 126 * 2 ** 20
+
+
+def run_sweep(args, rank, world, local_rank):
+    """One launch = enx_matmul_q4 over one projection shape at M tokens: CUDA-core matvec for
+    M < 16, the tcgen05 exact-limb GEMM from 16.  Each case cycles through enough copies of its
+    weights to exceed twice the L2, so every launch reads its weights from HBM.  N > 1 runs the
+    same sweep on every GPU (independent replicas)."""
+    import torch
+    import torch.distributed as dist
+
+    from enargeia_b200 import build, kernels as K
+    from enargeia_b200.format import quantize_tensor
+    from enargeia_b200._lib import MatmulQ4Dims, call
+    import ctypes as C
+
+    build.build()
+    torch.cuda.set_device(local_rank)
+    dev = torch.device("cuda", local_rank)
+    stream = torch.cuda.current_stream()
+    peaks = {}
+    try:
+        peaks = json.loads((ROOT / "MEASURED_PEAKS.json").read_text())
+    except (OSError, ValueError):
+        pass
+    hbm = float(peaks.get("hbm_gbs", 6650.0))
+    peak_src = "measured" if "hbm_gbs" in peaks else "fallback"
+    bf16 = float(peaks.get("bf16_tflops", 1590.0))
+    i8_peak = 2 * bf16  # dense int8 tensor ops/s: twice the measured dense bf16 rate (the nominal ratio)
+
+    def max_over_ranks(x):
+        if world == 1:
+            return x
+        t = torch.tensor([x], dtype=torch.float64, device=dev)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        return float(t.item())
+
+    shapes = SWEEP_SHAPES
+    ms_list = SWEEP_M
+    if args.case:
+        n_, k_, m_ = (int(v) for v in args.case.split(","))
+        shapes, ms_list = [("case", n_, k_)], [m_]
+    rng = np.random.default_rng(SEED + 1)
+    cases = []
+    for name, n, k in shapes:
+        t = quantize_tensor(name, rng.standard_normal((n, k), dtype=np.float32) * np.float32(0.02), 4)
+        wbytes = t.nbytes
+        copies = 1 if args.case else max(2, int(np.ceil(2 * L2_BYTES / wbytes)))
+        packed = K.to_device_u32(t.packed)
+        scales = torch.from_numpy(t.scales).to(dev)
+        zeros = K.to_device_u32(t.zeros)
+        ws = [(packed.clone(), scales.clone(), zeros.clone()) for _ in range(copies)]
+        for m in ms_list:
+            x = torch.from_numpy(rng.standard_normal((m, k)).astype(np.float32)).to(dev)
+            out = torch.empty(m * n, dtype=torch.float32, device=dev)
+            d = MatmulQ4Dims(m, n, k, 0, 64, k // 64, n, 0, min(n, 65535), 0, 0, 0)
+            s = C.c_void_p(stream.cuda_stream)
+
+            def launch(i, x=x, out=out, d=d, s=s, ws=ws):
+                p_, sc_, z_ = ws[i % len(ws)]
+                call("enx_matmul_q4", C.c_void_p(x.data_ptr()), C.c_void_p(p_.data_ptr()),
+                     C.c_void_p(sc_.data_ptr()), C.c_void_p(z_.data_ptr()), None, C.c_void_p(out.data_ptr()),
+                     C.byref(d), s)
+
+            reps = 3 if args.case else max(args.steps, len(ws))
+            for i in range(args.warmup):
+                launch(i)
+            torch.cuda.synchronize()
+            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            if args.case:  # a few eager launches (profiling)
+                e0.record(stream)
+                for i in range(reps):
+                    launch(i)
+                e1.record(stream)
+            else:  # the launches captured in one CUDA graph: device time, not Python launch time
+                g = torch.cuda.CUDAGraph()
+                with torch.cuda.graph(g):
+                    cs = torch.cuda.current_stream()
+                    sc = C.c_void_p(cs.cuda_stream)
+                    for i in range(reps):
+                        launch(i, s=sc)
+                g.replay()
+                torch.cuda.synchronize()
+                e0.record(stream)
+                g.replay()
+                e1.record(stream)
+            torch.cuda.synchronize()
+            us = max_over_ranks(e0.elapsed_time(e1)) / reps * 1e3
+            if not args.case:
+                del g
+            # e2e through the C ABI with host buffers: x in from pinned memory, y back, per launch
+            xh = x.cpu().pin_memory()
+            yh = torch.empty(m * n, dtype=torch.float32).pin_memory()
+            e2e_reps = 3 if args.case else min(reps, 50)
+            e0.record(stream)
+            for i in range(e2e_reps):
+                x.copy_(xh, non_blocking=True)
+                launch(i)
+                yh.copy_(out, non_blocking=True)
+            e1.record(stream)
+            torch.cuda.synchronize()
+            e2e_us = max_over_ranks(e0.elapsed_time(e1)) / e2e_reps * 1e3
+            io = m * k * 4 + m * n * 4
+            gbs = (wbytes + io) / (us / 1e6) / 1e9
+            tc = m >= 16
+            c = {"shape": name, "n": n, "k": k, "m": m, "path": "tcgen05 limb GEMM" if tc else "CUDA-core matvec",
+                 "us": round(us, 3), "hbm_gbs": round(gbs, 1), "hbm_frac": round(gbs / hbm, 4),
+                 "weight_bytes": wbytes, "e2e_us": round(e2e_us, 3), "launches": 2 if tc else 1}
+            if tc:
+                groups = -(-m // 32)
+                mma_ops = 2 * (-(-n // 128) * 128) * groups * 256 * k  # issued int8 MMA ops (8 limbs x 32 tokens)
+                c["useful_tflops"] = round(2 * m * n * k / (us / 1e6) / 1e12, 2)
+                c["int8_mma_tops"] = round(mma_ops / (us / 1e6) / 1e12, 1)
+                c["tensor_frac_of_int8_peak"] = round(mma_ops / (us / 1e6) / 1e12 / i8_peak, 4)
+            cases.append(c)
+            del out, x
+        del ws
+    m1 = [c for c in cases if c["m"] == 1]
+    base = m1 if m1 else cases
+    tot_bytes = sum(c["weight_bytes"] + c["m"] * (c["k"] + c["n"]) * 4 for c in base)
+    tot_us = sum(c["us"] for c in base)
+    tot_e2e = sum(c["e2e_us"] for c in base)
+    value = tot_bytes / (tot_us / 1e6) / 1e9
+    top = max(base, key=lambda c: c["weight_bytes"])
+    out = {
+        "metric": SWEEP_METRIC,
+        "value": round(value * world, 1),
+        "unit": "GB/s",
+        "n_gpus": world,
+        "steps": args.steps,
+        "warmup": args.warmup,
+        "ms_per_step": round(tot_us / 1e3, 5),
+        "higher_is_better": True,
+        "scaling": "weak",
+        "vs_baseline": None,
+        "dtype": "int4 weights x f32 activations (f64 accumulate)",
+        "data": "synthetic: seeded int4-quantised normal(0,0.02) weights, activations N(0,1)",
+        "config": {"workload": "config 1: int4 matvec/GEMM sweep over the projection shapes, M in {1, 8, 64, 256}",
+                   "parallelism": f"replicas x{world}",
+                   "l2": "weights cycled over copies totalling > 2x the 126 MB L2 (every launch reads HBM)",
+                   "step": "one launch of each projection shape at M=1"},
+        "e2e": {"value": round(tot_bytes / (tot_e2e / 1e6) / 1e9 * world, 1), "unit": "GB/s",
+                "h2d_bytes_per_step": sum(c["m"] * c["k"] * 4 for c in base),
+                "d2h_bytes_per_step": sum(c["m"] * c["n"] * 4 for c in base),
+                "api": "enx_matmul_q4 with x copied in from pinned host memory and y copied back per launch"},
+        "roofline": {"kernel": f"enx_matmul_q4 M=1 {top['shape']} ({top['n']}x{top['k']})", "bound": "hbm",
+                     "achieved": top["hbm_gbs"], "peak": hbm, "unit": "GB/s", "frac": top["hbm_frac"],
+                     "traffic": None, "algorithmic_bytes_per_launch": top["weight_bytes"]
+                     + top["m"] * (top["k"] + top["n"]) * 4, "launch_us": top["us"],
+                     "peak_source": f"{peak_src} MEASURED_PEAKS.json hbm_gbs (burst copy)"},
+        "int8_peak_tops": i8_peak,
+        "cases": cases,
+        "gpu_launches": sum(c["launches"] for c in base) * args.steps,
+    }
+    if rank == 0:
+        print(json.dumps(out), flush=True)
+
+
+# ---------------------------------------------------------------------------------------------
 # config 2: tied int8 LM head + sampling, vocab-sharded across GPUs (bench.py --workload config2)
 
 HEAD_VOCAB, HEAD_HIDDEN, HEAD_HIST = 151936, 896, 2048
@@ -708,9 +872,10 @@ def main():
     ap.add_argument("--impl", choices=["enx", "reference"], default="enx")
     ap.add_argument("--cpu-budget", type=float, default=15.0)
     ap.add_argument("--no-cpu-baseline", action="store_true")
-    ap.add_argument("--workload", choices=["config0", "config2", "config4"], default="config0",
-                    help="config0: greedy batch-1 decode (the headline); config2: vocab-sharded LM head + "
-                         "sampling; config4: batched sampled decode")
+    ap.add_argument("--workload", choices=["config0", "config1", "config2", "config4"], default="config0",
+                    help="config0: greedy batch-1 decode (the headline); config1: int4 matvec/GEMM sweep; "
+                         "config2: vocab-sharded LM head + sampling; config4: batched sampled decode")
+    ap.add_argument("--case", default="", help="config1: one case n,k,m with 3 timed launches (profiling)")
     ap.add_argument("--batch", type=int, default=256,
                     help="config4: total sequences over all GPUs; config2: rows per step (default 64)")
     args = ap.parse_args()
@@ -731,7 +896,11 @@ def main():
         torch.cuda.set_device(local_rank)
         dist.init_process_group("nccl", device_id=torch.device("cuda", local_rank))
     try:
-        if args.workload == "config2":
+        if args.workload == "config1":
+            if args.steps == 2016:
+                args.steps = 200
+            run_sweep(args, rank, world, local_rank)
+        elif args.workload == "config2":
             run_head(args, rank, world, local_rank)
         elif args.workload == "config4":
             if args.steps == 2016:

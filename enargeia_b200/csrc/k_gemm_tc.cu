@@ -3,21 +3,30 @@
 //
 // The reference sums these products in double (test/reference/quant.ts:95-112).  Tensor cores
 // cannot multiply doubles, but they can sum integers exactly, so the activations go in as
-// integers: for each token and 64-element quantisation block, x is scaled by a power of two 2^F
-// (F from the block's largest exponent) to a 46-bit integer X = rint(x * 2^F) -- exact unless a
-// value is 2^-22 below the block's largest -- split into six balanced int8 limbs (two more zero
-// limbs pad each token to 8 columns).  One kind::i8 MMA pair per block gives, per (row, token,
-// limb), the exact int32 sum over the block of q * limb.  The epilogue joins the limbs into the
-// exact int64 sum of q * X, takes off z * sum(X), and adds s * 2^-F times that to a double
-// accumulator: one rounding per block where the reference rounds per product.
+// integers: each token's row of x is scaled by a power of two 2^F (F from the row's largest
+// exponent) to 46-bit integers X = rint(x * 2^F) -- exact unless a value is 2^-22 below the row's
+// largest -- split into six balanced int8 limbs (two more zero limbs pad each token to 8 columns).  One kind::i8 MMA pair per block gives, per (row, token,
+// limb), the exact int32 sum over the block of a * limb, where a is the code q (int8, unsigned) or
+// q - z (int4, a signed byte).  The epilogue joins the limbs into the exact int64 sum of a * X,
+// takes off z * sum(X) for int8, and adds s times that to a double accumulator (one rounding per
+// block where the reference rounds per product); 2^-F is applied once at the end, exactly.
 //
-// Layout: a CTA owns 128 weight rows (M = 128 of the MMA) and 32 tokens (N = 8 limbs x 32 = 256).
-// Per 64-element block, all 256 threads unpack the rows' codes into a K-major shared-memory tile
-// (int4: nibbles to bytes, even elements then odd ones -- the limb tile uses the same order), one
-// thread streams the block's limb tile in with a bulk copy, one thread issues the MMAs into one of
-// two TMEM accumulators, and both warpgroups read the other accumulator (tokens 0-15 and 16-31)
-// while the tensor cores work.  Every wait is bounded; on timeout the kernel records an error and
-// returns, having freed its tensor memory.
+// Layout: a CTA owns 128 weight rows (M = 128 of the MMA), 32 tokens (N = 8 limbs x 32 = 256) and
+// a range of 64-element blocks (split-K when the row tiles x token groups do not fill the GPU;
+// the splits' double partials are then summed in split order by a second kernel).  Token groups
+// of a row tile are adjacent in the grid, so they read the tile's codes from L2.
+//
+// Warp roles, synchronised by mbarriers only:
+//   warps 0-7   epilogue: warpgroup wg drains tokens 16wg..16wg+15 of the accumulator the tensor
+//               cores are not writing (thread = row), then releases it;
+//   warp 8      TMEM allocation; lane 0 issues the two MMAs of each block;
+//   warps 9-10  producer: a thread per two rows, fetches the rows' packed codes (and int4 zero
+//               words) four blocks ahead with cp.async, unpacks each block into a K-major
+//               shared-memory tile (int4: nibbles to bytes minus the zero
+//               code, even elements then odd ones -- the limb tile uses the same order); one
+//               thread also streams the block's limb tile in with a bulk copy.
+// Four stages of (codes, limbs), two accumulators of 256 TMEM columns.  Every wait is bounded; on
+// timeout the kernel records an error, every role stops, and the tensor memory is freed.
 
 #include "enx_internal.cuh"
 #include "k_decode.cuh"
@@ -27,7 +36,6 @@ namespace enx {
 
 namespace {
 
-constexpr int kTcThreads = 256;
 constexpr uint32_t kTcRows = 128;     // weight rows per CTA (MMA M)
 constexpr uint32_t kTcTokens = 32;    // tokens per CTA (MMA N = 8 * 32)
 constexpr uint32_t kTcN = 8 * kTcTokens;
@@ -49,19 +57,11 @@ __device__ __forceinline__ uint64_t mdesc(uint32_t addr) {
     return (uint64_t)((addr >> 4) & 0x3FFF) | ((uint64_t)(128 >> 4) << 16) | ((uint64_t)(512 >> 4) << 32) | (1ull << 46);
 }
 
-// Instruction descriptor: s32 accumulate, A u8 (codes), B s8 (limbs), both K-major, N = 256, M = 128.
-constexpr uint32_t kIdesc = (2u << 4) | (0u << 7) | (1u << 10) | ((kTcN >> 3) << 17) | ((kTcRows >> 4) << 24);
-
-__device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity) {
-    for (uint32_t it = 0; it < kTcSpin; ++it) {
-        uint32_t ok;
-        asm volatile("{\n .reg .pred p;\n mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n selp.u32 %0, 1, 0, p;\n}\n"
-                     : "=r"(ok)
-                     : "r"(su32(bar)), "r"(parity)
-                     : "memory");
-        if (ok) return true;
-    }
-    return false;
+// Instruction descriptor: s32 accumulate, B s8 (limbs), both K-major, N = 256, M = 128; A is u8
+// (int8 codes q) or s8 (int4: q - z, which fits a signed byte).
+template <int BITS>
+__host__ __device__ constexpr uint32_t idesc() {
+    return (2u << 4) | ((BITS == 4 ? 1u : 0u) << 7) | (1u << 10) | ((kTcN >> 3) << 17) | ((kTcRows >> 4) << 24);
 }
 
 // Element order inside a 64-element block for int4 codes: slot j < 32 holds element 8(j/4)+2(j%4),
@@ -73,86 +73,202 @@ __host__ __device__ __forceinline__ uint32_t slot_element(int bits, uint32_t j) 
 
 }  // namespace
 
-// Per (token group, block): the 256 x 64 limb tile (canonical layout, rows token*8 + limb), then
-// per token the exact block sum of X (int64) and 2^-F (double).
+// Limb tiles: per (token group, block) the 256 x 64 limb tile (canonical layout, rows token*8 +
+// limb), then per token the exact block sum of X (int64) and 2^-F (double).  F is per token, from
+// the largest |x| of the token's whole row, so the tensor-core epilogue applies 2^-F once at the
+// end.  A warp per token and chunk of kLimbChunk blocks: the row maximum, then per block two slots
+// per lane, limbs staged through shared memory so each lane stores one 16-byte chunk.
+constexpr uint32_t kLimbChunk = 8;
+
 __global__ void __launch_bounds__(256) k_limbs(const float* __restrict__ x, uint32_t ld, uint32_t M, uint32_t K,
                                                int bits, uint8_t* __restrict__ out) {
-    const uint32_t g = blockIdx.y, b = blockIdx.x, nb = K / kBlock;
-    const uint32_t t = threadIdx.x >> 3, part = threadIdx.x & 7;  // token of the group, 8 elements each
-    const uint32_t m = g * kTcTokens + t;
-    uint8_t* tile = out + ((size_t)g * nb + b) * kTcLimbTileBytes;
-    // my 8 slots: part*8 .. part*8+7 of the block's 64 slots
-    float v[8];
+    pdl_launch_dependents();  // the GEMM may start its prologue; it waits for this grid's results
+    __shared__ __align__(16) uint8_t stage[8][8 * 64];
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const uint32_t m = blockIdx.x * 8 + warp, g = m / kTcTokens, t = m % kTcTokens;
+    const uint32_t nb = K / kBlock, b0 = blockIdx.y * kLimbChunk, b1 = min(b0 + kLimbChunk, nb);
+    const bool live = m < M;  // tokens past M fill their tile rows with zero limbs
+    const float* row = x + (size_t)(live ? m : 0) * ld;
     float amax = 0.f;
+    if (live)
+        for (uint32_t k = lane * 4; k < K; k += 128) {
+            const float4 v = *reinterpret_cast<const float4*>(row + k);
+            amax = fmaxf(amax, fmaxf(fmaxf(fabsf(v.x), fabsf(v.y)), fmaxf(fabsf(v.z), fabsf(v.w))));
+        }
 #pragma unroll
-    for (int i = 0; i < 8; ++i) {
-        const uint32_t e = slot_element(bits, part * 8 + i);
-        v[i] = m < M ? x[(size_t)m * ld + (size_t)b * kBlock + e] : 0.f;
-        amax = fmaxf(amax, fabsf(v[i]));
-    }
-#pragma unroll
-    for (int o = 1; o < 8; o <<= 1) amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, o));
-    // |x| < 2^e for the block's largest |x| (normal or zero); F = 46 - e keeps |X| < 2^46
+    for (int o = 16; o > 0; o >>= 1) amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, o));
+    // |x| < 2^e for the row's largest |x| (normal or zero); F = 46 - e keeps |X| < 2^46
     const int e = amax == 0.f ? 0 : (int)((__float_as_uint(amax) >> 23) & 0xFF) - 126;
     const int F = 46 - e;
     const double up = __hiloint2double((1023 + F) << 20, 0);
-    long long X[8], sum = 0;
+    const uint32_t s0 = slot_element(bits, 2 * lane), s1 = slot_element(bits, 2 * lane + 1);
+    float v[kLimbChunk][2];
 #pragma unroll
-    for (int i = 0; i < 8; ++i) {
-        X[i] = __double2ll_rn((double)v[i] * up);
-        sum += X[i];
+    for (uint32_t j = 0; j < kLimbChunk; ++j) {
+        const uint32_t b = b0 + j;
+        v[j][0] = live && b < b1 ? row[(size_t)b * kBlock + s0] : 0.f;
+        v[j][1] = live && b < b1 ? row[(size_t)b * kBlock + s1] : 0.f;
     }
+    uint8_t* st = stage[warp];
 #pragma unroll
-    for (int o = 1; o < 8; o <<= 1) sum += __shfl_xor_sync(0xffffffffu, sum, o);
-    // balanced base-256 digits: digit l of X is byte l of X + 0x808080808080, minus 128
+    for (uint32_t j = 0; j < kLimbChunk; ++j) {
+        const uint32_t b = b0 + j;
+        if (b >= b1) break;
+        uint8_t* tile = out + ((size_t)g * nb + b) * kTcLimbTileBytes;
+        const long long X0 = __double2ll_rn((double)v[j][0] * up), X1 = __double2ll_rn((double)v[j][1] * up);
+        long long sum = X0 + X1;
 #pragma unroll
-    for (uint32_t l = 0; l < 8; ++l) {
-        uint32_t w0 = 0, w1 = 0;
+        for (int o = 16; o > 0; o >>= 1) sum += __shfl_xor_sync(0xffffffffu, sum, o);
+        // balanced base-256 digits: digit l of X is byte l of X + 0x808080808080, minus 128
+        const unsigned long long u0 = (unsigned long long)(X0 + 0x808080808080LL);
+        const unsigned long long u1 = (unsigned long long)(X1 + 0x808080808080LL);
 #pragma unroll
-        for (int i = 0; i < 8; ++i) {
-            const uint32_t d = l < 6 ? (uint32_t)(((unsigned long long)(X[i] + 0x808080808080LL) >> (8 * l)) & 0xFF) - 128u : 0u;
-            if (i < 4) w0 |= (d & 0xFFu) << (8 * i);
-            else w1 |= (d & 0xFFu) << (8 * (i - 4));
+        for (uint32_t l = 0; l < 8; ++l) {
+            const uint32_t d0 = l < 6 ? (uint32_t)((u0 >> (8 * l)) & 0xFF) - 128u : 0u;
+            const uint32_t d1 = l < 6 ? (uint32_t)((u1 >> (8 * l)) & 0xFF) - 128u : 0u;
+            *reinterpret_cast<uint16_t*>(st + l * 64 + 2 * lane) = (uint16_t)((d0 & 0xFFu) | ((d1 & 0xFFu) << 8));
         }
-        uint2* dst = reinterpret_cast<uint2*>(tile + canon(t * 8 + l, part * 8));
-        *dst = make_uint2(w0, w1);
+        __syncwarp();
+        {
+            const uint32_t l = lane >> 2, c = lane & 3;  // lane stores chunk c of limb row l
+            *reinterpret_cast<uint4*>(tile + canon(t * 8 + l, c * 16)) = *reinterpret_cast<const uint4*>(st + l * 64 + c * 16);
+        }
+        if (lane == 0) {
+            long long* rec = reinterpret_cast<long long*>(tile + kTcN * 64);
+            rec[2 * t] = sum;
+            reinterpret_cast<double*>(rec)[2 * t + 1] = __hiloint2double((1023 - F) << 20, 0);
+        }
+        __syncwarp();
     }
-    if (part == 0) {
-        long long* xs = reinterpret_cast<long long*>(tile + kTcN * 64);
-        xs[2 * t] = sum;
-        reinterpret_cast<double*>(xs)[2 * t + 1] = __hiloint2double((1023 - F) << 20, 0);
+}
+
+constexpr uint32_t kTcStages = 4;
+constexpr int kTcEpiWarps = 8, kTcMmaWarp = 8, kTcProdWarp0 = 9;
+constexpr int kTcProdWarps = 2;                          // producer: 64 threads, two rows each
+constexpr int kTcWsThreads = (kTcEpiWarps + 1 + kTcProdWarps) * 32;  // 352: at most 3 warps per SMSP
+constexpr uint32_t kTcATile = kTcRows * 64;               // 8 KB of codes per block
+constexpr uint32_t kTcMaxSplit = 16;
+
+// Bounded wait on an mbarrier phase that gives up early when another role has failed.
+__device__ __forceinline__ bool mbar_wait_f(uint64_t* bar, uint32_t parity, volatile int* fail, uint32_t* err) {
+    for (uint32_t it = 0; it < kTcSpin; ++it) {
+        uint32_t ok;
+        asm volatile("{\n .reg .pred p;\n mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n selp.u32 %0, 1, 0, p;\n}\n"
+                     : "=r"(ok)
+                     : "r"(su32(bar)), "r"(parity)
+                     : "memory");
+        if (ok) return true;
+        if ((it & 31) == 31 && *fail) return false;
+    }
+    atomicMax(err, 3u);
+    *fail = 1;
+    return false;
+}
+
+__device__ __forceinline__ void mbar_arrive(uint64_t* bar) {
+    asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(su32(bar)) : "memory");
+}
+
+// Raw ring: the packed codes of one block for the CTA's 128 rows as stored (row-major, 32 or 64
+// bytes per row) and, for int4, each row's zero-point word; fetched with cp.async kTcRaw blocks
+// ahead of their unpacking.  A producer thread only ever reads back bytes it copied itself.
+constexpr uint32_t kTcRaw = 4;
+template <int BITS>
+struct RawGeom {
+    static constexpr uint32_t kRowBytes = 2 * BITS * 4;           // 32 (int4) or 64 (int8)
+    static constexpr uint32_t kCodes = kTcRows * kRowBytes;       // per block
+    static constexpr uint32_t kBytes = kCodes + kTcRows * 4;      // + zero words
+};
+
+__device__ __forceinline__ void cp_async16(void* dst, const void* src, bool ok) {
+    asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;" ::"r"(su32(dst)), "l"(src), "r"(ok ? 16 : 0)
+                 : "memory");
+}
+__device__ __forceinline__ void cp_async4(void* dst, const void* src, bool ok) {
+    asm volatile("cp.async.ca.shared.global [%0], [%1], 4, %2;" ::"r"(su32(dst)), "l"(src), "r"(ok ? 4 : 0)
+                 : "memory");
+}
+
+// Copies row `row`'s codes (and int4 zero word) of block b into raw slot `raw`.
+template <int BITS>
+__device__ __forceinline__ void fetch_row(uint8_t* raw, const QW& w, uint32_t r0, uint32_t row, uint32_t b) {
+    using G = RawGeom<BITS>;
+    const uint32_t K = w.cols, gr = r0 + row;
+    const bool ok = gr < w.rows;
+    const uint8_t* src = reinterpret_cast<const uint8_t*>(w.packed) + ((size_t)(ok ? gr : 0) * (K * BITS / 8)) +
+                         (size_t)b * G::kRowBytes;
+#pragma unroll
+    for (uint32_t c = 0; c < G::kRowBytes / 16; ++c) cp_async16(raw + row * G::kRowBytes + c * 16, src + c * 16, ok);
+    if (BITS == 4) {
+        const uint32_t blk = (ok ? gr : 0) * (K / kBlock) + b;
+        cp_async4(raw + G::kCodes + row * 4, w.zeros + (blk >> 3), ok);
+    }
+}
+
+// Unpacks row `row` of raw slot `raw` (block b) into the K-major canonical code tile.
+template <int BITS>
+__device__ __forceinline__ void unpack_row(const uint8_t* raw, uint8_t* tile, uint32_t row, uint32_t blk) {
+    using G = RawGeom<BITS>;
+    const uint4* q = reinterpret_cast<const uint4*>(raw + row * G::kRowBytes);
+    if (BITS == 4) {
+        // zero code of (row, block): nibble blk & 7 of the zero word fetched for it (blk = the
+        // row's block index gr * K/64 + b)
+        const uint32_t z = (*reinterpret_cast<const uint32_t*>(raw + G::kCodes + row * 4) >> ((blk & 7u) * 4u)) & 0xFu;
+        const uint32_t zz = z * 0x01010101u;
+#pragma unroll
+        for (int h = 0; h < 2; ++h) {  // words 4h..4h+3: low nibbles to k-bytes 16h.., high to 32+16h..
+            const uint4 v = q[h];
+            const uint32_t ww[4] = {v.x, v.y, v.z, v.w};
+            uint32_t lo[4], hi[4];
+#pragma unroll
+            for (int i = 0; i < 4; ++i) {  // q - z per byte: a signed byte in [-15, 15]
+                lo[i] = __vsub4(ww[i] & 0x0F0F0F0Fu, zz);
+                hi[i] = __vsub4((ww[i] >> 4) & 0x0F0F0F0Fu, zz);
+            }
+            *reinterpret_cast<uint4*>(tile + canon(row, h * 16)) = make_uint4(lo[0], lo[1], lo[2], lo[3]);
+            *reinterpret_cast<uint4*>(tile + canon(row, 32 + h * 16)) = make_uint4(hi[0], hi[1], hi[2], hi[3]);
+        }
+    } else {
+#pragma unroll
+        for (int i = 0; i < 4; ++i) *reinterpret_cast<uint4*>(tile + canon(row, i * 16)) = q[i];
     }
 }
 
 template <int BITS>
-__global__ void __launch_bounds__(kTcThreads, 1)
+__global__ void __launch_bounds__(kTcWsThreads, 1)
     k_gemm_tc(const uint8_t* __restrict__ limbs, QW w, const float* __restrict__ bias, float* __restrict__ out,
-              uint32_t M, uint32_t out_stride, uint32_t out_offset, uint32_t* err) {
-    constexpr uint32_t kATile = kTcRows * 64;  // 8 KB of codes per block
+              double* __restrict__ partial, uint32_t M, uint32_t out_stride, uint32_t out_offset, uint32_t blocks_per_split,
+              uint32_t* err) {
     extern __shared__ __align__(1024) uint8_t smem[];
-    constexpr uint32_t kSt = 3;                           // stages of codes and limb tiles
-    uint8_t* sA = smem;                                   // [3][kATile]
-    uint8_t* sB = smem + kSt * kATile;                    // [3][kTcLimbTileBytes]
-    float* sS = reinterpret_cast<float*>(sB + kSt * kTcLimbTileBytes);  // [3][128] scales
-    uint32_t* sZ = reinterpret_cast<uint32_t*>(sS + kSt * kTcRows);     // [3][128] zero codes
-    __shared__ __align__(8) uint64_t bar_b[kSt], bar_d[2];
+    uint8_t* sA = smem;                                // [stages][kTcATile]
+    uint8_t* sB = smem + kTcStages * kTcATile;         // [stages][kTcLimbTileBytes]
+    uint8_t* sR = sB + kTcStages * kTcLimbTileBytes;   // [kTcRaw][RawGeom::kBytes]
+    __shared__ __align__(8) uint64_t full[kTcStages], empty[kTcStages], accf[2], acce[2];
     __shared__ uint32_t tmem_base;
     __shared__ volatile int s_fail;
 
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
     const uint32_t K = w.cols, nb = K / kBlock, bpr = K / kBlock;
-    const uint32_t r0 = blockIdx.x * kTcRows, g = blockIdx.y;
+    const uint32_t g = blockIdx.x, r0 = blockIdx.y * kTcRows;
+    const uint32_t kb0 = blockIdx.z * blocks_per_split, kb1 = min(kb0 + blocks_per_split, nb);
+    const uint32_t nblk = kb1 > kb0 ? kb1 - kb0 : 0;
     const uint8_t* ltile = limbs + (size_t)g * nb * kTcLimbTileBytes;
 
-    if (warp == 0) {
+    if (warp == kTcMmaWarp) {
         asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(su32(&tmem_base)),
                      "r"(kTcTmemCols));
         asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;");
     }
     if (tid == 0) {
         s_fail = 0;
-        for (uint32_t i = 0; i < kSt; ++i) asm volatile("mbarrier.init.shared::cta.b64 [%0], 1;" ::"r"(su32(&bar_b[i])));
-        for (int i = 0; i < 2; ++i) asm volatile("mbarrier.init.shared::cta.b64 [%0], 1;" ::"r"(su32(&bar_d[i])));
+        for (uint32_t i = 0; i < kTcStages; ++i) {
+            asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(su32(&full[i])), "r"(kTcProdWarps * 32));
+            asm volatile("mbarrier.init.shared::cta.b64 [%0], 1;" ::"r"(su32(&empty[i])));
+        }
+        for (int i = 0; i < 2; ++i) {
+            asm volatile("mbarrier.init.shared::cta.b64 [%0], 1;" ::"r"(su32(&accf[i])));
+            asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(su32(&acce[i])), "r"(kTcEpiWarps));
+        }
         asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
     }
     asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
@@ -160,151 +276,261 @@ __global__ void __launch_bounds__(kTcThreads, 1)
     asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
     const uint32_t tmem = tmem_base;
 
-    // epilogue role: warpgroup wg takes tokens wg*16 .. wg*16+15 of rows 32*(warp%4) + lane
-    const uint32_t wg = warp >> 2, erow = 32 * (warp & 3) + lane, grow = r0 + erow;
-    double acc[16];
-#pragma unroll
-    for (int i = 0; i < 16; ++i) acc[i] = 0.0;
-
-    auto issue_b = [&](uint32_t b) {  // one thread: the block's limb tile into stage b % 3
-        const uint32_t s = b % kSt;
-        asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(su32(&bar_b[s])), "r"(kTcLimbTileBytes)
-                     : "memory");
-        asm volatile("cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(
-                         su32(sB + s * kTcLimbTileBytes)),
-                     "l"(ltile + (size_t)b * kTcLimbTileBytes), "r"(kTcLimbTileBytes), "r"(su32(&bar_b[s]))
-                     : "memory");
-    };
-    if (tid == 0) issue_b(0);
-
-    // Block b: codes and limbs in stage b % 3, accumulator b & 1.  Stage (b + 1) % 3 last held
-    // block b - 2, whose MMA finished (waited in iteration b - 1) and whose epilogue ran in
-    // iteration b - 1, so the limb copy for b + 1 may start right after the MMA of b.
-    for (uint32_t b = 0; b <= nb; ++b) {
-        const uint32_t s = b % kSt;
-        if (b < nb) {
-            // codes of block b into stage s: two threads per row, 32 elements each
-            const uint32_t row = tid >> 1, half = tid & 1, gr = r0 + row;
-            if (BITS == 4) {
-                uint4 q = make_uint4(0, 0, 0, 0);
-                if (gr < w.rows) q = __ldg(reinterpret_cast<const uint4*>(w.packed + (size_t)gr * (K / 8) + b * 8 + half * 4));
-                const uint32_t ww[4] = {q.x, q.y, q.z, q.w};
-                uint32_t lo[4], hi[4];
-#pragma unroll
-                for (int i = 0; i < 4; ++i) {
-                    lo[i] = ww[i] & 0x0F0F0F0Fu;
-                    hi[i] = (ww[i] >> 4) & 0x0F0F0F0Fu;
-                }
-                // slots: lo of words 0..7 fill k-bytes 0..31, hi fill 32..63
-                *reinterpret_cast<uint4*>(sA + s * kATile + canon(row, half * 16)) = make_uint4(lo[0], lo[1], lo[2], lo[3]);
-                *reinterpret_cast<uint4*>(sA + s * kATile + canon(row, 32 + half * 16)) = make_uint4(hi[0], hi[1], hi[2], hi[3]);
-            } else {
-                uint4 q0 = make_uint4(0, 0, 0, 0), q1 = q0;
-                if (gr < w.rows) {
-                    const uint4* p = reinterpret_cast<const uint4*>(w.packed + (size_t)gr * (K / 4) + b * 16 + half * 8);
-                    q0 = __ldg(p);
-                    q1 = __ldg(p + 1);
-                }
-                *reinterpret_cast<uint4*>(sA + s * kATile + canon(row, half * 32)) = q0;
-                *reinterpret_cast<uint4*>(sA + s * kATile + canon(row, half * 32 + 16)) = q1;
+    if (warp >= kTcProdWarp0) {
+        // ---- producer: thread = rows p and p + 64 ---------------------------------------------------
+        using G = RawGeom<BITS>;
+        const uint32_t p = tid - kTcProdWarp0 * 32;
+        for (uint32_t j = 0; j < kTcRaw; ++j) {  // prologue: blocks 0..kTcRaw-1 in flight
+            if (j < nblk) {
+                fetch_row<BITS>(sR + j * G::kBytes, w, r0, p, kb0 + j);
+                fetch_row<BITS>(sR + j * G::kBytes, w, r0, p + 64, kb0 + j);
             }
-            if (half == 0) {
-                const uint32_t blk = gr * bpr + b;
-                sS[s * kTcRows + row] = gr < w.rows ? __ldg(w.scales + blk) : 0.f;
-                sZ[s * kTcRows + row] = gr < w.rows ? zero_code<BITS>(w.zeros, blk) : 0u;
-            }
-            asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+            asm volatile("cp.async.commit_group;" ::: "memory");
         }
-        asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
-        __syncthreads();  // codes written; the previous epilogue is done with its accumulator
-        asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
-        if (tid == 0 && b < nb) {
-            if (!mbar_wait(&bar_b[s], (b / kSt) & 1)) {
-                atomicMax(err, 3u);
-                s_fail = 1;
-            } else {
-                const uint32_t dcol = tmem + (b & 1) * kTcN;
+        pdl_wait();  // the limb tiles (previous grid) are complete from here on
+        for (uint32_t i = 0; i < nblk; ++i) {
+            const uint32_t s = i % kTcStages, rs = i % kTcRaw;
+            if (i >= kTcStages && !mbar_wait_f(&empty[s], ((i / kTcStages) - 1) & 1, &s_fail, err)) break;
+            if (p == 0) {
+                asm volatile("mbarrier.expect_tx.relaxed.cta.shared::cta.b64 [%0], %1;" ::"r"(su32(&full[s])),
+                             "r"(kTcLimbTileBytes)
+                             : "memory");
+                asm volatile("cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(
+                                 su32(sB + s * kTcLimbTileBytes)),
+                             "l"(ltile + (size_t)(kb0 + i) * kTcLimbTileBytes), "r"(kTcLimbTileBytes), "r"(su32(&full[s]))
+                             : "memory");
+            }
+            asm volatile("cp.async.wait_group %0;" ::"n"(kTcRaw - 1) : "memory");  // block i's raw codes landed
+            // unpack_row takes the (row, block) index: its low 3 bits pick the int4 zero nibble
+            unpack_row<BITS>(sR + rs * G::kBytes, sA + s * kTcATile, p, (r0 + p) * bpr + kb0 + i);
+            unpack_row<BITS>(sR + rs * G::kBytes, sA + s * kTcATile, p + 64, (r0 + p + 64) * bpr + kb0 + i);
+            asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+            mbar_arrive(&full[s]);
+            if (i + kTcRaw < nblk) {  // refill the slot this thread just read
+                fetch_row<BITS>(sR + rs * G::kBytes, w, r0, p, kb0 + i + kTcRaw);
+                fetch_row<BITS>(sR + rs * G::kBytes, w, r0, p + 64, kb0 + i + kTcRaw);
+            }
+            asm volatile("cp.async.commit_group;" ::: "memory");
+        }
+        asm volatile("cp.async.wait_all;" ::: "memory");
+    } else if (warp == kTcMmaWarp) {
+        // ---- MMA issue: one thread ----------------------------------------------------------------
+        pdl_wait();
+        if (lane == 0) {
+            for (uint32_t i = 0; i < nblk; ++i) {
+                const uint32_t s = i % kTcStages, a = i & 1;
+                if (!mbar_wait_f(&full[s], (i / kTcStages) & 1, &s_fail, err)) break;
+                if (i >= 2 && !mbar_wait_f(&acce[a], ((i >> 1) - 1) & 1, &s_fail, err)) break;
+                asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+                const uint32_t dcol = tmem + a * kTcN;
 #pragma unroll
                 for (uint32_t kk = 0; kk < 2; ++kk) {
-                    const uint64_t ad = mdesc(su32(sA + s * kATile) + kk * 256);
+                    const uint64_t ad = mdesc(su32(sA + s * kTcATile) + kk * 256);
                     const uint64_t bd = mdesc(su32(sB + s * kTcLimbTileBytes) + kk * 256);
                     asm volatile("{\n .reg .pred p;\n setp.ne.b32 p, %4, 0;\n tcgen05.mma.cta_group::1.kind::i8 [%0], %1, %2, %3, p;\n}\n" ::"r"(
                                      dcol),
-                                 "l"(ad), "l"(bd), "r"(kIdesc), "r"(kk));
+                                 "l"(ad), "l"(bd), "r"(idesc<BITS>()), "r"(kk));
                 }
                 asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(
-                                 su32(&bar_d[b & 1]))
+                                 su32(&empty[s]))
                              : "memory");
-                if (b + 1 < nb) issue_b(b + 1);
+                asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(
+                                 su32(&accf[a]))
+                             : "memory");
             }
         }
-        if (b == 0) continue;
-        // epilogue of block b-1 from accumulator (b-1) & 1 (its scales and sums in stage (b-1) % 3)
-        const uint32_t pb = b - 1, ps = pb & 1, pst = pb % kSt;
-        if (tid == 0 && !s_fail && !mbar_wait(&bar_d[ps], (pb >> 1) & 1)) {
-            atomicMax(err, 3u);
-            s_fail = 1;
-        }
-        __syncthreads();
-        if (s_fail) break;
-        asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
-        {
-            const double sc = (double)sS[pst * kTcRows + erow];
-            const long long zc = (long long)sZ[pst * kTcRows + erow];
-            const long long* xs = reinterpret_cast<const long long*>(sB + pst * kTcLimbTileBytes + kTcN * 64);
+        __syncwarp();
+    } else {
+        // ---- epilogue: warpgroup wg, tokens 16wg..16wg+15, thread = row 32*(warp%4) + lane ---------
+        pdl_wait();  // limb records and the output may be touched from here on
+        const uint32_t wg = warp >> 2, erow = 32 * (warp & 3) + lane, grow = r0 + erow;
+        const bool rok = grow < w.rows;
+        double acc[16];
 #pragma unroll
-            for (int tt = 0; tt < 16; ++tt) {
-                const uint32_t t = wg * 16 + tt;
-                uint32_t d[8];
-                const uint32_t ta = tmem + ((uint32_t)(32 * (warp & 3)) << 16) + ps * kTcN + t * 8;
-                asm volatile("tcgen05.ld.sync.aligned.32x32b.x8.b32 {%0,%1,%2,%3,%4,%5,%6,%7}, [%8];"
-                             : "=r"(d[0]), "=r"(d[1]), "=r"(d[2]), "=r"(d[3]), "=r"(d[4]), "=r"(d[5]), "=r"(d[6]), "=r"(d[7])
-                             : "r"(ta));
+        for (int i = 0; i < 16; ++i) acc[i] = 0.0;
+        float sc_next = (nblk && rok) ? __ldg(w.scales + (size_t)grow * bpr + kb0) : 0.f;
+        uint32_t z_next = (BITS == 8 && nblk && rok) ? zero_code<BITS>(w.zeros, grow * bpr + kb0) : 0u;
+        for (uint32_t i = 0; i < nblk; ++i) {
+            const uint32_t a = i & 1, b = kb0 + i;
+            const double sc = (double)sc_next;
+            const long long zc = (long long)z_next;
+            if (i + 1 < nblk && rok) {  // the next block's scale (and int8 zero code) while this one drains
+                sc_next = __ldg(w.scales + (size_t)grow * bpr + b + 1);
+                if (BITS == 8) z_next = zero_code<BITS>(w.zeros, grow * bpr + b + 1);
+            }
+            int ok = 1;
+            if (lane == 0) ok = mbar_wait_f(&accf[a], (i >> 1) & 1, &s_fail, err);
+            if (!__shfl_sync(0xffffffffu, ok, 0)) break;
+            asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+            // per token of this block (int8 only): the X sum, from the limb tile in global memory
+            const int* tok = reinterpret_cast<const int*>(ltile + (size_t)b * kTcLimbTileBytes + kTcN * 64) +
+                             (wg * 16) * 4;
+            // tokens in groups of kTok (8 for int4, 4 for int8: register pressure), one TMEM wait each
+            constexpr int kTok = BITS == 4 ? 8 : 4, kLd = kTok / 4, kGroups = 16 / kTok;
+#pragma unroll
+            for (int hh = 0; hh < kGroups; ++hh) {
+                uint32_t d[kLd][32];
+#pragma unroll
+                for (int tq = 0; tq < kLd; ++tq) {  // four tokens (32 accumulator columns) per TMEM load
+                    const uint32_t ta =
+                        tmem + ((uint32_t)(32 * (warp & 3)) << 16) + a * kTcN + (wg * 16 + hh * kTok + tq * 4) * 8;
+                    asm volatile(
+                        "tcgen05.ld.sync.aligned.32x32b.x32.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,"
+                        "%16,%17,%18,%19,%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31}, [%32];"
+                        : "=r"(d[tq][0]), "=r"(d[tq][1]), "=r"(d[tq][2]), "=r"(d[tq][3]), "=r"(d[tq][4]),
+                          "=r"(d[tq][5]), "=r"(d[tq][6]), "=r"(d[tq][7]), "=r"(d[tq][8]), "=r"(d[tq][9]),
+                          "=r"(d[tq][10]), "=r"(d[tq][11]), "=r"(d[tq][12]), "=r"(d[tq][13]), "=r"(d[tq][14]),
+                          "=r"(d[tq][15]), "=r"(d[tq][16]), "=r"(d[tq][17]), "=r"(d[tq][18]), "=r"(d[tq][19]),
+                          "=r"(d[tq][20]), "=r"(d[tq][21]), "=r"(d[tq][22]), "=r"(d[tq][23]), "=r"(d[tq][24]),
+                          "=r"(d[tq][25]), "=r"(d[tq][26]), "=r"(d[tq][27]), "=r"(d[tq][28]), "=r"(d[tq][29]),
+                          "=r"(d[tq][30]), "=r"(d[tq][31])
+                        : "r"(ta));
+                }
                 asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
-                long long T = 0;
+                if (hh == kGroups - 1) {  // all 16 tokens are in registers: accumulator a may take block i + 2
+                    asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
+                    __syncwarp();
+                    if (lane == 0) mbar_arrive(&acce[a]);
+                }
 #pragma unroll
-                for (int l = 5; l >= 0; --l) T = T * 256 + (long long)(int)d[l];
-                T -= zc * xs[2 * t];
-                const double down = reinterpret_cast<const double*>(xs)[2 * t + 1];
-                acc[tt] = fma((double)T, sc * down, acc[tt]);
+                for (int j = 0; j < kTok; ++j) {
+                    const int tt = hh * kTok + j;
+                    const int* dl = reinterpret_cast<const int*>(&d[j >> 2][8 * (j & 3)]);
+                    // exact: each pair d_l + 256 d_(l+1) fits 32 bits
+                    const long long a0 = (long long)(dl[0] + dl[1] * 256);
+                    const long long a1 = (long long)(dl[2] + dl[3] * 256);
+                    const long long a2 = (long long)(dl[4] + dl[5] * 256);
+                    long long T = a0 + a1 * 65536LL + a2 * 4294967296LL;
+                    if (BITS == 8) {
+                        const int2 xs = __ldg(reinterpret_cast<const int2*>(tok + 4 * tt));
+                        T -= zc * (((long long)xs.y << 32) | (unsigned)xs.x);
+                    }
+                    acc[tt] = fma((double)T, sc, acc[tt]);
+                }
             }
         }
-    }
-    if (!s_fail && grow < w.rows) {
-        const double bv = bias ? (double)__ldg(bias + grow) : 0.0;
+        if (!s_fail && rok && nblk) {
+            // each token's 2^-F (the same in every block's record), applied once: exact
+            const double* rec = reinterpret_cast<const double*>(ltile + (size_t)kb0 * kTcLimbTileBytes + kTcN * 64);
 #pragma unroll
-        for (int tt = 0; tt < 16; ++tt) {
-            const uint32_t m = g * kTcTokens + wg * 16 + tt;
-            if (m < M) out[(size_t)m * out_stride + out_offset + grow] = (float)(acc[tt] + bv);
+            for (int tt = 0; tt < 16; ++tt) acc[tt] *= __ldg(rec + 2 * (wg * 16 + tt) + 1);
+            if (partial) {  // split-K: this split's double partial, [split][M][rows]
+                double* pp = partial + (size_t)blockIdx.z * M * w.rows;
+#pragma unroll
+                for (int tt = 0; tt < 16; ++tt) {
+                    const uint32_t m = g * kTcTokens + wg * 16 + tt;
+                    if (m < M) pp[(size_t)m * w.rows + grow] = acc[tt];
+                }
+            } else {
+                const double bv = bias ? (double)__ldg(bias + grow) : 0.0;
+#pragma unroll
+                for (int tt = 0; tt < 16; ++tt) {
+                    const uint32_t m = g * kTcTokens + wg * 16 + tt;
+                    if (m < M) out[(size_t)m * out_stride + out_offset + grow] = (float)(acc[tt] + bv);
+                }
+            }
         }
     }
     asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
     __syncthreads();
-    if (warp == 0) asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(kTcTmemCols));
+    asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+    if (warp == kTcMmaWarp)
+        asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(kTcTmemCols));
+}
+
+// Split-K: out = float(sum of the splits' partials in split order + bias).
+__global__ void k_gemm_tc_combine(const double* __restrict__ partial, uint32_t splits, uint32_t M, uint32_t N,
+                                  const float* __restrict__ bias, float* __restrict__ out, uint32_t out_stride,
+                                  uint32_t out_offset) {
+    const size_t i = (size_t)blockIdx.x * blockDim.x + threadIdx.x;
+    if (i >= (size_t)M * N) return;
+    const uint32_t m = (uint32_t)(i / N), n = (uint32_t)(i % N);
+    double acc = 0.0;
+    for (uint32_t s = 0; s < splits; ++s) acc += partial[(size_t)s * M * N + i];
+    if (bias) acc += (double)__ldg(bias + n);
+    out[(size_t)m * out_stride + out_offset + n] = (float)acc;
+}
+
+// Splits of the reduction axis: the count that minimises the modelled time waves(s) * (blocks
+// per split + kTcFixed), waves(s) = ceil(groups * row tiles * s / SMs), at least 2 blocks each.
+constexpr uint32_t kTcFixed = 3;  // per-CTA prologue and flush, in block times
+static uint32_t tc_splits(uint32_t m, uint32_t n, uint32_t k) {
+    const uint32_t groups = (m + kTcTokens - 1) / kTcTokens, tiles = (n + kTcRows - 1) / kTcRows;
+    const uint32_t ctas = groups * tiles, nb = k / kBlock;
+    const uint32_t sms = (uint32_t)num_sms();
+    uint32_t best = 1;
+    uint64_t best_cost = ~0ull;
+    for (uint32_t s = 1; s <= min(kTcMaxSplit, max(1u, nb / 2)); ++s) {
+        const uint32_t per = (nb + s - 1) / s, used = (nb + per - 1) / per;  // no empty splits
+        const uint64_t waves = ((uint64_t)ctas * used + sms - 1) / sms;
+        const uint64_t cost = waves * (per + kTcFixed);
+        if (cost < best_cost) {
+            best_cost = cost;
+            best = used;
+        }
+    }
+    return best;
+}
+
+static size_t limb_bytes(uint32_t m, uint32_t k) {
+    const size_t groups = (m + kTcTokens - 1) / kTcTokens;
+    return (groups * (k / kBlock) * (size_t)kTcLimbTileBytes + 255) / 256 * 256;
+}
+
+// Rows x splits the partial region of a workspace holds; launches that would need more run with
+// fewer splits.
+static size_t partial_rows(uint32_t m) {
+    const size_t groups = (m + kTcTokens - 1) / kTcTokens;
+    return 4 * 148 * (size_t)kTcRows / groups + kTcRows;
 }
 
 size_t gemm_tc_workspace_bytes(uint32_t m, uint32_t k) {
-    const size_t groups = (m + kTcTokens - 1) / kTcTokens;
-    return groups * (k / kBlock) * (size_t)kTcLimbTileBytes;
+    return limb_bytes(m, k) + (size_t)m * partial_rows(m) * sizeof(double) + 256;
 }
 
 cudaError_t launch_gemm_tc(int bits, const float* x, uint32_t ld, const QW& w, const float* bias, float* out,
                            uint32_t m, uint32_t out_stride, uint32_t out_offset, uint8_t* workspace, uint32_t* err,
                            cudaStream_t st) {
     const uint32_t groups = (m + kTcTokens - 1) / kTcTokens, nb = w.cols / kBlock;
-    k_limbs<<<dim3(nb, groups), 256, 0, st>>>(x, ld, m, w.cols, bits, workspace);
+    k_limbs<<<dim3(groups * (kTcTokens / 8), (nb + kLimbChunk - 1) / kLimbChunk), 256, 0, st>>>(x, ld, m, w.cols, bits,
+                                                                                          workspace);
     cudaError_t e = cudaGetLastError();
     if (e != cudaSuccess) return e;
-    const size_t smem = 3 * ((size_t)kTcRows * 64 + (size_t)kTcLimbTileBytes + kTcRows * 4 + kTcRows * 4);
-    const dim3 grid((w.rows + kTcRows - 1) / kTcRows, groups);
+    uint32_t splits = tc_splits(m, w.rows, w.cols);
+    while (splits > 1 && (size_t)splits * w.rows > partial_rows(m)) --splits;  // workspace bound
+    const uint32_t per = (nb + splits - 1) / splits;
+    double* partial = splits > 1 ? reinterpret_cast<double*>(workspace + limb_bytes(m, w.cols)) : nullptr;
+    const size_t smem = (size_t)kTcStages * (kTcATile + kTcLimbTileBytes) +
+                        (size_t)kTcRaw * (bits == 4 ? RawGeom<4>::kBytes : RawGeom<8>::kBytes);
+    const dim3 grid(groups, (w.rows + kTcRows - 1) / kTcRows, splits);
+    // programmatic dependent launch: the prologue and the weight prefetch overlap k_limbs
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = grid;
+    cfg.blockDim = dim3(kTcWsThreads);
+    cfg.dynamicSmemBytes = smem;
+    cfg.stream = st;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
     if (bits == 4) {
         e = cudaFuncSetAttribute(k_gemm_tc<4>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
-        if (e == cudaSuccess) k_gemm_tc<4><<<grid, kTcThreads, smem, st>>>(workspace, w, bias, out, m, out_stride, out_offset, err);
+        if (e == cudaSuccess)
+            e = cudaLaunchKernelEx(&cfg, k_gemm_tc<4>, (const uint8_t*)workspace, w, bias, out, partial, m, out_stride,
+                                   out_offset, per, err);
     } else {
         e = cudaFuncSetAttribute(k_gemm_tc<8>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
-        if (e == cudaSuccess) k_gemm_tc<8><<<grid, kTcThreads, smem, st>>>(workspace, w, bias, out, m, out_stride, out_offset, err);
+        if (e == cudaSuccess)
+            e = cudaLaunchKernelEx(&cfg, k_gemm_tc<8>, (const uint8_t*)workspace, w, bias, out, partial, m, out_stride,
+                                   out_offset, per, err);
     }
-    return e == cudaSuccess ? cudaGetLastError() : e;
+    if (e == cudaSuccess) e = cudaGetLastError();
+    if (e != cudaSuccess || splits == 1) return e;
+    const size_t total = (size_t)m * w.rows;
+    k_gemm_tc_combine<<<(unsigned)((total + 255) / 256), 256, 0, st>>>(partial, splits, m, w.rows, bias, out, out_stride,
+                                                                       out_offset);
+    return cudaGetLastError();
 }
 
 }  // namespace enx

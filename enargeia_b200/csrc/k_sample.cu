@@ -13,18 +13,18 @@
 //  3. s = logit / T (f32); m = max s, its argmax (ties lowest) is the fallback
 //  4. p = exp(s - m) / sum exp(s - m), in double, kept in shared memory
 //  5. top_p < 1: the reference's 32 bisection steps on f32 midpoints, deciding
-//     mass(p >= mid) < top_p.  The next 8 midpoints form a binary tree fixed by (lo, hi); one
-//     pass buckets every p by the tree's 255 sorted thresholds, suffix sums of the bucket masses
-//     give mass(p >= t) at every node, and walking the tree replays the 8 decisions exactly.
-//     Four passes replace 32 reductions.
+//     mass(p >= mid) < top_p, as four passes of 8 steps each (k_topp.cuh: a tree of midpoints,
+//     fixed-point bucket masses, suffix sums, the 8 decisions replayed).
 //  6. kept = sum of p >= threshold; target = random * max(kept, 1e-20); the first id in
 //     ascending order whose running kept-mass reaches the target wins (argmax if none).
-// Probabilities, masses and running totals are doubles (the oracle's exact-arithmetic rule).
+// Probabilities, kept masses and running totals are doubles (the oracle's exact-arithmetic
+// rule); bisection masses are exact 62-bit fixed point.
 
 #include <cooperative_groups.h>
 
 #include "enx_internal.cuh"
 #include "k_small.cuh"
+#include "k_topp.cuh"
 
 namespace cg = cooperative_groups;
 
@@ -38,9 +38,10 @@ constexpr uint32_t kMaxPer = 26624;  // ids per CTA kept on chip: 8 bytes each
 uint32_t sample_max_vocab() { return kMaxPer * kCluster; }
 
 struct SampleSmem {
-    double bucket[256];     // bucket masses of this CTA (then of the cluster)
-    double thr[256];        // sorted tree thresholds, thr[1..255]
-    float mids[256];        // tree midpoints by heap index 1..255
+    fx62_t bucket[256];     // fixed-point bucket masses of this CTA
+    fx62_t suffix[256];     // cluster suffix masses mass(p >= thr[j])
+    fx62_t wsum[8];
+    ToppTree tree;          // midpoints of the current 8 bisection steps
     double wred[kSWarps];
     float fred[kSWarps];
     uint32_t ired[kSWarps];
@@ -48,8 +49,6 @@ struct SampleSmem {
     float cta_f;            // published per-CTA max
     uint32_t cta_i;         // published per-CTA argmax / crossing id
     float lo, hi;
-    double suffix[257];
-    float tl[256], th[256];  // tree interval bounds by heap index
 };
 
 __device__ __forceinline__ bool better(float v, uint32_t i, float bv, uint32_t bi) {
@@ -230,98 +229,35 @@ __global__ void __cluster_dims__(kCluster, 1, 1) __launch_bounds__(kSThreads, 1)
     __syncthreads();
     for (uint32_t i = tbeg; i < tend; ++i) pbuf[i - cbeg] = pbuf[i - cbeg] / gsum;
 
-    // ---- 5. top-p threshold: 4 passes x 8 bisection steps --------------------------------
+    // ---- 5. top-p threshold: 4 passes x 8 bisection steps (k_topp.cuh) --------------------
     float lo = 0.0f, hi = 1.0f;
     if (P.top_p < 1.0f) {
+        const int lane = threadIdx.x & 31;
         for (int round = 0; round < 4; ++round) {
-            if (threadIdx.x == 0) {
-                // heap-indexed tree of the next 8 midpoints, and its in-order (sorted) listing
-                float* L = sm.tl;
-                float* Hh = sm.th;
-                L[1] = lo; Hh[1] = hi;
-                for (int n = 1; n < 256; ++n) {
-                    float mid = (L[n] + Hh[n]) * 0.5f;
-                    sm.mids[n] = mid;
-                    if (n < 128) {
-                        L[2 * n] = L[n]; Hh[2 * n] = mid;
-                        L[2 * n + 1] = mid; Hh[2 * n + 1] = Hh[n];
-                    }
-                }
-                // in-order rank of heap node n at depth d (0-based): (2*(n - 2^d) + 1) * 2^(7-d)
-                for (int n = 1; n < 256; ++n) {
-                    int d = 31 - __clz(n);
-                    int rnk = (2 * (n - (1 << d)) + 1) << (7 - d);
-                    sm.thr[rnk] = (double)sm.mids[n];
-                }
-            }
-            for (int b = threadIdx.x; b < 256; b += kSThreads) sm.bucket[b] = 0.0;
+            if (threadIdx.x < 32) topp_build_tree_warp(sm.tree, lo, hi);
+            for (int b = threadIdx.x; b < 256; b += kSThreads) sm.bucket[b] = 0;
             __syncthreads();
-            const double tlo = sm.thr[1], thi = sm.thr[255];
-            double below = 0.0, above = 0.0;
-            const int lane = threadIdx.x & 31;
-            for (uint32_t k = 0; k < E; ++k) {
-                uint32_t i = tbeg + k;
-                bool valid = i < tend;
-                double p = valid ? pbuf[i - cbeg] : 0.0;
-                int b = -1;  // -1: no shared-memory update needed
-                if (valid) {
-                    if (p < tlo) below += p;
-                    else if (p >= thi) above += p;
-                    else {
-                        int bb = 0;
-#pragma unroll
-                        for (int step = 128; step >= 1; step >>= 1)
-                            if (sm.thr[bb + step] <= p) bb += step;
-                        b = bb;
-                    }
-                }
-                // aggregate equal buckets across the warp before touching shared memory
-                unsigned pending = __ballot_sync(0xffffffffu, b >= 0);
-                while (pending) {
-                    int leader = __ffs(pending) - 1;
-                    int lb = __shfl_sync(0xffffffffu, b, leader);
-                    bool mine = (b == lb) && ((pending >> lane) & 1u);
-                    double contrib = warp_sum_d(mine ? p : 0.0);
-                    if (lane == leader) atomicAdd(&sm.bucket[lb], contrib);
-                    pending &= ~__ballot_sync(0xffffffffu, mine);
-                }
-            }
-            double tb = block_sum_d(sm, below);
-            double ta = block_sum_d(sm, above);
-            if (threadIdx.x == 0) { sm.bucket[0] += tb; sm.bucket[255] += ta; }
+            topp_bucket_range(sm.tree, pbuf, tbeg - cbeg, tend - cbeg, sm.bucket);
             cluster.sync();
-            // cluster bucket totals (a thread per bucket, ranks in order), then suffix sums
-            // mass(p >= thr[j]): within each warp of 32 buckets, then the warps above added on
+            // cluster bucket totals (a thread per bucket), then suffix masses: within each warp of
+            // 32 buckets, then the warps above added on (integers: exact in any order)
             if (threadIdx.x < 256) {
-                double t = 0.0;
+                fx62_t t = 0;
                 for (int r = 0; r < kCluster; ++r) t += cluster.map_shared_rank(&sm, r)->bucket[threadIdx.x];
-                double v = t;
-#pragma unroll
-                for (int o = 1; o < 32; o <<= 1) {
-                    const double n = __shfl_down_sync(0xffffffffu, v, o);
-                    if (lane + o < 32) v += n;
-                }
+                const fx62_t v = topp_warp_suffix(t);
                 sm.suffix[threadIdx.x] = v;
-                if (lane == 0) sm.wred[threadIdx.x >> 5] = v;
+                if (lane == 0) sm.wsum[threadIdx.x >> 5] = v;
             }
             __syncthreads();
             if (threadIdx.x < 256) {
-                double add = 0.0;
-                for (int w = (threadIdx.x >> 5) + 1; w < 8; ++w) add += sm.wred[w];
+                fx62_t add = 0;
+                for (int w = (threadIdx.x >> 5) + 1; w < 8; ++w) add += sm.wsum[w];
                 sm.suffix[threadIdx.x] += add;
             }
             __syncthreads();
             if (threadIdx.x == 0) {
                 float l = lo, h = hi;
-                int n = 1;
-                for (int step = 0; step < 8; ++step) {
-                    int d = 31 - __clz(n);
-                    int rnk = (2 * (n - (1 << d)) + 1) << (7 - d);
-                    // p >= mid  <=>  bucket >= rank  (thresholds sorted, bucket = #thr <= p)
-                    double mass = sm.suffix[rnk];
-                    if (mass < (double)P.top_p) { h = sm.mids[n]; n = 2 * n; }
-                    else { l = sm.mids[n]; n = 2 * n + 1; }
-                }
+                topp_decide(sm.tree, sm.suffix, P.top_p, l, h);
                 sm.lo = l;
                 sm.hi = h;
             }

@@ -13,9 +13,10 @@
 //             the unit's greedy candidate (max logit, lowest id) and scaled candidate
 //             (max logit/T, lowest id)                                             -> cand
 //   probs     m = best scaled candidate; e = exp(logit/T - m) in double; the unit's sum -> sum
-//   buckets   round k of the top-p bisection (8 steps per round, 4 rounds): walk round k-1's
-//             gathered bucket masses to the new interval (round 0: normalise p by the total),
-//             then the unit's masses of p in the 256 intervals cut by the next 255 midpoints
+//   buckets   round k of the top-p bisection (8 steps per round, 4 rounds, k_topp.cuh): walk
+//             round k-1's gathered bucket masses to the new interval (round 0: normalise p by
+//             the total), then the unit's fixed-point masses of p in the 256 intervals cut by the
+//             next 255 midpoints
 //                                                                                    -> bucket
 //   kept      walk the last round to the threshold; the unit's mass of p >= threshold -> kept
 //   pick      offset of the unit = kept mass of the units before it; target = random *
@@ -25,10 +26,12 @@
 //             scaled candidate's id.
 //
 // The arithmetic is the single-GPU sampler's (k_sample.cu): f32 penalty and scaling, double
-// probabilities, masses and running totals, f32 bisection midpoints.
+// probabilities, kept masses and running totals, f32 bisection midpoints, exact 62-bit
+// fixed-point bisection masses.
 
 #include "enx_internal.cuh"
 #include "k_small.cuh"
+#include "k_topp.cuh"
 
 namespace enx {
 
@@ -116,72 +119,39 @@ __device__ __forceinline__ size_t gidx(uint32_t u, uint32_t row, uint32_t rows, 
     return ((size_t)(u / split) * rows + row) * split + u % split;
 }
 
-// Heap-indexed tree of the 255 midpoints of 8 bisection steps from (lo, hi), and its sorted
-// listing thr[1..255] (in-order rank of heap node n at depth d: (2(n - 2^d) + 1) * 2^(7-d)).
-struct Tree {
-    float tl[256], th[256], mids[256];
-    double thr[256];
-    double suffix[256];
-    double wsum[8];
+// Tree of the current 8 bisection steps, suffix masses and the walked interval.
+struct Walk {
+    ToppTree t;
+    fx62_t suffix[256];
+    fx62_t wsum[8];
     float lo, hi;
 };
 
-__device__ __forceinline__ int inorder_rank(int n) {
-    const int d = 31 - __clz(n);
-    return (2 * (n - (1 << d)) + 1) << (7 - d);
-}
-
-__device__ void build_tree(Tree& t, float lo, float hi) {  // one thread
-    t.tl[1] = lo;
-    t.th[1] = hi;
-    for (int n = 1; n < 256; ++n) {
-        const float mid = (t.tl[n] + t.th[n]) * 0.5f;
-        t.mids[n] = mid;
-        if (n < 128) {
-            t.tl[2 * n] = t.tl[n]; t.th[2 * n] = mid;
-            t.tl[2 * n + 1] = mid; t.th[2 * n + 1] = t.th[n];
-        }
-    }
-    for (int n = 1; n < 256; ++n) t.thr[inorder_rank(n)] = (double)t.mids[n];
-}
-
-// Replays 8 bisection steps from (lo, hi) on the gathered bucket masses of the round that used
-// that interval: mass(p >= mid) < top_p moves hi down, else lo up.  Whole block; the new
-// interval in t.lo / t.hi.
-__device__ void walk(Tree& t, const double* bucket_all, uint32_t row, uint32_t rows, uint32_t units,
+// Replays 8 bisection steps from (lo, hi) on the gathered fixed-point bucket masses of the
+// round that used that interval (k_topp.cuh).  Whole block; the new interval in w.lo / w.hi.
+__device__ void walk(Walk& w, const fx62_t* bucket_all, uint32_t row, uint32_t rows, uint32_t units,
                      uint32_t split, float lo, float hi, float top_p) {
     const int lane = threadIdx.x & 31;
-    if (threadIdx.x == 0) build_tree(t, lo, hi);
+    if (threadIdx.x < 32) topp_build_tree_warp(w.t, lo, hi);
     if (threadIdx.x < 256) {
-        double s = 0.0;
+        fx62_t s = 0;
         for (uint32_t u = 0; u < units; ++u) s += bucket_all[gidx(u, row, rows, split) * 256 + threadIdx.x];
-        // suffix sums within each warp of 32 buckets, then the warps above added on
-        double v = s;
-#pragma unroll
-        for (int o = 1; o < 32; o <<= 1) {
-            const double nb = __shfl_down_sync(0xffffffffu, v, o);
-            if (lane + o < 32) v += nb;
-        }
-        t.suffix[threadIdx.x] = v;
-        if (lane == 0) t.wsum[threadIdx.x >> 5] = v;
+        const fx62_t v = topp_warp_suffix(s);
+        w.suffix[threadIdx.x] = v;
+        if (lane == 0) w.wsum[threadIdx.x >> 5] = v;
     }
     __syncthreads();
     if (threadIdx.x < 256) {
-        double add = 0.0;
-        for (int w = (threadIdx.x >> 5) + 1; w < 8; ++w) add += t.wsum[w];
-        t.suffix[threadIdx.x] += add;
+        fx62_t add = 0;
+        for (int k = (threadIdx.x >> 5) + 1; k < 8; ++k) add += w.wsum[k];
+        w.suffix[threadIdx.x] += add;
     }
     __syncthreads();
     if (threadIdx.x == 0) {
         float l = lo, h = hi;
-        int n = 1;
-        for (int step = 0; step < 8; ++step) {
-            const double mass = t.suffix[inorder_rank(n)];  // mass(p >= mids[n])
-            if (mass < (double)top_p) { h = t.mids[n]; n = 2 * n; }
-            else { l = t.mids[n]; n = 2 * n + 1; }
-        }
-        t.lo = l;
-        t.hi = h;
+        topp_decide(w.t, w.suffix, top_p, l, h);
+        w.lo = l;
+        w.hi = h;
     }
     __syncthreads();
 }
@@ -287,19 +257,18 @@ __global__ void __launch_bounds__(kShThreads) k_shard_probs(const float* logits_
 
 __global__ void __launch_bounds__(kShThreads) k_shard_buckets(uint32_t n, uint32_t split, uint32_t world,
                                                               uint32_t round, const SampleRow* rows,
-                                                              const double* sum_all, const double* bucket_prev,
-                                                              ShardState* state, double* pbuf, double* bucket) {
+                                                              const double* sum_all, const fx62_t* bucket_prev,
+                                                              ShardState* state, double* pbuf, fx62_t* bucket) {
     const uint32_t row = blockIdx.y, nrows = gridDim.y, units = world * split;
     const SampleRow P = rows[row];
-    double* out = bucket + ((size_t)row * split + blockIdx.x) * 256;
-    __shared__ Tree t;
-    __shared__ double bk[256];
+    fx62_t* out = bucket + ((size_t)row * split + blockIdx.x) * 256;
+    __shared__ Walk w;
+    __shared__ fx62_t bk[256];
     __shared__ double s_sum;
-    __shared__ ShRed red;
     const Span S = my_span(n, split);
     double* p = pbuf + (size_t)row * n;
     if (P.temperature <= 0.0f) {
-        for (int b = threadIdx.x; b < 256; b += kShThreads) out[b] = 0.0;
+        for (int b = threadIdx.x; b < 256; b += kShThreads) out[b] = 0;
         return;
     }
     if (round == 0) {  // normalise by the vocabulary total, units in order
@@ -309,70 +278,35 @@ __global__ void __launch_bounds__(kShThreads) k_shard_buckets(uint32_t n, uint32
         for (uint32_t i = S.tbeg; i < S.tend; ++i) p[i] = p[i] / gs;
     }
     if (P.top_p >= 1.0f) {
-        for (int b = threadIdx.x; b < 256; b += kShThreads) out[b] = 0.0;
+        for (int b = threadIdx.x; b < 256; b += kShThreads) out[b] = 0;
         return;
     }
     float lo = 0.0f, hi = 1.0f;
     if (round > 0) {
-        walk(t, bucket_prev, row, nrows, units, split, state[row].lohi[round - 1][0], state[row].lohi[round - 1][1],
+        walk(w, bucket_prev, row, nrows, units, split, state[row].lohi[round - 1][0], state[row].lohi[round - 1][1],
              P.top_p);
-        lo = t.lo;
-        hi = t.hi;
+        lo = w.lo;
+        hi = w.hi;
         if (blockIdx.x == 0 && threadIdx.x == 0) {
             state[row].lohi[round][0] = lo;
             state[row].lohi[round][1] = hi;
         }
     }
-    __syncthreads();  // the walk's tree is read before it is rebuilt
-    if (threadIdx.x == 0) build_tree(t, lo, hi);
-    for (int b = threadIdx.x; b < 256; b += kShThreads) bk[b] = 0.0;
+    if (threadIdx.x < 32) topp_build_tree_warp(w.t, lo, hi);
+    for (int b = threadIdx.x; b < 256; b += kShThreads) bk[b] = 0;
     __syncthreads();
-    const double tlo = t.thr[1], thi = t.thr[255];
-    const uint32_t E = S.tend - S.tbeg;
-    const uint32_t Emax = ((S.cend - S.cbeg) + kShThreads - 1) / kShThreads;
-    const int lane = threadIdx.x & 31;
-    double below = 0.0, above = 0.0;
-    for (uint32_t k = 0; k < Emax; ++k) {
-        const bool valid = k < E;
-        const double v = valid ? p[S.tbeg + k] : 0.0;
-        int b = -1;  // -1: no shared-memory update needed
-        if (valid) {
-            if (v < tlo) below += v;
-            else if (v >= thi) above += v;
-            else {
-                int bb = 0;
-#pragma unroll
-                for (int step = 128; step >= 1; step >>= 1)
-                    if (t.thr[bb + step] <= v) bb += step;
-                b = bb;
-            }
-        }
-        // aggregate equal buckets across the warp before touching shared memory
-        unsigned pending = __ballot_sync(0xffffffffu, b >= 0);
-        while (pending) {
-            const int leader = __ffs(pending) - 1;
-            const int lb = __shfl_sync(0xffffffffu, b, leader);
-            const bool mine = (b == lb) && ((pending >> lane) & 1u);
-            const double contrib = warp_sum_d(mine ? v : 0.0);
-            if (lane == leader) atomicAdd(&bk[lb], contrib);
-            pending &= ~__ballot_sync(0xffffffffu, mine);
-        }
-    }
-    double tb, ta;
-    block_scan(red, below, &tb);
-    block_scan(red, above, &ta);
-    if (threadIdx.x == 0) { bk[0] += tb; bk[255] += ta; }
+    topp_bucket_range(w.t, p, S.tbeg, S.tend, bk);
     __syncthreads();
     for (int b = threadIdx.x; b < 256; b += kShThreads) out[b] = bk[b];
 }
 
 __global__ void __launch_bounds__(kShThreads) k_shard_kept(uint32_t n, uint32_t split, uint32_t world,
                                                            uint32_t rounds, const SampleRow* rows,
-                                                           const double* sum_all, const double* bucket_last,
+                                                           const double* sum_all, const fx62_t* bucket_last,
                                                            ShardState* state, double* pbuf, double* kept) {
     const uint32_t row = blockIdx.y, nrows = gridDim.y, units = world * split;
     const SampleRow P = rows[row];
-    __shared__ Tree t;
+    __shared__ Walk w;
     __shared__ ShRed red;
     __shared__ double s_sum;
     double* p = pbuf + (size_t)row * n;
@@ -389,9 +323,9 @@ __global__ void __launch_bounds__(kShThreads) k_shard_kept(uint32_t n, uint32_t 
     }
     double thr = 0.0;
     if (P.top_p < 1.0f && rounds > 0) {
-        walk(t, bucket_last, row, nrows, units, split, state[row].lohi[rounds - 1][0],
+        walk(w, bucket_last, row, nrows, units, split, state[row].lohi[rounds - 1][0],
              state[row].lohi[rounds - 1][1], P.top_p);
-        thr = (double)t.lo;
+        thr = (double)w.lo;
     }
     if (blockIdx.x == 0 && threadIdx.x == 0) state[row].thr = thr;
     double mine = 0.0;
@@ -524,29 +458,30 @@ extern "C" enx_status enx_shard_probs(const float* logits, uint32_t n, uint32_t 
 
 extern "C" enx_status enx_shard_buckets(uint32_t n, uint32_t rows, uint32_t split, uint32_t world, uint32_t round,
                                         const enx_sampling_row* params, const double* sum_all,
-                                        const double* bucket_prev, void* state, double* probs, double* bucket,
+                                        const uint64_t* bucket_prev, void* state, double* probs, uint64_t* bucket,
                                         void* stream) {
     if (!params || !state || !probs || !bucket || (round == 0 && !sum_all) || (round > 0 && !bucket_prev))
         return fail(ENX_ERR_INVALID, "enx_shard_buckets: null pointer");
     if (!sh_dims_ok(n, rows, split, world) || round > 3)
         return fail(ENX_ERR_RANGE, "enx_shard_buckets: bad dimensions");
     k_shard_buckets<<<dim3(split, rows), kShThreads, 0, as_stream(stream)>>>(
-        n, split, world, round, reinterpret_cast<const SampleRow*>(params), sum_all, bucket_prev,
-        static_cast<ShardState*>(state), probs, bucket);
+        n, split, world, round, reinterpret_cast<const SampleRow*>(params), sum_all,
+        reinterpret_cast<const fx62_t*>(bucket_prev), static_cast<ShardState*>(state), probs,
+        reinterpret_cast<fx62_t*>(bucket));
     return sh_launched("enx_shard_buckets");
 }
 
 extern "C" enx_status enx_shard_kept(uint32_t n, uint32_t rows, uint32_t split, uint32_t world, uint32_t rounds,
                                      const enx_sampling_row* params, const double* sum_all,
-                                     const double* bucket_last, void* state, double* probs, double* kept,
+                                     const uint64_t* bucket_last, void* state, double* probs, double* kept,
                                      void* stream) {
     if (!params || !state || !probs || !kept || (rounds == 0 && !sum_all) || (rounds > 0 && !bucket_last))
         return fail(ENX_ERR_INVALID, "enx_shard_kept: null pointer");
     if (!sh_dims_ok(n, rows, split, world) || (rounds != 0 && rounds != 4))
         return fail(ENX_ERR_RANGE, "enx_shard_kept: rounds must be 0 or 4");
     k_shard_kept<<<dim3(split, rows), kShThreads, 0, as_stream(stream)>>>(
-        n, split, world, rounds, reinterpret_cast<const SampleRow*>(params), sum_all, bucket_last,
-        static_cast<ShardState*>(state), probs, kept);
+        n, split, world, rounds, reinterpret_cast<const SampleRow*>(params), sum_all,
+        reinterpret_cast<const fx62_t*>(bucket_last), static_cast<ShardState*>(state), probs, kept);
     return sh_launched("enx_shard_kept");
 }
 

@@ -147,7 +147,7 @@ class ShardedSampler:
         self.probs = torch.empty(R * self.n, dtype=torch.float64, device=dev)
         self.cand = torch.empty(R * S * 4, dtype=torch.int32, device=dev)
         self.sums = torch.empty(R * S, dtype=torch.float64, device=dev)
-        self.bucket = torch.empty(R * S * 256, dtype=torch.float64, device=dev)
+        self.bucket = torch.empty(R * S * 256, dtype=torch.int64, device=dev)  # u64 fixed-point masses
         self.kept_buf = torch.empty(R * S, dtype=torch.float64, device=dev)
         self.pick_buf = torch.empty(R * S, dtype=torch.int32, device=dev)
         self.out = torch.empty(R, dtype=torch.int32, device=dev)

@@ -313,9 +313,10 @@ ENX_API enx_status enx_batch_profile(enx_ctx* ctx, uint32_t batch, float* ms, ui
  * writes a send buffer of one record per (row, cta) - [rows][split] - and the caller allgathers
  * every rank's send buffer into [world][rows][split] (rank-major: NCCL all_gather_into_tensor)
  * before the next phase reads it:
- *   prepare -> cand u32[4]  | probs -> sum f64 | buckets x4 -> bucket f64[256] | kept -> kept f64
+ *   prepare -> cand u32[4]  | probs -> sum f64 | buckets x4 -> bucket u64[256] | kept -> kept f64
  *   | pick -> pick u32 | finish -> out[rows]
- * With topp_rounds 0 (no row has top_p < 1) the bucket phases are skipped and kept normalises.
+ * Bucket masses are round(p * 2^62) summed as integers (exact, order-free).  With topp_rounds 0
+ * (no row has top_p < 1) the bucket phases are skipped and kept normalises.
  * `state` (enx_shard_state_bytes(rows), device) and `probs` (f64 [rows][n], device) stay on the
  * rank between phases.  Every rank computes the same ids in `out`.  All pointers device.
  * ---------------------------------------------------------------------------------------- */
@@ -330,11 +331,11 @@ ENX_API enx_status enx_shard_probs(const float* logits, uint32_t n, uint32_t row
                                    void* stream);
 ENX_API enx_status enx_shard_buckets(uint32_t n, uint32_t rows, uint32_t split, uint32_t world,
                                      uint32_t round, const enx_sampling_row* params,
-                                     const double* sum_all, const double* bucket_prev, void* state,
-                                     double* probs, double* bucket, void* stream);
+                                     const double* sum_all, const uint64_t* bucket_prev, void* state,
+                                     double* probs, uint64_t* bucket, void* stream);
 ENX_API enx_status enx_shard_kept(uint32_t n, uint32_t rows, uint32_t split, uint32_t world,
                                   uint32_t topp_rounds, const enx_sampling_row* params,
-                                  const double* sum_all, const double* bucket_last, void* state,
+                                  const double* sum_all, const uint64_t* bucket_last, void* state,
                                   double* probs, double* kept, void* stream);
 ENX_API enx_status enx_shard_pick(uint32_t n, uint32_t row_begin, uint32_t rows, uint32_t split,
                                   uint32_t world, uint32_t rank, const enx_sampling_row* params,

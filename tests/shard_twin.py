@@ -42,6 +42,10 @@ def _tree(lo, hi):
     return mids, thr
 
 
+def _fx62(p):
+    return np.rint(np.asarray(p, np.float64) * 2.0 ** 62).astype(np.uint64)
+
+
 def _gidx(u, row, rows, split):
     return ((u // split) * rows + row) * split + u % split
 
@@ -106,14 +110,15 @@ class NumpyPhases:
 
     def _walk(self, bucket_all, r, rows, units, split, lo, hi, top_p):
         mids, _ = _tree(lo, hi)
-        B = bucket_all.numpy().reshape(-1, 256)
-        tot = np.zeros(256)
+        B = bucket_all.numpy().view(np.uint64).reshape(-1, 256)
+        tot = np.zeros(256, np.uint64)
         for u in range(units):
             tot += B[_gidx(u, r, rows, split)]
         suffix = np.cumsum(tot[::-1])[::-1]
+        goal = _fx62(np.float64(top_p))
         n, l, h = 1, lo, hi
         for _ in range(8):
-            if suffix[_rank(n)] < float(top_p):
+            if suffix[_rank(n)] < goal:
                 h, n = mids[n], 2 * n
             else:
                 l, n = mids[n], 2 * n + 1
@@ -128,11 +133,11 @@ class NumpyPhases:
     def buckets(self, n, rows, split, world, rnd, params, sum_all, prev, state, probs, bucket):
         P = _params(params)
         p = probs.numpy().reshape(rows, n)
-        out = bucket.numpy().reshape(rows, split, 256)
+        out = bucket.numpy().view(np.uint64).reshape(rows, split, 256)
         units = world * split
         for r in range(rows):
             T, top_p = P[r, 0], P[r, 1]
-            out[r] = 0.0
+            out[r] = 0
             if T <= 0:
                 continue
             if rnd == 0:
@@ -147,7 +152,7 @@ class NumpyPhases:
             for c, (b, e) in enumerate(self._spans(n, split)):
                 seg = p[r, b:e]
                 k = np.searchsorted(thr[1:256], seg, side="right")
-                out[r, c] = np.bincount(k, weights=seg, minlength=256)
+                np.add.at(out[r, c], k, _fx62(seg))
 
     def kept(self, n, rows, split, world, rounds, params, sum_all, last, state, probs, kept):
         P = _params(params)

@@ -2,13 +2,17 @@
 
 The kernel replaces the reference's 32 sequential bisection steps (src/kernels/sample.wgsl:
 241-262) by four passes that each resolve 8 steps through a tree of midpoints.  This mirror of
-that tree walk, in numpy, must land on exactly the threshold the oracle's sequential bisection
+that tree walk, in numpy, with the kernels' exact 62-bit fixed-point bucket masses, must land on exactly the threshold the oracle's sequential bisection
 finds, for every distribution shape including ties."""
 
 import numpy as np
 import pytest
 
 f32 = np.float32
+
+
+def fx62(p):
+    return np.rint(np.asarray(p, np.float64) * 2.0 ** 62).astype(np.uint64)
 
 
 def tree_bisection(p: np.ndarray, top_p: float) -> float:
@@ -29,12 +33,14 @@ def tree_bisection(p: np.ndarray, top_p: float) -> float:
         for n in range(1, 256):
             thr[rank(n)] = float(mids[n])
         b = np.searchsorted(thr[1:256], p, side="right")  # number of thresholds <= p
-        M = np.bincount(b, weights=p, minlength=256)
+        M = np.zeros(256, np.uint64)  # 62-bit fixed-point masses, as the kernels sum them
+        np.add.at(M, b, fx62(p))
         suffix = np.cumsum(M[::-1])[::-1]
+        goal = fx62(float(f32(top_p)))
         n = 1
         l, h = lo, hi
         for _ in range(8):
-            if suffix[rank(n)] < float(f32(top_p)):
+            if suffix[rank(n)] < goal:
                 h = mids[n]
                 n = 2 * n
             else:
