@@ -306,6 +306,144 @@ def run_enx(args, rank, world, local_rank):
 
 
 # ---------------------------------------------------------------------------------------------
+# config 3: chunked prefill (bench.py --workload config3)
+
+PREFILL_LEN, PREFILL_CHUNK = 2048, 256
+PREFILL_METRIC = "prefill tok/s (2048-token prompt in 256-query chunks, Qwen2.5-0.5B int4 + int8 head)"
+
+
+def run_prefill(args, rank, world, local_rank):
+    """One step = enx_prefill of a fresh 2048-token uniform-random prompt in 256-query chunks: per
+    chunk and layer the q|k|v, o, gate|up and down projections on the tcgen05 limb GEMM, RoPE and
+    the f16 cache writes, causal GQA attention over the cache so far; the tied head for the last
+    row.  N > 1: independent replicas (independent prompts are data-parallel)."""
+    import ctypes as C
+
+    import torch
+    import torch.distributed as dist
+
+    from enargeia_b200 import build
+    from enargeia_b200._lib import MatmulQ4Dims, call
+    from enargeia_b200.session import Model
+
+    build.build()
+    torch.cuda.set_device(local_rank)
+    dev = torch.device("cuda", local_rank)
+    if local_rank == 0:
+        build_model_file(QWEN2_0_5B, SEED, model_path())
+    if world > 1:
+        dist.barrier()
+    cfg = QWEN2_0_5B
+    m = Model(cfg, local_rank).load(model_path()).kv_alloc(PREFILL_LEN + 1, 1)
+    stream = torch.cuda.ExternalStream(m.stream_handle(), device=dev)
+    prompt = [int(v) for v in np.random.default_rng(3000 + rank).integers(0, cfg.vocab, PREFILL_LEN)]
+
+    def barrier():
+        if world > 1:
+            dist.barrier()
+        torch.cuda.synchronize()
+
+    def max_over_ranks(x):
+        if world == 1:
+            return x
+        t = torch.tensor([x], dtype=torch.float64, device=dev)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        return float(t.item())
+
+    steps = min(args.steps, 20)
+    for _ in range(args.warmup):
+        m.reset(0)
+        m.prefill(0, prompt, PREFILL_CHUNK)
+    with ClockSampler(local_rank) as clocks:
+        barrier()
+        dev_ms, wall = 0.0, 0.0
+        for _ in range(steps):
+            m.reset(0)
+            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            t0 = time.perf_counter()
+            e0.record(stream)
+            m.prefill(0, prompt, PREFILL_CHUNK)  # host ids in; returns when the chunks are done
+            e1.record(stream)
+            torch.cuda.synchronize()
+            wall += time.perf_counter() - t0
+            dev_ms += e0.elapsed_time(e1)
+        barrier()
+    dev_ms = max_over_ranks(dev_ms)
+    wall_ms = max_over_ranks(wall * 1e3)
+    value = world * steps * PREFILL_LEN / (dev_ms / 1e3)
+    # roofline: layer 0's gate projection at the chunk size, alone, 20 launches on the model stream
+    g = m.tensor_view("model.layers.0.mlp.gate_proj.weight")
+    x = torch.randn(PREFILL_CHUNK, g["cols"], device=dev)
+    out = torch.empty(PREFILL_CHUNK * g["rows"], device=dev)
+    d = MatmulQ4Dims(PREFILL_CHUNK, g["rows"], g["cols"], 0, 64, g["cols"] // 64, g["rows"], 0,
+                     min(g["rows"], 65535), 0, 0, 0)
+    sh = C.c_void_p(m.stream_handle())
+
+    def launch():
+        call("enx_matmul_q4", C.c_void_p(x.data_ptr()), C.c_void_p(g["packed"]), C.c_void_p(g["scales"]),
+             C.c_void_p(g["zeros"]), None, C.c_void_p(out.data_ptr()), C.byref(d), sh)
+
+    for _ in range(3):
+        launch()
+    torch.cuda.synchronize()
+    reps = 20
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record(stream)
+    for _ in range(reps):
+        launch()
+    e1.record(stream)
+    torch.cuda.synchronize()
+    gemm_us = e0.elapsed_time(e1) / reps * 1e3
+    peaks = {}
+    try:
+        peaks = json.loads((ROOT / "MEASURED_PEAKS.json").read_text())
+    except (OSError, ValueError):
+        pass
+    bf16 = float(peaks.get("bf16_tflops", 1590.0))
+    i8_peak = 2 * bf16
+    groups = -(-PREFILL_CHUNK // 32)
+    mma_ops = 2 * (-(-g["rows"] // 128) * 128) * groups * 256 * g["cols"]
+    useful = 2 * PREFILL_CHUNK * g["rows"] * g["cols"]
+    proj_macs = cfg.layers * (cfg.hidden * (cfg.hidden + 2 * cfg.kv_dim) + cfg.hidden * cfg.hidden
+                              + 3 * cfg.hidden * cfg.intermediate)
+    attn_macs = cfg.layers * cfg.heads * cfg.head_dim * 2 * (PREFILL_LEN * (PREFILL_LEN + 1) // 2)
+    step_flops = 2 * (proj_macs * PREFILL_LEN + attn_macs + cfg.vocab * cfg.hidden)
+    out_line = {
+        "metric": PREFILL_METRIC,
+        "value": round(value, 1),
+        "unit": "tok/s",
+        "n_gpus": world,
+        "steps": steps,
+        "warmup": args.warmup,
+        "ms_per_step": round(dev_ms / steps, 3),
+        "higher_is_better": True,
+        "scaling": "weak",
+        "vs_baseline": None,
+        "dtype": "int4/int8 weights x f32 activations (exact int8-limb tensor-core block sums, f64 accumulate), f16 KV",
+        "data": "synthetic: seeded random-init weights normal(0,0.02); 2048 uniform random prompt ids",
+        "config": {"workload": "config 3: chunked prefill of a 2048-token prompt in 256-query chunks through the "
+                               "config-0 model", "parallelism": f"replicas x{world}",
+                   "l2": "inputs larger than L2: 351 MB of weights per chunk",
+                   "step_flops": step_flops},
+        "e2e": {"value": round(world * steps * PREFILL_LEN / (wall_ms / 1e3), 1), "unit": "tok/s",
+                "h2d_bytes_per_step": PREFILL_LEN * 4, "d2h_bytes_per_step": 0,
+                "api": "Model.prefill -> enx_prefill (host ids in, synchronous), wall clock"},
+        "roofline": {"kernel": f"enx_matmul_q4 M={PREFILL_CHUNK} gate ({g['rows']}x{g['cols']}, tcgen05 limb GEMM)",
+                     "bound": "tensor", "achieved": round(mma_ops / (gemm_us / 1e6) / 1e12, 2),
+                     "peak": i8_peak, "unit": "TOP/s (int8 MMA)",
+                     "frac": round(mma_ops / (gemm_us / 1e6) / 1e12 / i8_peak, 4), "traffic": None,
+                     "useful_tflops": round(useful / (gemm_us / 1e6) / 1e12, 2), "launch_us": round(gemm_us, 2),
+                     "peak_source": "2 x measured MEASURED_PEAKS.json bf16_tflops (dense int8 = 2x dense bf16)"},
+        "step_tflops": round(step_flops / (dev_ms / steps / 1e3) / 1e12, 2),
+        "gpu_launches": None,
+        "clocks": clocks.summary(),
+    }
+    if rank == 0:
+        print(json.dumps(out_line), flush=True)
+    m.close()
+
+
+# ---------------------------------------------------------------------------------------------
 # config 4: batched sampled decode (bench.py --workload config4)
 
 BATCH_PROMPT, BATCH_CTX = 512, 2048
@@ -872,9 +1010,10 @@ def main():
     ap.add_argument("--impl", choices=["enx", "reference"], default="enx")
     ap.add_argument("--cpu-budget", type=float, default=15.0)
     ap.add_argument("--no-cpu-baseline", action="store_true")
-    ap.add_argument("--workload", choices=["config0", "config1", "config2", "config4"], default="config0",
+    ap.add_argument("--workload", choices=["config0", "config1", "config2", "config3", "config4"], default="config0",
                     help="config0: greedy batch-1 decode (the headline); config1: int4 matvec/GEMM sweep; "
-                         "config2: vocab-sharded LM head + sampling; config4: batched sampled decode")
+                         "config2: vocab-sharded LM head + sampling; config3: chunked prefill; "
+                         "config4: batched sampled decode")
     ap.add_argument("--case", default="", help="config1: one case n,k,m with 3 timed launches (profiling)")
     ap.add_argument("--batch", type=int, default=256,
                     help="config4: total sequences over all GPUs; config2: rows per step (default 64)")
@@ -900,6 +1039,8 @@ def main():
             if args.steps == 2016:
                 args.steps = 200
             run_sweep(args, rank, world, local_rank)
+        elif args.workload == "config3":
+            run_prefill(args, rank, world, local_rank)
         elif args.workload == "config2":
             run_head(args, rank, world, local_rank)
         elif args.workload == "config4":

@@ -1102,7 +1102,7 @@ static cudaError_t batch_body(enx_ctx* c, uint32_t B, cudaStream_t st) {
 // section's time (ms) to ms[k]: 0 embed, 1 RMSNorms, 2 q|k|v GEMMs, 3 RoPE + cache rows,
 // 4 attention, 5 o GEMM + residual, 6 gate/up GEMMs + SiLU, 7 down GEMM + residual, 8 head GEMM,
 // 9 sampler.  It reruns the last step's rows (same cache rows and logits).
-static enx_status batch_profile(enx_ctx* c, uint32_t B, float* ms) {
+static enx_status batch_profile(enx_ctx* c, uint32_t B, float* ms, uint32_t count) {
     const enx_model_config& C = c->cfg;
     const uint32_t H = C.hidden, kvd = C.kv_heads * C.head_dim, I = C.intermediate;
     cudaStream_t st = c->stream;
@@ -1136,7 +1136,15 @@ static enx_status batch_profile(enx_ctx* c, uint32_t B, float* ms) {
             return r == cudaSuccess ? proj_b(c, 4, c->b_xn, L.wv, L.bv, c->b_v, B, kvd, st) : r;
         });
         if (e == cudaSuccess) e = section(3, [&] { return launch_rope_cache_batch(S, l, c->b_q, c->b_k, c->b_v, B, st); });
-        if (e == cudaSuccess) e = section(4, [&] { return launch_attn(S, l, B, c->b_att, st, false); });
+        if (e == cudaSuccess) {
+            if (count >= 14 && attn_split_path(S, B)) {  // attention stage by stage
+                for (int k = 0; k < 4 && e == cudaSuccess; ++k)
+                    e = section(10 + k, [&] { return launch_attn(S, l, B, c->b_att, st, false, k); });
+                ms[4] = ms[10] + ms[11] + ms[12] + ms[13];
+            } else {
+                e = section(4, [&] { return launch_attn(S, l, B, c->b_att, st, false); });
+            }
+        }
         if (e == cudaSuccess) e = section(5, [&] {
             cudaError_t r = proj_b(c, 4, c->b_att, L.wo, nullptr, c->b_t, B, H, st);
             return r == cudaSuccess ? launch_add(c->b_x, c->b_t, c->b_x, B * H, st) : r;
@@ -1587,5 +1595,5 @@ extern "C" enx_status enx_batch_profile(enx_ctx* c, uint32_t batch, float* ms, u
     DeviceGuard g(c->device);
     for (uint32_t i = 0; i < count; ++i) ms[i] = 0.f;
     ENX_CUDA(cudaStreamSynchronize(c->stream));
-    return batch_profile(c, batch, ms);
+    return batch_profile(c, batch, ms, count);
 }

@@ -443,43 +443,11 @@ cudaError_t launch_matmul(int bits, const float* x, const QW& w, const float* bi
                      : launch_matmul_bits<4>(x, w, bias, out, m, out_stride, out_offset, st, pdl);
 }
 
-// Stages n rows of hd f16 values (rows `stride` halfs apart in global memory) into shared memory
-// as doubles, rows dst_stride doubles apart, zero rows from n to nmax: 16-byte loads, eight in
-// flight per thread before any is converted.
-__device__ __forceinline__ void stage_rows_f16_to_f64(double* dst, uint32_t dst_stride, const uint16_t* src,
-                                                      uint32_t stride, uint32_t n, uint32_t nmax, uint32_t hd) {
-    const uint32_t row8 = hd / 8, total = nmax * row8;
-    for (uint32_t base = threadIdx.x; base < total; base += 8 * blockDim.x) {
-        uint4 v[8];
-#pragma unroll
-        for (int k = 0; k < 8; ++k) {
-            const uint32_t i = base + k * blockDim.x;
-            v[k] = make_uint4(0, 0, 0, 0);
-            if (i < total && i / row8 < n)
-                v[k] = __ldcg(reinterpret_cast<const uint4*>(src + (size_t)(i / row8) * stride) + i % row8);
-        }
-#pragma unroll
-        for (int k = 0; k < 8; ++k) {
-            const uint32_t i = base + k * blockDim.x;
-            if (i >= total) break;
-            const __half2* h2 = reinterpret_cast<const __half2*>(&v[k]);
-            double* d = dst + (size_t)(i / row8) * dst_stride + (i % row8) * 8;
-#pragma unroll
-            for (int e = 0; e < 4; ++e) {
-                const float2 f = __half22float2(h2[e]);
-                d[2 * e] = (double)f.x;
-                d[2 * e + 1] = (double)f.y;
-            }
-        }
-    }
-}
-
-// Many-token attention scores: one CTA per (kv head, 128-position split, token), a thread per
-// position holding all the group's heads (kMaxGroupSplit accumulators), so each K pair read from
-// shared memory feeds every head and the q pairs are warp-wide broadcasts.  The split's K rows are
-// widened to double once, row stride hd + 2 doubles (an odd number of 16-byte units: conflict-free
-// 16-byte reads).  scores[t][h][j] = float(sum_d q[h][d] * K[j][d] / sqrt(hd))
-// (test/reference/ops.ts:123-151).
+// Many-token attention, scores: one CTA per (kv head, split of kAttnSplit positions, token), a
+// thread per position holding all the group's heads (kMaxGroupSplit accumulators).  The thread
+// reads its K row (f16) straight into registers and takes the dot products with the group's
+// query heads (doubles in shared memory, warp-wide broadcasts) in double, dimension pairs in
+// order: scores[t][h][j] = float(sum_d q[h][d] * K[j][d] / sqrt(hd)) (test/reference/ops.ts:123-151).
 constexpr uint32_t kMaxGroupSplit = 8;
 __global__ void __launch_bounds__(kAttnSplit) k_attn_scores_split(StepArgs S, uint32_t layer) {
     pdl_launch_dependents();
@@ -488,27 +456,35 @@ __global__ void __launch_bounds__(kAttnSplit) k_attn_scores_split(StepArgs S, ui
     const uint32_t hd = S.head_dim, group = S.heads / S.kv_heads, kvd = S.kv_heads * hd;
     const uint32_t npos = S.pos_of(t) + 1, j0 = sp * kAttnSplit;
     if (j0 >= npos) return;
-    const uint32_t n = min(kAttnSplit, npos - j0), ks = hd + 2;
-    extern __shared__ double kd[];             // [kAttnSplit][hd + 2]
-    double* qd = kd + (size_t)kAttnSplit * ks;  // [group][hd]
-    const uint16_t* K = S.kcache + S.cache_offset(S.seq_of(t), layer, j0) + g * hd;
+    const uint32_t n = min(kAttnSplit, npos - j0);
+    __shared__ __align__(16) double qd[kMaxGroupSplit * 64];  // [group][hd]
     for (uint32_t i = threadIdx.x; i < group * hd; i += blockDim.x)
         qd[i] = (double)__ldcg(S.q + (size_t)t * S.hidden + g * group * hd + i);
-    stage_rows_f16_to_f64(kd, ks, K, kvd, n, n, hd);
     __syncthreads();
     const uint32_t j = threadIdx.x;
     if (j >= n) return;
+    const uint4* kr = reinterpret_cast<const uint4*>(S.kcache + S.cache_offset(S.seq_of(t), layer, j0 + j) + g * hd);
+    uint4 kq[8];
+#pragma unroll
+    for (uint32_t c = 0; c < 8; ++c) kq[c] = c < hd / 8 ? __ldcg(kr + c) : make_uint4(0, 0, 0, 0);
     double acc[kMaxGroupSplit];
 #pragma unroll
     for (int h = 0; h < (int)kMaxGroupSplit; ++h) acc[h] = 0.0;
-    const double2* kr = reinterpret_cast<const double2*>(kd + j * ks);
-    for (uint32_t d2 = 0; d2 < hd / 2; ++d2) {
-        const double2 kv = kr[d2];
 #pragma unroll
-        for (int h = 0; h < (int)kMaxGroupSplit; ++h) {
-            if (h < (int)group) {
-                const double2 qv = reinterpret_cast<const double2*>(qd + h * hd)[d2];
-                acc[h] = fma(qv.y, kv.y, fma(qv.x, kv.x, acc[h]));
+    for (uint32_t c = 0; c < 8; ++c) {
+        if (c >= hd / 8) break;
+        const __half2* h2 = reinterpret_cast<const __half2*>(&kq[c]);
+#pragma unroll
+        for (int e = 0; e < 4; ++e) {
+            const float2 kf = __half22float2(h2[e]);
+            const double kx = kf.x, ky = kf.y;
+            const uint32_t d2 = c * 4 + e;
+#pragma unroll
+            for (int h = 0; h < (int)kMaxGroupSplit; ++h) {
+                if (h < (int)group) {
+                    const double2 qv = reinterpret_cast<const double2*>(qd + h * hd)[d2];
+                    acc[h] = fma(qv.y, ky, fma(qv.x, kx, acc[h]));
+                }
             }
         }
     }
@@ -552,9 +528,10 @@ __global__ void __launch_bounds__(kThreads) k_attn_stats(StepArgs S) {
 }
 
 // Weighted V over one split of kAttnSplit positions for the query heads of one kv head, in double
-// (test/reference/ops.ts:181-204): attn_part[t][split][h][d].  A thread per (dimension pair,
-// quarter of the positions) holds every head of the group, so each V pair read from shared memory
-// feeds all heads and the weight pairs are broadcasts; the quarters meet in fixed order.
+// (test/reference/ops.ts:181-204): attn_part[t][split][h][d].  A warp per quarter of the positions
+// and a lane per dimension pair holds every head of the group: each V pair (f16, read from global
+// memory by the lane, a coalesced row per warp) feeds all heads, the weights are shared-memory
+// broadcasts, and the quarters meet in fixed order.  Positions past the token's last are not read.
 // grid = (kv_heads, splits, ntok), 4 warps.
 __global__ void __launch_bounds__(128) k_attn_apply_split(StepArgs S, uint32_t layer) {
     pdl_launch_dependents();
@@ -564,14 +541,11 @@ __global__ void __launch_bounds__(128) k_attn_apply_split(StepArgs S, uint32_t l
     const uint32_t npos = S.pos_of(t) + 1, j0 = sp * kAttnSplit;
     if (j0 >= npos) return;
     const uint32_t n = min(kAttnSplit, npos - j0);
-    extern __shared__ double vs[];                  // [kAttnSplit][hd]
-    double* ws = vs + (size_t)kAttnSplit * hd;       // [group][kAttnSplit]
-    double* red = ws + (size_t)kMaxGroupSplit * kAttnSplit;  // [4][group][hd]
-    const uint16_t* V = S.vcache + S.cache_offset(S.seq_of(t), layer, j0) + g * hd;
-    stage_rows_f16_to_f64(vs, hd, V, kvd, n, kAttnSplit, hd);
+    __shared__ float ws[kMaxGroupSplit][kAttnSplit];        // weights of the split's positions
+    __shared__ double red[4][kMaxGroupSplit][64];            // per-quarter sums
     for (uint32_t i = threadIdx.x; i < group * kAttnSplit; i += blockDim.x) {
-        const uint32_t h = i / kAttnSplit, j = i % kAttnSplit;
-        ws[i] = j < n ? (double)S.scores[((size_t)t * S.heads + g * group + h) * S.score_stride + j0 + j] : 0.0;
+        const uint32_t h = i / kAttnSplit, jj = i % kAttnSplit;
+        ws[h][jj] = jj < n ? S.scores[((size_t)t * S.heads + g * group + h) * S.score_stride + j0 + jj] : 0.f;
     }
     __syncthreads();
     const uint32_t lane = threadIdx.x & 31, q4 = threadIdx.x >> 5;  // dimension pair, position quarter
@@ -581,31 +555,37 @@ __global__ void __launch_bounds__(128) k_attn_apply_split(StepArgs S, uint32_t l
 #pragma unroll
         for (int h = 0; h < (int)kMaxGroupSplit; ++h) ax[h] = ay[h] = 0.0;
         const uint32_t jb = q4 * (kAttnSplit / 4), je = jb + kAttnSplit / 4;
-        for (uint32_t j = jb; j < je; j += 2) {  // zero weights past n keep the tail exact
-            const double2 v0 = reinterpret_cast<const double2*>(vs + (size_t)j * hd)[lane];
-            const double2 v1 = reinterpret_cast<const double2*>(vs + (size_t)(j + 1) * hd)[lane];
+        const __half2* V = reinterpret_cast<const __half2*>(S.vcache + S.cache_offset(S.seq_of(t), layer, j0) + g * hd) + lane;
+        const uint32_t rstride = kvd / 2;  // half2 per position
+#pragma unroll 4
+        for (uint32_t jj = jb; jj < je; jj += 2) {  // zero weights and rows past n keep the tail exact
+            const float2 f0 = jj < n ? __half22float2(__ldcg(V + (size_t)jj * rstride)) : make_float2(0.f, 0.f);
+            const float2 f1 = jj + 1 < n ? __half22float2(__ldcg(V + (size_t)(jj + 1) * rstride)) : make_float2(0.f, 0.f);
+            const double v0x = f0.x, v0y = f0.y, v1x = f1.x, v1y = f1.y;
 #pragma unroll
             for (int h = 0; h < (int)kMaxGroupSplit; ++h) {
                 if (h < (int)group) {
-                    const double2 w = reinterpret_cast<const double2*>(ws + h * kAttnSplit)[j >> 1];
-                    ax[h] = fma(w.y, v1.x, fma(w.x, v0.x, ax[h]));
-                    ay[h] = fma(w.y, v1.y, fma(w.x, v0.y, ay[h]));
+                    const float2 w = *reinterpret_cast<const float2*>(&ws[h][jj]);
+                    const double wx = w.x, wy = w.y;
+                    ax[h] = fma(wy, v1x, fma(wx, v0x, ax[h]));
+                    ay[h] = fma(wy, v1y, fma(wx, v0y, ay[h]));
                 }
             }
         }
 #pragma unroll
         for (int h = 0; h < (int)kMaxGroupSplit; ++h) {
             if (h < (int)group) {
-                red[((size_t)q4 * group + h) * hd + 2 * lane] = ax[h];
-                red[((size_t)q4 * group + h) * hd + 2 * lane + 1] = ay[h];
+                red[q4][h][2 * lane] = ax[h];
+                red[q4][h][2 * lane + 1] = ay[h];
             }
         }
     }
     __syncthreads();
     double* part = S.attn_part + (((size_t)t * (S.score_stride / kAttnSplit) + sp) * S.heads + g * group) * hd;
     for (uint32_t o = threadIdx.x; o < group * hd; o += blockDim.x) {
+        const uint32_t h = o / hd, d = o % hd;
         double v = 0.0;
-        for (uint32_t k = 0; k < 4; ++k) v += red[(size_t)k * group * hd + o];  // quarters in order
+        for (uint32_t k = 0; k < 4; ++k) v += red[k][h][d];  // quarters in order
         part[o] = v;
     }
 }
@@ -623,28 +603,35 @@ __global__ void k_attn_combine(StepArgs S, float* out) {
     }
 }
 
-cudaError_t launch_attn(const StepArgs& S, uint32_t layer, uint32_t ntok, float* out, cudaStream_t st, bool pdl) {
+cudaError_t launch_attn(const StepArgs& S, uint32_t layer, uint32_t ntok, float* out, cudaStream_t st, bool pdl,
+                        int only) {
     const uint32_t group = S.heads / S.kv_heads;
-    cudaError_t e;
-    if (S.attn_part && ntok >= 8 && S.score_stride % kAttnSplit == 0 && group <= kMaxGroupSplit && S.head_dim <= 64 &&
-        S.head_dim % 2 == 0) {
+    cudaError_t e = cudaSuccess;
+    if (attn_split_path(S, ntok)) {
         // many tokens: scores over position splits, softmax rows, V over position splits, then
         // the fixed-order combine
-        e = launch(k_attn_scores_split, dim3(S.kv_heads, S.score_stride / kAttnSplit, ntok), dim3(kAttnSplit),
-                   (size_t)(kAttnSplit * (S.head_dim + 2) + group * S.head_dim) * 8, st, pdl, S, layer);
-        if (e != cudaSuccess) return e;
-        e = launch(k_attn_stats, dim3(S.heads, ntok), dim3(kThreads), 0, st, pdl, S);
-        if (e != cudaSuccess) return e;
-        e = launch(k_attn_apply_split, dim3(S.kv_heads, S.score_stride / kAttnSplit, ntok), dim3(128),
-                   ((size_t)kAttnSplit * (S.head_dim + kMaxGroupSplit) + 4 * (size_t)group * S.head_dim) * 8, st, pdl, S,
-                   layer);
-        if (e != cudaSuccess) return e;
-        return launch(k_attn_combine, dim3(ntok), dim3(kThreads), 0, st, pdl, S, out);
+        if (only < 0 || only == 0)
+            e = launch(k_attn_scores_split, dim3(S.kv_heads, S.score_stride / kAttnSplit, ntok), dim3(kAttnSplit), 0,
+                       st, pdl, S, layer);
+        if (e == cudaSuccess && (only < 0 || only == 1))
+            e = launch(k_attn_stats, dim3(S.heads, ntok), dim3(kThreads), 0, st, pdl, S);
+        if (e == cudaSuccess && (only < 0 || only == 2))
+            e = launch(k_attn_apply_split, dim3(S.kv_heads, S.score_stride / kAttnSplit, ntok), dim3(128), 0, st,
+                       pdl, S, layer);
+        if (e == cudaSuccess && (only < 0 || only == 3)) e = launch(k_attn_combine, dim3(ntok), dim3(kThreads), 0, st, pdl, S, out);
+        return e;
     }
-    e = launch(k_attn_scores, dim3(S.kv_heads, S.score_stride / kAttnChunk, ntok), dim3(kThreads), 0, st, pdl, S, layer);
-    if (e != cudaSuccess) return e;
-    return launch(k_attn_apply, dim3(S.kv_heads, ntok), dim3(kThreads), (size_t)group * S.score_stride * 4, st, pdl,
-                  S, layer, out);
+    if (only < 0 || only == 0)
+        e = launch(k_attn_scores, dim3(S.kv_heads, S.score_stride / kAttnChunk, ntok), dim3(kThreads), 0, st, pdl, S, layer);
+    if (e == cudaSuccess && (only < 0 || only == 2))
+        e = launch(k_attn_apply, dim3(S.kv_heads, ntok), dim3(kThreads), (size_t)group * S.score_stride * 4, st, pdl,
+                   S, layer, out);
+    return e;
+}
+
+bool attn_split_path(const StepArgs& S, uint32_t ntok) {
+    return S.attn_part && ntok >= 8 && S.score_stride % kAttnSplit == 0 && S.heads / S.kv_heads <= kMaxGroupSplit &&
+           S.head_dim <= 64 && S.head_dim % 8 == 0;
 }
 
 template <int MT>

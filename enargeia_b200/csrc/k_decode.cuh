@@ -80,7 +80,10 @@ cudaError_t launch_layer(uint32_t mt, const LayerArgs& L, const StepArgs& S, cud
 cudaError_t launch_head(uint32_t mt, int bits, const HeadArgs& Hd, const StepArgs& S, cudaStream_t st);
 // Attention of `ntok` queries (S.q rows) over the cache: scores into S.scores, then softmax and
 // V into `out` [ntok][hidden].  Used by the layer path, prefill and the raw entry points.
-cudaError_t launch_attn(const StepArgs& S, uint32_t layer, uint32_t ntok, float* out, cudaStream_t st, bool pdl);
+// `only` >= 0 launches one stage (0 scores, 1 softmax rows, 2 weighted V, 3 combine), for timing.
+cudaError_t launch_attn(const StepArgs& S, uint32_t layer, uint32_t ntok, float* out, cudaStream_t st, bool pdl,
+                        int only = -1);
+bool attn_split_path(const StepArgs& S, uint32_t ntok);
 // Batched decode: RoPE of q (in place) and k, and k/v into each token's own cache row (token t is
 // sequence t at position S.pos_of(t)).
 cudaError_t launch_rope_cache_batch(const StepArgs& S, uint32_t layer, float* q, const float* k, const float* v,

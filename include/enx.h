@@ -299,8 +299,9 @@ ENX_API enx_status enx_launch_step_kernel(enx_ctx* ctx, uint32_t batch, uint32_t
 /* Measurement hook for batched decode (more than 4 sequences): runs the last batched step's body
  * once, outside its graph, with CUDA events between sections, and writes each section's total
  * time in ms to ms[0..9]: embed, RMSNorms, q|k|v GEMMs, RoPE + cache rows, attention, o GEMM +
- * residual, gate/up GEMMs + SiLU, down GEMM + residual, head GEMM, sampler.  It rewrites the same
- * cache rows and logits.  count must be at least 10. */
+ * residual, gate/up GEMMs + SiLU, down GEMM + residual, head GEMM, sampler.  With count >= 14 the
+ * many-token attention is also timed stage by stage into ms[10..13]: scores, softmax rows,
+ * weighted V, combine.  It rewrites the same cache rows and logits.  count must be at least 10. */
 ENX_API enx_status enx_batch_profile(enx_ctx* ctx, uint32_t batch, float* ms, uint32_t count);
 
 /* ------------------------------------------------------------------------------------------
