@@ -101,9 +101,9 @@ extern "C" enx_status enx_matmul_q4(const float* x, const uint32_t* packed, cons
     if (d->m >= kTcMinTokens) {  // tensor cores (exact limb GEMM), library-owned workspace
         uint8_t* ws = nullptr;
         uint32_t* err = nullptr;
-        ENX_TRY(tc_workspace(gemm_tc_workspace_bytes(d->m, d->k), &ws, &err));
-        ENX_CUDA(launch_gemm_tc(4, x, d->k, w, d->use_bias ? bias : nullptr, out, d->m, d->out_stride, d->out_offset, ws,
-                                err, as_stream(stream)));
+        ENX_TRY(tc_workspace(gemm_tc_workspace_bytes(d->m, d->k) + gemm_tc_codes_bytes(d->n, d->k), &ws, &err));
+        ENX_CUDA(launch_gemm_tc(4, x, d->k, w, nullptr, d->use_bias ? bias : nullptr, out, d->m, d->out_stride,
+                                d->out_offset, ws, err, as_stream(stream)));
         return ENX_OK;
     }
     ENX_CUDA(launch_matmul(4, x, w, d->use_bias ? bias : nullptr, out, d->m, d->out_stride, d->out_offset,
@@ -125,7 +125,7 @@ extern "C" enx_status enx_lm_head_q8(const float* x, const uint32_t* packed, con
         uint8_t* ws = nullptr;
         uint32_t* err = nullptr;
         ENX_TRY(tc_workspace(gemm_tc_workspace_bytes(d->seq, d->hidden), &ws, &err));
-        ENX_CUDA(launch_gemm_tc(8, x, d->hidden, w, nullptr, out, d->seq, stride, d->out_offset, ws, err,
+        ENX_CUDA(launch_gemm_tc(8, x, d->hidden, w, nullptr, nullptr, out, d->seq, stride, d->out_offset, ws, err,
                                 as_stream(stream)));
         return ENX_OK;
     }
@@ -378,6 +378,8 @@ __global__ void k_batch_loop_post(uint32_t* blk, BatchLayout Lb, uint32_t* ids, 
 
 }  // namespace
 
+static enx_status ensure_codes8(enx_ctx* c);
+
 struct enx_ctx {
     enx_model_config cfg{};
     int device = 0;
@@ -439,6 +441,8 @@ struct enx_ctx {
           *b_t = nullptr, *b_g = nullptr, *b_u = nullptr, *b_scores = nullptr, *b_rand = nullptr;
     uint32_t* b_ids = nullptr;
     uint8_t* b_ws = nullptr;
+    // int4 projection weights as the byte matrices (q - z) the tensor-core GEMM reads, by packed pointer
+    std::map<const uint32_t*, uint8_t*> codes8;
     std::map<uint32_t, cudaGraphExec_t> b_graph, b_loop_graph;
     std::map<uint32_t, uint32_t> b_launches;
     bool loop_batched = false;  // the last enx_decode_loop ran the batched path
@@ -454,6 +458,7 @@ enx_status dalloc(T** p, size_t count, const char* what) {
     if (e != cudaSuccess) return fail(ENX_ERR_NOMEM, std::string("cudaMalloc(") + what + "): " + cudaGetErrorString(e));
     return ENX_OK;
 }
+
 
 template <typename T>
 void dfree(T*& p) {
@@ -595,6 +600,7 @@ enx_status bind_model(enx_ctx* c) {
 
 }  // namespace
 
+
 extern "C" enx_status enx_create(const enx_model_config* cfg, int device, enx_ctx** out) {
     CHECK_ARG(cfg && out, "enx_create: null pointer");
     const enx_model_config& C = *cfg;
@@ -624,6 +630,7 @@ extern "C" enx_status enx_destroy(enx_ctx* c) {
         if (c->stream) cudaStreamSynchronize(c->stream);
         free_kv(c);
         dfree(c->d_trace);
+        for (auto& kv : c->codes8) cudaFree(kv.second);
         if (c->arena) cudaFree(c->arena);
         if (c->stream) cudaStreamDestroy(c->stream);
     }
@@ -700,6 +707,8 @@ extern "C" enx_status enx_load_enargeia_memory(enx_ctx* c, const void* data, siz
     }
     DeviceGuard g(c->device);
     if (c->arena) { cudaFree(c->arena); c->arena = nullptr; }
+    for (auto& kv : c->codes8) cudaFree(kv.second);
+    c->codes8.clear();
     c->tensors.clear();
     c->loaded = false;
     free_graphs(c);
@@ -729,6 +738,7 @@ extern "C" enx_status enx_load_enargeia_memory(enx_ctx* c, const void* data, siz
     ENX_CUDA(cudaStreamSynchronize(c->stream));
     ENX_TRY(bind_model(c));
     c->loaded = true;
+    if (c->pf_ws || (c->d_bb && c->batch >= kTcMinTokens)) ENX_TRY(ensure_codes8(c));  // buffers set up before the load
     return ENX_OK;
 }
 
@@ -817,6 +827,7 @@ extern "C" enx_status enx_kv_alloc(enx_ctx* c, uint32_t max_context, uint32_t ba
         ENX_TRY(dalloc(&c->b_rand, Bn * max_context, "batch loop randoms"));
         ENX_TRY(dalloc(&c->b_ids, Bn * max_context, "batch loop ids"));
         ENX_TRY(dalloc(&c->b_ws, gemm_tc_workspace_bytes(batch, (uint32_t)(I > H ? I : H)), "batch GEMM workspace"));
+        if (batch >= kTcMinTokens) ENX_TRY(ensure_codes8(c));
     }
     ENX_CUDA(cudaStreamSynchronize(c->stream));
     c->max_ctx = max_context;
@@ -868,11 +879,35 @@ static StepArgs step_args(enx_ctx* c) {
     return S;
 }
 
+// The byte matrices of every int4 projection weight for the tensor-core GEMM, prepared once
+// (before any graph capture) and reused by prefill and batched decode.
+static enx_status ensure_codes8(enx_ctx* c) {
+    if (!c->codes8.empty()) return ENX_OK;
+    for (const LayerArgs& L : c->layers) {
+        for (const QW* w : {&L.wq, &L.wk, &L.wv, &L.wo, &L.wg, &L.wu, &L.wd}) {
+            if (c->codes8.count(w->packed)) continue;
+            uint8_t* buf = nullptr;
+            ENX_TRY(dalloc(&buf, gemm_tc_codes_bytes(w->rows, w->cols), "GEMM code matrix"));
+            c->codes8[w->packed] = buf;
+            ENX_CUDA(launch_codes_i8(*w, buf, c->stream));
+        }
+    }
+    ENX_CUDA(cudaStreamSynchronize(c->stream));
+    return ENX_OK;
+}
+
+static const uint8_t* codes_of(const enx_ctx* c, const QW& w) {
+    const auto it = c->codes8.find(w.packed);
+    return it == c->codes8.end() ? nullptr : it->second;
+}
+
 // A projection of m prefill rows: tensor cores for m >= kTcMinTokens, CUDA cores below.
 static cudaError_t proj(enx_ctx* c, int bits, const float* x, const QW& w, const float* bias, float* out, uint32_t m,
                         uint32_t stride, uint32_t offset, cudaStream_t st) {
+    if (m >= kTcMinTokens && c->pf_ws && bits == 4 && !codes_of(c, w)) return cudaErrorInvalidValue;  // never prepared
     if (m >= kTcMinTokens && c->pf_ws)
-        return launch_gemm_tc(bits, x, w.cols, w, bias, out, m, stride, offset, c->pf_ws, &c->d_step->err, st);
+        return launch_gemm_tc(bits, x, w.cols, w, bits == 4 ? codes_of(c, w) : nullptr, bias, out, m, stride, offset,
+                              c->pf_ws, &c->d_step->err, st);
     return launch_matmul(bits, x, w, bias, out, m, stride, offset, st, false);
 }
 
@@ -895,8 +930,10 @@ static enx_status ensure_prefill(enx_ctx* c, uint32_t chunk) {
     ENX_TRY(dalloc(&c->pf_part, (size_t)chunk * split_stride(c->max_ctx) * C.heads, "prefill scores"));
     ENX_TRY(dalloc(&c->pf_apart, (size_t)chunk * (split_stride(c->max_ctx) / kAttnSplit) * H, "prefill attention splits"));
     ENX_TRY(dalloc(&c->pf_ids, chunk, "prefill ids"));
-    if (chunk >= kTcMinTokens)
+    if (chunk >= kTcMinTokens) {
         ENX_TRY(dalloc(&c->pf_ws, gemm_tc_workspace_bytes(chunk, (uint32_t)(I > H ? I : H)), "prefill GEMM workspace"));
+        ENX_TRY(ensure_codes8(c));
+    }
     c->pf_chunk = chunk;
     return ENX_OK;
 }
@@ -1052,8 +1089,10 @@ static bool mega_eligible(enx_ctx* c, uint32_t B, const StepArgs& S, MegaArgs& A
 // A projection of B batched tokens: tensor cores from kTcMinTokens tokens, CUDA cores below.
 static cudaError_t proj_b(enx_ctx* c, int bits, const float* x, const QW& w, const float* bias, float* out, uint32_t B,
                           uint32_t stride, cudaStream_t st) {
+    if (B >= kTcMinTokens && bits == 4 && !codes_of(c, w)) return cudaErrorInvalidValue;  // never prepared
     if (B >= kTcMinTokens)
-        return launch_gemm_tc(bits, x, w.cols, w, bias, out, B, stride, 0, c->b_ws, c->d_bb + c->bl.err(), st);
+        return launch_gemm_tc(bits, x, w.cols, w, bits == 4 ? codes_of(c, w) : nullptr, bias, out, B, stride, 0, c->b_ws,
+                              c->d_bb + c->bl.err(), st);
     return launch_matmul(bits, x, w, bias, out, B, stride, 0, st, false);
 }
 

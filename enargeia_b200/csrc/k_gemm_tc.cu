@@ -17,16 +17,18 @@
 // of a row tile are adjacent in the grid, so they read the tile's codes from L2.
 //
 // Warp roles, synchronised by mbarriers only:
-//   warps 0-7   epilogue: warpgroup wg drains tokens 16wg..16wg+15 of the accumulator the tensor
+//   warps 0-15  epilogue: warpgroup wg drains tokens 8wg..8wg+7 of the accumulator the tensor
 //               cores are not writing (thread = row), then releases it;
-//   warp 8      TMEM allocation; lane 0 issues the two MMAs of each block;
-//   warps 9-10  producer: a thread per two rows, fetches the rows' packed codes (and int4 zero
+//   warp 16     TMEM allocation; lane 0 issues the two MMAs of each block;
+//   warps 17-18 producer: a thread per two rows, fetches the rows' packed codes (and int4 zero
 //               words) four blocks ahead with cp.async, unpacks each block into a K-major
 //               shared-memory tile (int4: nibbles to bytes minus the zero
 //               code, even elements then odd ones -- the limb tile uses the same order); one
 //               thread also streams the block's limb tile in with a bulk copy.
 // Four stages of (codes, limbs), two accumulators of 256 TMEM columns.  Every wait is bounded; on
 // timeout the kernel records an error, every role stops, and the tensor memory is freed.
+
+#include <cuda.h>
 
 #include "enx_internal.cuh"
 #include "k_decode.cuh"
@@ -78,7 +80,7 @@ __host__ __device__ __forceinline__ uint32_t slot_element(int bits, uint32_t j) 
 // the largest |x| of the token's whole row, so the tensor-core epilogue applies 2^-F once at the
 // end.  A warp per token and chunk of kLimbChunk blocks: the row maximum, then per block two slots
 // per lane, limbs staged through shared memory so each lane stores one 16-byte chunk.
-constexpr uint32_t kLimbChunk = 8;
+constexpr uint32_t kLimbChunk = 2;
 
 __global__ void __launch_bounds__(256) k_limbs(const float* __restrict__ x, uint32_t ld, uint32_t M, uint32_t K,
                                                int bits, uint8_t* __restrict__ out) {
@@ -142,10 +144,11 @@ __global__ void __launch_bounds__(256) k_limbs(const float* __restrict__ x, uint
     }
 }
 
-constexpr uint32_t kTcStages = 4;
-constexpr int kTcEpiWarps = 8, kTcMmaWarp = 8, kTcProdWarp0 = 9;
-constexpr int kTcProdWarps = 2;                          // producer: 64 threads, two rows each
-constexpr int kTcWsThreads = (kTcEpiWarps + 1 + kTcProdWarps) * 32;  // 352: at most 3 warps per SMSP
+constexpr uint32_t kTcStages = 8;  // loads take ~2 us to land: 8 blocks in flight
+constexpr int kTcEpiGroups = 4;                          // epilogue warpgroups
+constexpr int kTcEpiTok = kTcTokens / kTcEpiGroups;      // tokens per epilogue thread (8)
+constexpr int kTcEpiWarps = 4 * kTcEpiGroups, kTcMmaWarp = kTcEpiWarps, kTcProdWarp = kTcEpiWarps + 1;
+constexpr int kTcWsThreads = (kTcEpiWarps + 2) * 32;     // 576
 constexpr uint32_t kTcATile = kTcRows * 64;               // 8 KB of codes per block
 constexpr uint32_t kTcMaxSplit = 16;
 
@@ -169,80 +172,60 @@ __device__ __forceinline__ void mbar_arrive(uint64_t* bar) {
     asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(su32(bar)) : "memory");
 }
 
-// Raw ring: the packed codes of one block for the CTA's 128 rows as stored (row-major, 32 or 64
-// bytes per row) and, for int4, each row's zero-point word; fetched with cp.async kTcRaw blocks
-// ahead of their unpacking.  A producer thread only ever reads back bytes it copied itself.
-constexpr uint32_t kTcRaw = 4;
-template <int BITS>
-struct RawGeom {
-    static constexpr uint32_t kRowBytes = 2 * BITS * 4;           // 32 (int4) or 64 (int8)
-    static constexpr uint32_t kCodes = kTcRows * kRowBytes;       // per block
-    static constexpr uint32_t kBytes = kCodes + kTcRows * 4;      // + zero words
-};
-
-__device__ __forceinline__ void cp_async16(void* dst, const void* src, bool ok) {
-    asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;" ::"r"(su32(dst)), "l"(src), "r"(ok ? 16 : 0)
-                 : "memory");
-}
-__device__ __forceinline__ void cp_async4(void* dst, const void* src, bool ok) {
-    asm volatile("cp.async.ca.shared.global [%0], [%1], 4, %2;" ::"r"(su32(dst)), "l"(src), "r"(ok ? 4 : 0)
-                 : "memory");
+// Code tiles arrive by TMA from a byte matrix [rows][K] (int8 codes as stored; int4 as the signed
+// bytes q - z prepared by k_codes_i8): per block four 2D boxes of 16 bytes x 128 rows, one per
+// 16-byte chunk of the block, land as four chunk planes.  Each 8-row x 16-byte core matrix is then
+// contiguous, K-adjacent core matrices are 2048 bytes apart and row-adjacent ones 128 bytes apart,
+// which is the K-major, unswizzled layout the MMA descriptor below describes.
+__device__ __forceinline__ uint64_t mdesc_a(uint32_t addr) {
+    return (uint64_t)((addr >> 4) & 0x3FFF) | ((uint64_t)(2048 >> 4) << 16) | ((uint64_t)(128 >> 4) << 32) | (1ull << 46);
 }
 
-// Copies row `row`'s codes (and int4 zero word) of block b into raw slot `raw`.
-template <int BITS>
-__device__ __forceinline__ void fetch_row(uint8_t* raw, const QW& w, uint32_t r0, uint32_t row, uint32_t b) {
-    using G = RawGeom<BITS>;
-    const uint32_t K = w.cols, gr = r0 + row;
-    const bool ok = gr < w.rows;
-    const uint8_t* src = reinterpret_cast<const uint8_t*>(w.packed) + ((size_t)(ok ? gr : 0) * (K * BITS / 8)) +
-                         (size_t)b * G::kRowBytes;
+__device__ __forceinline__ void tma_codes(uint8_t* dst, const CUtensorMap* map, uint32_t block, uint32_t row,
+                                          uint64_t* bar) {
 #pragma unroll
-    for (uint32_t c = 0; c < G::kRowBytes / 16; ++c) cp_async16(raw + row * G::kRowBytes + c * 16, src + c * 16, ok);
-    if (BITS == 4) {
-        const uint32_t blk = (ok ? gr : 0) * (K / kBlock) + b;
-        cp_async4(raw + G::kCodes + row * 4, w.zeros + (blk >> 3), ok);
-    }
+    for (uint32_t c = 0; c < 4; ++c)  // x = 64 * block + 16 * c bytes: 16-byte aligned
+        asm volatile(
+            "cp.async.bulk.tensor.2d.shared::cluster.global.tile.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3}], [%4];" ::"r"(
+                su32(dst + c * 2048)),
+            "l"(map), "r"(block * 64 + c * 16), "r"(row), "r"(su32(bar))
+            : "memory");
 }
 
-// Unpacks row `row` of raw slot `raw` (block b) into the K-major canonical code tile.
-template <int BITS>
-__device__ __forceinline__ void unpack_row(const uint8_t* raw, uint8_t* tile, uint32_t row, uint32_t blk) {
-    using G = RawGeom<BITS>;
-    const uint4* q = reinterpret_cast<const uint4*>(raw + row * G::kRowBytes);
-    if (BITS == 4) {
-        // zero code of (row, block): nibble blk & 7 of the zero word fetched for it (blk = the
-        // row's block index gr * K/64 + b)
-        const uint32_t z = (*reinterpret_cast<const uint32_t*>(raw + G::kCodes + row * 4) >> ((blk & 7u) * 4u)) & 0xFu;
-        const uint32_t zz = z * 0x01010101u;
+// int4 codes to the byte matrix the GEMM reads: per row and 64-element block, the signed bytes
+// q - z in MMA slot order (the low nibbles of the block's 32 packed bytes, then the high ones).
+// A thread per (row, block).
+__global__ void k_codes_i8(QW w, uint8_t* __restrict__ out) {
+    const uint32_t nb = w.cols / kBlock;
+    const size_t i = (size_t)blockIdx.x * blockDim.x + threadIdx.x;
+    if (i >= (size_t)w.rows * nb) return;
+    const uint32_t row = (uint32_t)(i / nb), b = (uint32_t)(i % nb);
+    const uint4* q = reinterpret_cast<const uint4*>(w.packed + (size_t)row * (w.cols / 8) + b * 8);
+    const uint32_t zz = zero_code<4>(w.zeros, row * nb + b) * 0x01010101u;
+    uint4* dst = reinterpret_cast<uint4*>(out + (size_t)row * w.cols + (size_t)b * kBlock);
 #pragma unroll
-        for (int h = 0; h < 2; ++h) {  // words 4h..4h+3: low nibbles to k-bytes 16h.., high to 32+16h..
-            const uint4 v = q[h];
-            const uint32_t ww[4] = {v.x, v.y, v.z, v.w};
-            uint32_t lo[4], hi[4];
+    for (int h = 0; h < 2; ++h) {  // words 4h..4h+3: low nibbles to bytes 16h.., high to 32+16h..
+        const uint4 v = __ldg(q + h);
+        const uint32_t ww[4] = {v.x, v.y, v.z, v.w};
+        uint32_t lo[4], hi[4];
 #pragma unroll
-            for (int i = 0; i < 4; ++i) {  // q - z per byte: a signed byte in [-15, 15]
-                lo[i] = __vsub4(ww[i] & 0x0F0F0F0Fu, zz);
-                hi[i] = __vsub4((ww[i] >> 4) & 0x0F0F0F0Fu, zz);
-            }
-            *reinterpret_cast<uint4*>(tile + canon(row, h * 16)) = make_uint4(lo[0], lo[1], lo[2], lo[3]);
-            *reinterpret_cast<uint4*>(tile + canon(row, 32 + h * 16)) = make_uint4(hi[0], hi[1], hi[2], hi[3]);
+        for (int k = 0; k < 4; ++k) {  // per byte ((q | 0x80) - z) ^ 0x80: no borrow, 0x80 + q - z >= 0x71
+            lo[k] = (((ww[k] & 0x0F0F0F0Fu) | 0x80808080u) - zz) ^ 0x80808080u;
+            hi[k] = ((((ww[k] >> 4) & 0x0F0F0F0Fu) | 0x80808080u) - zz) ^ 0x80808080u;
         }
-    } else {
-#pragma unroll
-        for (int i = 0; i < 4; ++i) *reinterpret_cast<uint4*>(tile + canon(row, i * 16)) = q[i];
+        dst[h] = make_uint4(lo[0], lo[1], lo[2], lo[3]);
+        dst[2 + h] = make_uint4(hi[0], hi[1], hi[2], hi[3]);
     }
 }
 
 template <int BITS>
 __global__ void __launch_bounds__(kTcWsThreads, 1)
-    k_gemm_tc(const uint8_t* __restrict__ limbs, QW w, const float* __restrict__ bias, float* __restrict__ out,
-              double* __restrict__ partial, uint32_t M, uint32_t out_stride, uint32_t out_offset, uint32_t blocks_per_split,
-              uint32_t* err) {
+    k_gemm_tc(const __grid_constant__ CUtensorMap cmap, const uint8_t* __restrict__ limbs, QW w,
+              const float* __restrict__ bias, float* __restrict__ out, double* __restrict__ partial, uint32_t M,
+              uint32_t out_stride, uint32_t out_offset, uint32_t blocks_per_split, uint32_t* err) {
     extern __shared__ __align__(1024) uint8_t smem[];
     uint8_t* sA = smem;                                // [stages][kTcATile]
     uint8_t* sB = smem + kTcStages * kTcATile;         // [stages][kTcLimbTileBytes]
-    uint8_t* sR = sB + kTcStages * kTcLimbTileBytes;   // [kTcRaw][RawGeom::kBytes]
     __shared__ __align__(8) uint64_t full[kTcStages], empty[kTcStages], accf[2], acce[2];
     __shared__ uint32_t tmem_base;
     __shared__ volatile int s_fail;
@@ -262,7 +245,7 @@ __global__ void __launch_bounds__(kTcWsThreads, 1)
     if (tid == 0) {
         s_fail = 0;
         for (uint32_t i = 0; i < kTcStages; ++i) {
-            asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(su32(&full[i])), "r"(kTcProdWarps * 32));
+            asm volatile("mbarrier.init.shared::cta.b64 [%0], 1;" ::"r"(su32(&full[i])));
             asm volatile("mbarrier.init.shared::cta.b64 [%0], 1;" ::"r"(su32(&empty[i])));
         }
         for (int i = 0; i < 2; ++i) {
@@ -276,43 +259,24 @@ __global__ void __launch_bounds__(kTcWsThreads, 1)
     asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
     const uint32_t tmem = tmem_base;
 
-    if (warp >= kTcProdWarp0) {
-        // ---- producer: thread = rows p and p + 64 ---------------------------------------------------
-        using G = RawGeom<BITS>;
-        const uint32_t p = tid - kTcProdWarp0 * 32;
-        for (uint32_t j = 0; j < kTcRaw; ++j) {  // prologue: blocks 0..kTcRaw-1 in flight
-            if (j < nblk) {
-                fetch_row<BITS>(sR + j * G::kBytes, w, r0, p, kb0 + j);
-                fetch_row<BITS>(sR + j * G::kBytes, w, r0, p + 64, kb0 + j);
-            }
-            asm volatile("cp.async.commit_group;" ::: "memory");
-        }
-        pdl_wait();  // the limb tiles (previous grid) are complete from here on
-        for (uint32_t i = 0; i < nblk; ++i) {
-            const uint32_t s = i % kTcStages, rs = i % kTcRaw;
-            if (i >= kTcStages && !mbar_wait_f(&empty[s], ((i / kTcStages) - 1) & 1, &s_fail, err)) break;
-            if (p == 0) {
-                asm volatile("mbarrier.expect_tx.relaxed.cta.shared::cta.b64 [%0], %1;" ::"r"(su32(&full[s])),
-                             "r"(kTcLimbTileBytes)
+    if (warp == kTcProdWarp) {
+        // ---- producer: one thread, a TMA box of codes and a bulk copy of limbs per block ------------
+        if (lane == 0) {
+            for (uint32_t i = 0; i < nblk; ++i) {
+                const uint32_t s = i % kTcStages;
+                if (i >= kTcStages && !mbar_wait_f(&empty[s], ((i / kTcStages) - 1) & 1, &s_fail, err)) break;
+                asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(su32(&full[s])),
+                             "r"(kTcATile + kTcLimbTileBytes)
                              : "memory");
+                tma_codes(sA + s * kTcATile, &cmap, kb0 + i, r0, &full[s]);  // weights: no wait needed
+                if (i == 0) pdl_wait();  // the limb tiles (previous grid) are complete from here on
                 asm volatile("cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(
                                  su32(sB + s * kTcLimbTileBytes)),
                              "l"(ltile + (size_t)(kb0 + i) * kTcLimbTileBytes), "r"(kTcLimbTileBytes), "r"(su32(&full[s]))
                              : "memory");
             }
-            asm volatile("cp.async.wait_group %0;" ::"n"(kTcRaw - 1) : "memory");  // block i's raw codes landed
-            // unpack_row takes the (row, block) index: its low 3 bits pick the int4 zero nibble
-            unpack_row<BITS>(sR + rs * G::kBytes, sA + s * kTcATile, p, (r0 + p) * bpr + kb0 + i);
-            unpack_row<BITS>(sR + rs * G::kBytes, sA + s * kTcATile, p + 64, (r0 + p + 64) * bpr + kb0 + i);
-            asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
-            mbar_arrive(&full[s]);
-            if (i + kTcRaw < nblk) {  // refill the slot this thread just read
-                fetch_row<BITS>(sR + rs * G::kBytes, w, r0, p, kb0 + i + kTcRaw);
-                fetch_row<BITS>(sR + rs * G::kBytes, w, r0, p + 64, kb0 + i + kTcRaw);
-            }
-            asm volatile("cp.async.commit_group;" ::: "memory");
         }
-        asm volatile("cp.async.wait_all;" ::: "memory");
+        __syncwarp();
     } else if (warp == kTcMmaWarp) {
         // ---- MMA issue: one thread ----------------------------------------------------------------
         pdl_wait();
@@ -324,8 +288,8 @@ __global__ void __launch_bounds__(kTcWsThreads, 1)
                 asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
                 const uint32_t dcol = tmem + a * kTcN;
 #pragma unroll
-                for (uint32_t kk = 0; kk < 2; ++kk) {
-                    const uint64_t ad = mdesc(su32(sA + s * kTcATile) + kk * 256);
+                for (uint32_t kk = 0; kk < 2; ++kk) {  // K = 32 per MMA: two chunk planes of A
+                    const uint64_t ad = mdesc_a(su32(sA + s * kTcATile) + kk * 4096);
                     const uint64_t bd = mdesc(su32(sB + s * kTcLimbTileBytes) + kk * 256);
                     asm volatile("{\n .reg .pred p;\n setp.ne.b32 p, %4, 0;\n tcgen05.mma.cta_group::1.kind::i8 [%0], %1, %2, %3, p;\n}\n" ::"r"(
                                      dcol),
@@ -341,13 +305,13 @@ __global__ void __launch_bounds__(kTcWsThreads, 1)
         }
         __syncwarp();
     } else {
-        // ---- epilogue: warpgroup wg, tokens 16wg..16wg+15, thread = row 32*(warp%4) + lane ---------
+        // ---- epilogue: warpgroup wg, tokens 8wg..8wg+7, thread = row 32*(warp%4) + lane -------------
         pdl_wait();  // limb records and the output may be touched from here on
         const uint32_t wg = warp >> 2, erow = 32 * (warp & 3) + lane, grow = r0 + erow;
         const bool rok = grow < w.rows;
-        double acc[16];
+        double acc[kTcEpiTok];
 #pragma unroll
-        for (int i = 0; i < 16; ++i) acc[i] = 0.0;
+        for (int i = 0; i < kTcEpiTok; ++i) acc[i] = 0.0;
         float sc_next = (nblk && rok) ? __ldg(w.scales + (size_t)grow * bpr + kb0) : 0.f;
         uint32_t z_next = (BITS == 8 && nblk && rok) ? zero_code<BITS>(w.zeros, grow * bpr + kb0) : 0u;
         for (uint32_t i = 0; i < nblk; ++i) {
@@ -364,16 +328,16 @@ __global__ void __launch_bounds__(kTcWsThreads, 1)
             asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
             // per token of this block (int8 only): the X sum, from the limb tile in global memory
             const int* tok = reinterpret_cast<const int*>(ltile + (size_t)b * kTcLimbTileBytes + kTcN * 64) +
-                             (wg * 16) * 4;
+                             (wg * kTcEpiTok) * 4;
             // tokens in groups of kTok (8 for int4, 4 for int8: register pressure), one TMEM wait each
-            constexpr int kTok = BITS == 4 ? 8 : 4, kLd = kTok / 4, kGroups = 16 / kTok;
+            constexpr int kTok = 4, kLd = 1, kGroups = kTcEpiTok / kTok;
 #pragma unroll
             for (int hh = 0; hh < kGroups; ++hh) {
                 uint32_t d[kLd][32];
 #pragma unroll
                 for (int tq = 0; tq < kLd; ++tq) {  // four tokens (32 accumulator columns) per TMEM load
                     const uint32_t ta =
-                        tmem + ((uint32_t)(32 * (warp & 3)) << 16) + a * kTcN + (wg * 16 + hh * kTok + tq * 4) * 8;
+                        tmem + ((uint32_t)(32 * (warp & 3)) << 16) + a * kTcN + (wg * kTcEpiTok + hh * kTok + tq * 4) * 8;
                     asm volatile(
                         "tcgen05.ld.sync.aligned.32x32b.x32.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,"
                         "%16,%17,%18,%19,%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31}, [%32];"
@@ -387,7 +351,7 @@ __global__ void __launch_bounds__(kTcWsThreads, 1)
                         : "r"(ta));
                 }
                 asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
-                if (hh == kGroups - 1) {  // all 16 tokens are in registers: accumulator a may take block i + 2
+                if (hh == kGroups - 1) {  // all the warp's tokens are in registers: accumulator a may take block i + 2
                     asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
                     __syncwarp();
                     if (lane == 0) mbar_arrive(&acce[a]);
@@ -413,19 +377,19 @@ __global__ void __launch_bounds__(kTcWsThreads, 1)
             // each token's 2^-F (the same in every block's record), applied once: exact
             const double* rec = reinterpret_cast<const double*>(ltile + (size_t)kb0 * kTcLimbTileBytes + kTcN * 64);
 #pragma unroll
-            for (int tt = 0; tt < 16; ++tt) acc[tt] *= __ldg(rec + 2 * (wg * 16 + tt) + 1);
+            for (int tt = 0; tt < kTcEpiTok; ++tt) acc[tt] *= __ldg(rec + 2 * (wg * kTcEpiTok + tt) + 1);
             if (partial) {  // split-K: this split's double partial, [split][M][rows]
                 double* pp = partial + (size_t)blockIdx.z * M * w.rows;
 #pragma unroll
-                for (int tt = 0; tt < 16; ++tt) {
-                    const uint32_t m = g * kTcTokens + wg * 16 + tt;
+                for (int tt = 0; tt < kTcEpiTok; ++tt) {
+                    const uint32_t m = g * kTcTokens + wg * kTcEpiTok + tt;
                     if (m < M) pp[(size_t)m * w.rows + grow] = acc[tt];
                 }
             } else {
                 const double bv = bias ? (double)__ldg(bias + grow) : 0.0;
 #pragma unroll
-                for (int tt = 0; tt < 16; ++tt) {
-                    const uint32_t m = g * kTcTokens + wg * 16 + tt;
+                for (int tt = 0; tt < kTcEpiTok; ++tt) {
+                    const uint32_t m = g * kTcTokens + wg * kTcEpiTok + tt;
                     if (m < M) out[(size_t)m * out_stride + out_offset + grow] = (float)(acc[tt] + bv);
                 }
             }
@@ -484,26 +448,54 @@ static size_t partial_rows(uint32_t m) {
     return 4 * 148 * (size_t)kTcRows / groups + kTcRows;
 }
 
-size_t gemm_tc_workspace_bytes(uint32_t m, uint32_t k) {
-    return limb_bytes(m, k) + (size_t)m * partial_rows(m) * sizeof(double) + 256;
+static size_t partial_bytes(uint32_t m) { return ((size_t)m * partial_rows(m) * sizeof(double) + 255) / 256 * 256; }
+
+size_t gemm_tc_workspace_bytes(uint32_t m, uint32_t k) { return limb_bytes(m, k) + partial_bytes(m); }
+
+size_t gemm_tc_codes_bytes(uint32_t rows, uint32_t k) { return ((size_t)rows * k + 255) / 256 * 256; }
+
+cudaError_t launch_codes_i8(const QW& w, uint8_t* out, cudaStream_t st) {
+    const size_t n = (size_t)w.rows * (w.cols / kBlock);
+    k_codes_i8<<<(unsigned)((n + 255) / 256), 256, 0, st>>>(w, out);
+    return cudaGetLastError();
 }
 
-cudaError_t launch_gemm_tc(int bits, const float* x, uint32_t ld, const QW& w, const float* bias, float* out,
-                           uint32_t m, uint32_t out_stride, uint32_t out_offset, uint8_t* workspace, uint32_t* err,
-                           cudaStream_t st) {
+cudaError_t launch_gemm_tc(int bits, const float* x, uint32_t ld, const QW& w, const uint8_t* codes8, const float* bias,
+                           float* out, uint32_t m, uint32_t out_stride, uint32_t out_offset, uint8_t* workspace,
+                           uint32_t* err, cudaStream_t st) {
     const uint32_t groups = (m + kTcTokens - 1) / kTcTokens, nb = w.cols / kBlock;
+    cudaError_t e;
+    if (bits == 8) {
+        codes8 = reinterpret_cast<const uint8_t*>(w.packed);  // int8 codes are the byte matrix already
+    } else if (!codes8) {  // no prepared copy: convert into the workspace's code region
+        uint8_t* conv = workspace + limb_bytes(m, w.cols) + partial_bytes(m);
+        e = launch_codes_i8(w, conv, st);
+        if (e != cudaSuccess) return e;
+        codes8 = conv;
+    }
     k_limbs<<<dim3(groups * (kTcTokens / 8), (nb + kLimbChunk - 1) / kLimbChunk), 256, 0, st>>>(x, ld, m, w.cols, bits,
                                                                                           workspace);
-    cudaError_t e = cudaGetLastError();
+    e = cudaGetLastError();
     if (e != cudaSuccess) return e;
+    // the code bytes as a 2D tensor (K bytes x rows); a box is one 16-byte chunk of 128 rows
+    CUtensorMap cmap;
+    {
+        const cuuint64_t dims[2] = {w.cols, w.rows};
+        const cuuint64_t strides[1] = {w.cols};
+        const cuuint32_t box[2] = {16, kTcRows};
+        const cuuint32_t estr[2] = {1, 1};
+        const CUresult r = cuTensorMapEncodeTiled(&cmap, CU_TENSOR_MAP_DATA_TYPE_UINT8, 2, (void*)codes8, dims, strides,
+                                                  box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE,
+                                                  CU_TENSOR_MAP_L2_PROMOTION_L2_128B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+        if (r != CUDA_SUCCESS) return cudaErrorInvalidValue;
+    }
     uint32_t splits = tc_splits(m, w.rows, w.cols);
     while (splits > 1 && (size_t)splits * w.rows > partial_rows(m)) --splits;  // workspace bound
     const uint32_t per = (nb + splits - 1) / splits;
     double* partial = splits > 1 ? reinterpret_cast<double*>(workspace + limb_bytes(m, w.cols)) : nullptr;
-    const size_t smem = (size_t)kTcStages * (kTcATile + kTcLimbTileBytes) +
-                        (size_t)kTcRaw * (bits == 4 ? RawGeom<4>::kBytes : RawGeom<8>::kBytes);
+    const size_t smem = (size_t)kTcStages * (kTcATile + kTcLimbTileBytes);
     const dim3 grid(groups, (w.rows + kTcRows - 1) / kTcRows, splits);
-    // programmatic dependent launch: the prologue and the weight prefetch overlap k_limbs
+    // programmatic dependent launch: the prologue and the code loads overlap k_limbs
     cudaLaunchConfig_t cfg = {};
     cfg.gridDim = grid;
     cfg.blockDim = dim3(kTcWsThreads);
@@ -517,13 +509,13 @@ cudaError_t launch_gemm_tc(int bits, const float* x, uint32_t ld, const QW& w, c
     if (bits == 4) {
         e = cudaFuncSetAttribute(k_gemm_tc<4>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
         if (e == cudaSuccess)
-            e = cudaLaunchKernelEx(&cfg, k_gemm_tc<4>, (const uint8_t*)workspace, w, bias, out, partial, m, out_stride,
-                                   out_offset, per, err);
+            e = cudaLaunchKernelEx(&cfg, k_gemm_tc<4>, cmap, (const uint8_t*)workspace, w, bias, out, partial, m,
+                                   out_stride, out_offset, per, err);
     } else {
         e = cudaFuncSetAttribute(k_gemm_tc<8>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
         if (e == cudaSuccess)
-            e = cudaLaunchKernelEx(&cfg, k_gemm_tc<8>, (const uint8_t*)workspace, w, bias, out, partial, m, out_stride,
-                                   out_offset, per, err);
+            e = cudaLaunchKernelEx(&cfg, k_gemm_tc<8>, cmap, (const uint8_t*)workspace, w, bias, out, partial, m,
+                                   out_stride, out_offset, per, err);
     }
     if (e == cudaSuccess) e = cudaGetLastError();
     if (e != cudaSuccess || splits == 1) return e;

@@ -9,14 +9,22 @@ namespace enx {
 // token the block sum of the scaled activations (int64) and its scale 2^-F (double).
 constexpr uint32_t kTcLimbTileBytes = 256 * 64 + 32 * 16;
 
-// Workspace for launch_gemm_tc: the limb tiles of m tokens over k.
+// Workspace for launch_gemm_tc: the limb tiles of m tokens over k and the split-K partials.
 size_t gemm_tc_workspace_bytes(uint32_t m, uint32_t k);
+// Extra workspace when an int4 call passes no prepared code matrix (converted per call).
+size_t gemm_tc_codes_bytes(uint32_t rows, uint32_t k);
+
+// The byte matrix [rows][cols] the GEMM reads for int4 weights: q - z per element, in the GEMM's
+// slot order (gemm_tc_codes_bytes(rows, cols) bytes).  Prepared once per weight by callers that
+// reuse it.
+cudaError_t launch_codes_i8(const QW& w, uint8_t* out, cudaStream_t st);
 
 // out[t * out_stride + out_offset + n] = float(x[t] . W[n] (+ bias[n])) for t < m, n < w.rows;
-// x rows ld floats apart.  bits 4 or 8; w.cols a multiple of 64.  *err is raised to 3 if a
-// bounded wait inside the kernel gives up.
-cudaError_t launch_gemm_tc(int bits, const float* x, uint32_t ld, const QW& w, const float* bias, float* out,
-                           uint32_t m, uint32_t out_stride, uint32_t out_offset, uint8_t* workspace, uint32_t* err,
-                           cudaStream_t st);
+// x rows ld floats apart.  bits 4 or 8; w.cols a multiple of 64.  codes8: the prepared int4 byte
+// matrix, or null to convert into the workspace (which then needs gemm_tc_codes_bytes more).
+// *err is raised to 3 if a bounded wait inside the kernel gives up.
+cudaError_t launch_gemm_tc(int bits, const float* x, uint32_t ld, const QW& w, const uint8_t* codes8, const float* bias,
+                           float* out, uint32_t m, uint32_t out_stride, uint32_t out_offset, uint8_t* workspace,
+                           uint32_t* err, cudaStream_t st);
 
 }  // namespace enx
