@@ -47,7 +47,7 @@ def build(verbose: bool = False) -> Path:
         objs = list(ex.map(_compile, srcs))
     if not LIB.exists() or LIB.stat().st_mtime < max(o.stat().st_mtime for o in objs):
         tmp = LIB.with_suffix(".so.tmp")
-        cmd = [nvcc(), *ARCH, "-shared", "-o", str(tmp), *map(str, objs), "-lcuda"]
+        cmd = [nvcc(), *ARCH, "-shared", "-o", str(tmp), *map(str, objs)]
         r = subprocess.run(cmd, capture_output=True, text=True)
         if r.returncode != 0:
             raise RuntimeError(f"link failed:\n{r.stderr}")

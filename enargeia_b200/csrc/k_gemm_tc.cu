@@ -460,6 +460,23 @@ cudaError_t launch_codes_i8(const QW& w, uint8_t* out, cudaStream_t st) {
     return cudaGetLastError();
 }
 
+// cuTensorMapEncodeTiled, looked up through the runtime so the library needs no link-time driver
+// dependency (it loads on hosts without a GPU driver, where only its exports are inspected).
+typedef CUresult (*EncodeTiledFn)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*, const cuuint64_t*,
+                                  const cuuint64_t*, const cuuint32_t*, const cuuint32_t*, CUtensorMapInterleave,
+                                  CUtensorMapSwizzle, CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
+static EncodeTiledFn encode_tiled() {
+    static EncodeTiledFn fn = [] {
+        void* p = nullptr;
+        cudaDriverEntryPointQueryResult q;
+        if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) != cudaSuccess ||
+            q != cudaDriverEntryPointSuccess)
+            p = nullptr;
+        return reinterpret_cast<EncodeTiledFn>(p);
+    }();
+    return fn;
+}
+
 cudaError_t launch_gemm_tc(int bits, const float* x, uint32_t ld, const QW& w, const uint8_t* codes8, const float* bias,
                            float* out, uint32_t m, uint32_t out_stride, uint32_t out_offset, uint8_t* workspace,
                            uint32_t* err, cudaStream_t st) {
@@ -484,9 +501,11 @@ cudaError_t launch_gemm_tc(int bits, const float* x, uint32_t ld, const QW& w, c
         const cuuint64_t strides[1] = {w.cols};
         const cuuint32_t box[2] = {16, kTcRows};
         const cuuint32_t estr[2] = {1, 1};
-        const CUresult r = cuTensorMapEncodeTiled(&cmap, CU_TENSOR_MAP_DATA_TYPE_UINT8, 2, (void*)codes8, dims, strides,
-                                                  box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE,
-                                                  CU_TENSOR_MAP_L2_PROMOTION_L2_128B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+        const EncodeTiledFn encode = encode_tiled();
+        if (!encode) return cudaErrorNotSupported;
+        const CUresult r = encode(&cmap, CU_TENSOR_MAP_DATA_TYPE_UINT8, 2, (void*)codes8, dims, strides, box, estr,
+                                  CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE,
+                                  CU_TENSOR_MAP_L2_PROMOTION_L2_128B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
         if (r != CUDA_SUCCESS) return cudaErrorInvalidValue;
     }
     uint32_t splits = tc_splits(m, w.rows, w.cols);
