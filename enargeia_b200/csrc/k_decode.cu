@@ -443,12 +443,24 @@ cudaError_t launch_matmul(int bits, const float* x, const QW& w, const float* bi
                      : launch_matmul_bits<4>(x, w, bias, out, m, out_stride, out_offset, st, pdl);
 }
 
-// Many-token attention, scores: one CTA per (kv head, split of kAttnSplit positions, token), a
-// thread per position holding all the group's heads (kMaxGroupSplit accumulators).  The thread
-// reads its K row (f16) straight into registers and takes the dot products with the group's
-// query heads (doubles in shared memory, warp-wide broadcasts) in double, dimension pairs in
-// order: scores[t][h][j] = float(sum_d q[h][d] * K[j][d] / sqrt(hd)) (test/reference/ops.ts:123-151).
+// Many-token attention on the f64 tensor cores (mma.sync m8n8k4 .f64: D[8x8] += A[8x4] B[4x8]).
+// Lane roles in a fragment: A row / D row = lane / 4, A column / B row (the k index) = lane % 4,
+// B column = lane / 4, D columns = 2 (lane % 4) + {0, 1}.
 constexpr uint32_t kMaxGroupSplit = 8;
+
+__device__ __forceinline__ void dmma(double& d0, double& d1, double a, double b) {
+    asm volatile("mma.sync.aligned.m8n8k4.row.col.f64.f64.f64.f64 {%0, %1}, {%2}, {%3}, {%0, %1};"
+                 : "+d"(d0), "+d"(d1)
+                 : "d"(a), "d"(b));
+}
+
+// Scores: one CTA per (kv head, split of kAttnSplit positions, token), a warp per 8 positions at a
+// time: D[head][position] over the group's query heads (rows, 8 at most) and 8 positions
+// (columns), k running over the head dimension.  Lane k-slot q (lane % 4) owns dimensions
+// q*hd/4 .. q*hd/4 + hd/4 - 1, and MMA step s uses dimension q*hd/4 + s in both operands, so A
+// (its head's query, widened once) stays in registers and B is one coalesced read of the lane's
+// hd/4 K values per position.  scores[t][h][j] = float(sum_d q[h][d] * K[j][d] / sqrt(hd)), the
+// products exact in double (test/reference/ops.ts:123-151).
 __global__ void __launch_bounds__(kAttnSplit) k_attn_scores_split(StepArgs S, uint32_t layer) {
     pdl_launch_dependents();
     pdl_wait();
@@ -457,41 +469,42 @@ __global__ void __launch_bounds__(kAttnSplit) k_attn_scores_split(StepArgs S, ui
     const uint32_t npos = S.pos_of(t) + 1, j0 = sp * kAttnSplit;
     if (j0 >= npos) return;
     const uint32_t n = min(kAttnSplit, npos - j0);
-    __shared__ __align__(16) double qd[kMaxGroupSplit * 64];  // [group][hd]
-    for (uint32_t i = threadIdx.x; i < group * hd; i += blockDim.x)
-        qd[i] = (double)__ldcg(S.q + (size_t)t * S.hidden + g * group * hd + i);
-    __syncthreads();
-    const uint32_t j = threadIdx.x;
-    if (j >= n) return;
-    const uint4* kr = reinterpret_cast<const uint4*>(S.kcache + S.cache_offset(S.seq_of(t), layer, j0 + j) + g * hd);
-    uint4 kq[8];
+    const uint32_t warp = threadIdx.x >> 5, lane = threadIdx.x & 31, row = lane >> 2, quad = lane & 3;
+    const uint32_t steps = hd / 4, base = quad * steps;  // hd in {32, 64}: 8 or 16 steps
+    double qa[16];
+    const float* qrow = S.q + (size_t)t * S.hidden + (size_t)(g * group + row) * hd + base;
 #pragma unroll
-    for (uint32_t c = 0; c < 8; ++c) kq[c] = c < hd / 8 ? __ldcg(kr + c) : make_uint4(0, 0, 0, 0);
-    double acc[kMaxGroupSplit];
+    for (uint32_t s = 0; s < 16; ++s) qa[s] = (row < group && s < steps) ? (double)__ldcg(qrow + s) : 0.0;
+    const double scale = 1.0 / sqrt((double)hd);
+    const uint16_t* K = S.kcache + S.cache_offset(S.seq_of(t), layer, j0) + g * hd + base;
+    float* out = S.scores + ((size_t)t * S.heads + g * group + row) * S.score_stride + j0;
+    // the warp's positions p0 = 8 warp + 32 i, i < 4: all K reads issued before the first MMA
+    uint4 kv[4][2];
 #pragma unroll
-    for (int h = 0; h < (int)kMaxGroupSplit; ++h) acc[h] = 0.0;
-#pragma unroll
-    for (uint32_t c = 0; c < 8; ++c) {
-        if (c >= hd / 8) break;
-        const __half2* h2 = reinterpret_cast<const __half2*>(&kq[c]);
-#pragma unroll
-        for (int e = 0; e < 4; ++e) {
-            const float2 kf = __half22float2(h2[e]);
-            const double kx = kf.x, ky = kf.y;
-            const uint32_t d2 = c * 4 + e;
-#pragma unroll
-            for (int h = 0; h < (int)kMaxGroupSplit; ++h) {
-                if (h < (int)group) {
-                    const double2 qv = reinterpret_cast<const double2*>(qd + h * hd)[d2];
-                    acc[h] = fma(qv.y, ky, fma(qv.x, kx, acc[h]));
-                }
-            }
+    for (uint32_t i = 0; i < 4; ++i) {
+        const uint32_t pos = warp * 8 + 32 * i + row;  // this lane's B column
+        kv[i][0] = kv[i][1] = make_uint4(0, 0, 0, 0);
+        if (pos < n) {
+            const uint4* kp = reinterpret_cast<const uint4*>(K + (size_t)pos * kvd);
+            kv[i][0] = __ldcg(kp);
+            if (steps > 8) kv[i][1] = __ldcg(kp + 1);
         }
     }
-    const double scale = 1.0 / sqrt((double)hd);
 #pragma unroll
-    for (int h = 0; h < (int)kMaxGroupSplit; ++h)
-        if (h < (int)group) S.scores[((size_t)t * S.heads + g * group + h) * S.score_stride + j0 + j] = (float)(acc[h] * scale);
+    for (uint32_t i = 0; i < 4; ++i) {
+        const uint32_t p0 = warp * 8 + 32 * i;
+        if (p0 >= n) break;
+        const __half* kh = reinterpret_cast<const __half*>(kv[i]);
+        double d0 = 0.0, d1 = 0.0;
+#pragma unroll
+        for (uint32_t s = 0; s < 16; ++s)
+            if (s < steps) dmma(d0, d1, qa[s], (double)__half2float(kh[s]));
+        const uint32_t c0 = p0 + 2 * quad;  // D columns: positions c0, c0 + 1
+        if (row < group) {
+            if (c0 < n) out[c0] = (float)(d0 * scale);
+            if (c0 + 1 < n) out[c0 + 1] = (float)(d1 * scale);
+        }
+    }
 }
 
 // Many-token attention, after k_attn_scores: the softmax of every (token, head) row in place --
@@ -527,56 +540,64 @@ __global__ void __launch_bounds__(kThreads) k_attn_stats(StepArgs S) {
     for (uint32_t j = threadIdx.x; j < npos; j += blockDim.x) sc[j] = (float)((double)sc[j] / sum);
 }
 
-// Weighted V over one split of kAttnSplit positions for the query heads of one kv head, in double
-// (test/reference/ops.ts:181-204): attn_part[t][split][h][d].  A warp per quarter of the positions
-// and a lane per dimension pair holds every head of the group: each V pair (f16, read from global
-// memory by the lane, a coalesced row per warp) feeds all heads, the weights are shared-memory
-// broadcasts, and the quarters meet in fixed order.  Positions past the token's last are not read.
-// grid = (kv_heads, splits, ntok), 4 warps.
+// Weighted V on the f64 tensor cores: out[h][d] = sum_j w[h][j] V[j][d] over one split of
+// kApplySplit positions for the query heads of one kv head (test/reference/ops.ts:181-204), into
+// attn_part[t][split][h][d].  A warp per quarter of the split, 4 positions per MMA step: A = the
+// weights (head x position), B = V (position x 8 dimensions).  D column c of tile n holds
+// dimension c*hd/8 + n, so a lane (B column lane / 4) reads hd/8 contiguous f16 values of its
+// position per step.  The quarters meet in fixed order; positions past the token's last are not
+// read (the cache beyond it may hold stale bits).  grid = (kv_heads, splits, ntok), 4 warps.
 __global__ void __launch_bounds__(128) k_attn_apply_split(StepArgs S, uint32_t layer) {
     pdl_launch_dependents();
     pdl_wait();
     const uint32_t g = blockIdx.x, sp = blockIdx.y, t = blockIdx.z;
     const uint32_t hd = S.head_dim, group = S.heads / S.kv_heads, kvd = S.kv_heads * hd;
-    const uint32_t npos = S.pos_of(t) + 1, j0 = sp * kAttnSplit;
+    const uint32_t npos = S.pos_of(t) + 1, j0 = sp * kApplySplit;
     if (j0 >= npos) return;
-    const uint32_t n = min(kAttnSplit, npos - j0);
-    __shared__ float ws[kMaxGroupSplit][kAttnSplit];        // weights of the split's positions
-    __shared__ double red[4][kMaxGroupSplit][64];            // per-quarter sums
-    for (uint32_t i = threadIdx.x; i < group * kAttnSplit; i += blockDim.x) {
-        const uint32_t h = i / kAttnSplit, jj = i % kAttnSplit;
-        ws[h][jj] = jj < n ? S.scores[((size_t)t * S.heads + g * group + h) * S.score_stride + j0 + jj] : 0.f;
-    }
-    __syncthreads();
-    const uint32_t lane = threadIdx.x & 31, q4 = threadIdx.x >> 5;  // dimension pair, position quarter
-    const uint32_t pairs = hd / 2;
-    if (lane < pairs) {
-        double ax[kMaxGroupSplit], ay[kMaxGroupSplit];
+    const uint32_t n = min(kApplySplit, npos - j0);
+    __shared__ double red[4][kMaxGroupSplit][64];  // per-quarter sums
+    const uint32_t warp = threadIdx.x >> 5, lane = threadIdx.x & 31, row = lane >> 2, quad = lane & 3;
+    const uint32_t tiles = hd / 8;  // 4 or 8
+    const float* W = S.scores + ((size_t)t * S.heads + g * group + row) * S.score_stride + j0;
+    const uint16_t* V = S.vcache + S.cache_offset(S.seq_of(t), layer, j0) + g * hd + row * tiles;
+    double acc[8][2];
 #pragma unroll
-        for (int h = 0; h < (int)kMaxGroupSplit; ++h) ax[h] = ay[h] = 0.0;
-        const uint32_t jb = q4 * (kAttnSplit / 4), je = jb + kAttnSplit / 4;
-        const __half2* V = reinterpret_cast<const __half2*>(S.vcache + S.cache_offset(S.seq_of(t), layer, j0) + g * hd) + lane;
-        const uint32_t rstride = kvd / 2;  // half2 per position
-#pragma unroll 4
-        for (uint32_t jj = jb; jj < je; jj += 2) {  // zero weights and rows past n keep the tail exact
-            const float2 f0 = jj < n ? __half22float2(__ldcg(V + (size_t)jj * rstride)) : make_float2(0.f, 0.f);
-            const float2 f1 = jj + 1 < n ? __half22float2(__ldcg(V + (size_t)(jj + 1) * rstride)) : make_float2(0.f, 0.f);
-            const double v0x = f0.x, v0y = f0.y, v1x = f1.x, v1y = f1.y;
+    for (int i = 0; i < 8; ++i) acc[i][0] = acc[i][1] = 0.0;
+    const uint32_t jb = warp * (kApplySplit / 4), je = min(jb + kApplySplit / 4, (n + 3) & ~3u);
+    constexpr uint32_t kAhead = 8;  // MMA steps whose weights and V rows are read before their MMAs
+    for (uint32_t k0 = jb; k0 < je; k0 += 4 * kAhead) {
+        double w[kAhead];
+        uint4 vv[kAhead];
 #pragma unroll
-            for (int h = 0; h < (int)kMaxGroupSplit; ++h) {
-                if (h < (int)group) {
-                    const float2 w = *reinterpret_cast<const float2*>(&ws[h][jj]);
-                    const double wx = w.x, wy = w.y;
-                    ax[h] = fma(wy, v1x, fma(wx, v0x, ax[h]));
-                    ay[h] = fma(wy, v1y, fma(wx, v0y, ay[h]));
+        for (uint32_t i = 0; i < kAhead; ++i) {
+            const uint32_t pos = k0 + 4 * i + quad;  // A column / B row
+            const bool live = k0 + 4 * i < je && pos < n;
+            w[i] = (row < group && live) ? (double)__ldcg(W + pos) : 0.0;
+            vv[i] = make_uint4(0, 0, 0, 0);
+            if (live) {
+                if (tiles == 8) vv[i] = __ldcg(reinterpret_cast<const uint4*>(V + (size_t)pos * kvd));
+                else {
+                    const uint2 h = __ldcg(reinterpret_cast<const uint2*>(V + (size_t)pos * kvd));
+                    vv[i].x = h.x;
+                    vv[i].y = h.y;
                 }
             }
         }
 #pragma unroll
-        for (int h = 0; h < (int)kMaxGroupSplit; ++h) {
-            if (h < (int)group) {
-                red[q4][h][2 * lane] = ax[h];
-                red[q4][h][2 * lane + 1] = ay[h];
+        for (uint32_t i = 0; i < kAhead; ++i) {
+            if (k0 + 4 * i >= je) break;
+            const __half* vh = reinterpret_cast<const __half*>(&vv[i]);
+#pragma unroll
+            for (uint32_t nn = 0; nn < 8; ++nn)
+                if (nn < tiles) dmma(acc[nn][0], acc[nn][1], w[i], (double)__half2float(vh[nn]));
+        }
+    }
+    if (row < group) {
+#pragma unroll
+        for (uint32_t nn = 0; nn < 8; ++nn) {
+            if (nn < tiles) {
+                red[warp][row][(2 * quad) * tiles + nn] = acc[nn][0];
+                red[warp][row][(2 * quad + 1) * tiles + nn] = acc[nn][1];
             }
         }
     }
@@ -585,7 +606,7 @@ __global__ void __launch_bounds__(128) k_attn_apply_split(StepArgs S, uint32_t l
     for (uint32_t o = threadIdx.x; o < group * hd; o += blockDim.x) {
         const uint32_t h = o / hd, d = o % hd;
         double v = 0.0;
-        for (uint32_t k = 0; k < 4; ++k) v += red[k][h][d];  // quarters in order
+        for (uint32_t k = 0; k < 4; ++k) v += red[k][h][d];  // quarters in order (empty ones hold 0)
         part[o] = v;
     }
 }
@@ -594,7 +615,7 @@ __global__ void __launch_bounds__(128) k_attn_apply_split(StepArgs S, uint32_t l
 __global__ void k_attn_combine(StepArgs S, float* out) {
     pdl_launch_dependents();
     pdl_wait();
-    const uint32_t t = blockIdx.x, nsp = (S.pos_of(t) + kAttnSplit) / kAttnSplit, stride = S.score_stride / kAttnSplit;
+    const uint32_t t = blockIdx.x, nsp = (S.pos_of(t) + kApplySplit) / kApplySplit, stride = S.score_stride / kAttnSplit;
     const double* part = S.attn_part + (size_t)t * stride * S.hidden;
     for (uint32_t o = threadIdx.x; o < S.hidden; o += blockDim.x) {
         double v = 0.0;
@@ -616,7 +637,7 @@ cudaError_t launch_attn(const StepArgs& S, uint32_t layer, uint32_t ntok, float*
         if (e == cudaSuccess && (only < 0 || only == 1))
             e = launch(k_attn_stats, dim3(S.heads, ntok), dim3(kThreads), 0, st, pdl, S);
         if (e == cudaSuccess && (only < 0 || only == 2))
-            e = launch(k_attn_apply_split, dim3(S.kv_heads, S.score_stride / kAttnSplit, ntok), dim3(128), 0, st,
+            e = launch(k_attn_apply_split, dim3(S.kv_heads, (S.score_stride + kApplySplit - 1) / kApplySplit, ntok), dim3(128), 0, st,
                        pdl, S, layer);
         if (e == cudaSuccess && (only < 0 || only == 3)) e = launch(k_attn_combine, dim3(ntok), dim3(kThreads), 0, st, pdl, S, out);
         return e;
@@ -631,7 +652,7 @@ cudaError_t launch_attn(const StepArgs& S, uint32_t layer, uint32_t ntok, float*
 
 bool attn_split_path(const StepArgs& S, uint32_t ntok) {
     return S.attn_part && ntok >= 8 && S.score_stride % kAttnSplit == 0 && S.heads / S.kv_heads <= kMaxGroupSplit &&
-           S.head_dim <= 64 && S.head_dim % 8 == 0;
+           (S.head_dim == 32 || S.head_dim == 64);
 }
 
 template <int MT>

@@ -6,7 +6,9 @@
 namespace enx {
 
 constexpr uint32_t kAttnChunk = 64;  // positions per attention-score split
-constexpr uint32_t kAttnSplit = 128; // positions per weighted-V split (many-token attention)
+constexpr uint32_t kAttnSplit = 128; // positions per scores split (many-token attention)
+constexpr uint32_t kApplySplit = 512; // positions per weighted-V split: attn_part holds at most
+                                      // score_stride / kAttnSplit splits, more than it needs
 
 // Buffers and geometry of one decode step (shared by every layer of the step).
 struct StepArgs {
