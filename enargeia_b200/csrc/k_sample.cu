@@ -33,12 +33,13 @@ namespace enx {
 constexpr int kCluster = 8;
 constexpr int kSThreads = 1024;
 constexpr int kSWarps = kSThreads / 32;
-constexpr uint32_t kMaxPer = 26624;  // ids per CTA kept on chip: 8 bytes each
+constexpr uint32_t kMaxPer = 25344;  // ids per CTA kept on chip: 8 bytes each (+ 26 KB static, within 227 KB)
 
 uint32_t sample_max_vocab() { return kMaxPer * kCluster; }
 
 struct SampleSmem {
-    fx62_t bucket[256];     // fixed-point bucket masses of this CTA
+    fx62_t bucket[kToppSubs * 256];  // fixed-point bucket masses of this CTA (sub-histograms)
+    fx62_t ctab[256];                // their totals, read by the cluster
     fx62_t suffix[256];     // cluster suffix masses mass(p >= thr[j])
     fx62_t wsum[8];
     ToppTree tree;          // midpoints of the current 8 bisection steps
@@ -235,15 +236,17 @@ __global__ void __cluster_dims__(kCluster, 1, 1) __launch_bounds__(kSThreads, 1)
         const int lane = threadIdx.x & 31;
         for (int round = 0; round < 4; ++round) {
             if (threadIdx.x < 32) topp_build_tree_warp(sm.tree, lo, hi);
-            for (int b = threadIdx.x; b < 256; b += kSThreads) sm.bucket[b] = 0;
+            for (int b = threadIdx.x; b < kToppSubs * 256; b += kSThreads) sm.bucket[b] = 0;
             __syncthreads();
             topp_bucket_range(sm.tree, pbuf, tbeg - cbeg, tend - cbeg, sm.bucket);
+            __syncthreads();
+            if (threadIdx.x < 256) sm.ctab[threadIdx.x] = topp_sub_total(sm.bucket, threadIdx.x);
             cluster.sync();
             // cluster bucket totals (a thread per bucket), then suffix masses: within each warp of
             // 32 buckets, then the warps above added on (integers: exact in any order)
             if (threadIdx.x < 256) {
                 fx62_t t = 0;
-                for (int r = 0; r < kCluster; ++r) t += cluster.map_shared_rank(&sm, r)->bucket[threadIdx.x];
+                for (int r = 0; r < kCluster; ++r) t += cluster.map_shared_rank(&sm, r)->ctab[threadIdx.x];
                 const fx62_t v = topp_warp_suffix(t);
                 sm.suffix[threadIdx.x] = v;
                 if (lane == 0) sm.wsum[threadIdx.x >> 5] = v;
@@ -261,7 +264,7 @@ __global__ void __cluster_dims__(kCluster, 1, 1) __launch_bounds__(kSThreads, 1)
                 sm.lo = l;
                 sm.hi = h;
             }
-            cluster.sync();  // all CTAs done reading bucket[] before the next round clears it
+            cluster.sync();  // all CTAs done reading ctab[] before the next round rewrites it
             lo = sm.lo;
             hi = sm.hi;
         }

@@ -263,7 +263,7 @@ __global__ void __launch_bounds__(kShThreads) k_shard_buckets(uint32_t n, uint32
     const SampleRow P = rows[row];
     fx62_t* out = bucket + ((size_t)row * split + blockIdx.x) * 256;
     __shared__ Walk w;
-    __shared__ fx62_t bk[256];
+    __shared__ fx62_t bk[kToppSubs * 256];
     __shared__ double s_sum;
     const Span S = my_span(n, split);
     double* p = pbuf + (size_t)row * n;
@@ -293,11 +293,11 @@ __global__ void __launch_bounds__(kShThreads) k_shard_buckets(uint32_t n, uint32
         }
     }
     if (threadIdx.x < 32) topp_build_tree_warp(w.t, lo, hi);
-    for (int b = threadIdx.x; b < 256; b += kShThreads) bk[b] = 0;
+    for (int b = threadIdx.x; b < kToppSubs * 256; b += kShThreads) bk[b] = 0;
     __syncthreads();
     topp_bucket_range(w.t, p, S.tbeg, S.tend, bk);
     __syncthreads();
-    for (int b = threadIdx.x; b < 256; b += kShThreads) out[b] = bk[b];
+    for (int b = threadIdx.x; b < 256; b += kShThreads) out[b] = topp_sub_total(bk, b);
 }
 
 __global__ void __launch_bounds__(kShThreads) k_shard_kept(uint32_t n, uint32_t split, uint32_t world,

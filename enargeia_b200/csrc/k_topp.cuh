@@ -54,11 +54,17 @@ __device__ inline void topp_build_tree_warp(ToppTree& t, float lo, float hi) {
     }
 }
 
-// Adds the fixed-point masses of p[i], i in [beg, end), to bk[bucket] (shared, 256 entries).
-// Whole warps: masses below the first threshold and from the last one up are summed per warp
-// and added once.
+// Sub-histograms a CTA spreads its bucket atomics over (warp % kToppSubs): with flat
+// distributions most elements of a round fall into a few buckets, and one shared copy
+// serialises them.
+constexpr int kToppSubs = 8;
+
+// Adds the fixed-point masses of p[i], i in [beg, end), to bk[bucket] of this warp's
+// sub-histogram (shared, kToppSubs x 256 entries; sum them with topp_sub_total).  Whole warps:
+// masses below the first threshold and from the last one up are summed per warp and added once.
 __device__ __forceinline__ void topp_bucket_range(const ToppTree& t, const double* p, uint32_t beg, uint32_t end,
-                                                  fx62_t* bk) {
+                                                  fx62_t* bk_subs) {
+    fx62_t* bk = bk_subs + ((threadIdx.x >> 5) % kToppSubs) * 256;
     const double tlo = t.thr[1], thi = t.thr[255];
     fx62_t below = 0, above = 0;
     for (uint32_t i = beg; i < end; ++i) {
@@ -83,6 +89,14 @@ __device__ __forceinline__ void topp_bucket_range(const ToppTree& t, const doubl
         if (below) atomicAdd(&bk[0], below);
         if (above) atomicAdd(&bk[255], above);
     }
+}
+
+// Bucket b's total over the sub-histograms (integers: exact in any order).
+__device__ __forceinline__ fx62_t topp_sub_total(const fx62_t* bk_subs, int b) {
+    fx62_t s = 0;
+#pragma unroll
+    for (int k = 0; k < kToppSubs; ++k) s += bk_subs[k * 256 + b];
+    return s;
 }
 
 // Suffix sum within a warp of 32 consecutive buckets (lane l gets the sum of lanes l..31).
