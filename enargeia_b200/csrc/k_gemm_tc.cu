@@ -5,13 +5,14 @@
 // cannot multiply doubles, but they can sum integers exactly, so the activations go in as
 // integers: each token's row of x is scaled by a power of two 2^F (F from the row's largest
 // exponent) to 46-bit integers X = rint(x * 2^F) -- exact unless a value is 2^-22 below the row's
-// largest -- split into six balanced int8 limbs (two more zero limbs pad each token to 8 columns).  One kind::i8 MMA pair per block gives, per (row, token,
+// largest -- split into six balanced int8 limbs.  One kind::i8 MMA pair per block gives, per (row, token,
 // limb), the exact int32 sum over the block of a * limb, where a is the code q (int8, unsigned) or
 // q - z (int4, a signed byte).  The epilogue joins the limbs into the exact int64 sum of a * X,
 // takes off z * sum(X) for int8, and adds s times that to a double accumulator (one rounding per
 // block where the reference rounds per product); 2^-F is applied once at the end, exactly.
 //
-// Layout: a CTA owns 128 weight rows (M = 128 of the MMA), 32 tokens (N = 8 limbs x 32 = 256) and
+// Layout: a CTA owns 128 weight rows (M = 128 of the MMA), 32 tokens (N = 6 limbs x 32 = 192,
+// limb-major) and
 // a range of 64-element blocks (split-K when the row tiles x token groups do not fill the GPU;
 // the splits' double partials are then summed in split order by a second kernel).  Token groups
 // of a row tile are adjacent in the grid, so they read the tile's codes from L2.
@@ -25,7 +26,7 @@
 //               shared-memory tile (int4: nibbles to bytes minus the zero
 //               code, even elements then odd ones -- the limb tile uses the same order); one
 //               thread also streams the block's limb tile in with a bulk copy.
-// Four stages of (codes, limbs), two accumulators of 256 TMEM columns.  Every wait is bounded; on
+// Eight stages of (codes, limbs), two accumulators 256 TMEM columns apart.  Every wait is bounded; on
 // timeout the kernel records an error, every role stops, and the tensor memory is freed.
 
 #include <cuda.h>
@@ -39,8 +40,10 @@ namespace enx {
 namespace {
 
 constexpr uint32_t kTcRows = 128;     // weight rows per CTA (MMA M)
-constexpr uint32_t kTcTokens = 32;    // tokens per CTA (MMA N = 8 * 32)
-constexpr uint32_t kTcN = 8 * kTcTokens;
+constexpr uint32_t kTcTokens = 32;    // tokens per CTA
+constexpr uint32_t kTcLimbs = 6;       // balanced int8 limbs of a 46-bit X
+constexpr uint32_t kTcN = kTcLimbs * kTcTokens;  // MMA N = 192, limb-major: column 32 l + t
+constexpr uint32_t kTcAccCols = 256;   // columns between the two accumulators
 constexpr uint32_t kTcTmemCols = 512;  // two accumulators of 256 columns
 constexpr uint32_t kTcSpin = 1u << 24;
 
@@ -59,7 +62,7 @@ __device__ __forceinline__ uint64_t mdesc(uint32_t addr) {
     return (uint64_t)((addr >> 4) & 0x3FFF) | ((uint64_t)(128 >> 4) << 16) | ((uint64_t)(512 >> 4) << 32) | (1ull << 46);
 }
 
-// Instruction descriptor: s32 accumulate, B s8 (limbs), both K-major, N = 256, M = 128; A is u8
+// Instruction descriptor: s32 accumulate, B s8 (limbs), both K-major, N = 192, M = 128; A is u8
 // (int8 codes q) or s8 (int4: q - z, which fits a signed byte).
 template <int BITS>
 __host__ __device__ constexpr uint32_t idesc() {
@@ -125,15 +128,16 @@ __global__ void __launch_bounds__(256) k_limbs(const float* __restrict__ x, uint
         const unsigned long long u0 = (unsigned long long)(X0 + 0x808080808080LL);
         const unsigned long long u1 = (unsigned long long)(X1 + 0x808080808080LL);
 #pragma unroll
-        for (uint32_t l = 0; l < 8; ++l) {
-            const uint32_t d0 = l < 6 ? (uint32_t)((u0 >> (8 * l)) & 0xFF) - 128u : 0u;
-            const uint32_t d1 = l < 6 ? (uint32_t)((u1 >> (8 * l)) & 0xFF) - 128u : 0u;
+        for (uint32_t l = 0; l < kTcLimbs; ++l) {
+            const uint32_t d0 = (uint32_t)((u0 >> (8 * l)) & 0xFF) - 128u;
+            const uint32_t d1 = (uint32_t)((u1 >> (8 * l)) & 0xFF) - 128u;
             *reinterpret_cast<uint16_t*>(st + l * 64 + 2 * lane) = (uint16_t)((d0 & 0xFFu) | ((d1 & 0xFFu) << 8));
         }
         __syncwarp();
-        {
-            const uint32_t l = lane >> 2, c = lane & 3;  // lane stores chunk c of limb row l
-            *reinterpret_cast<uint4*>(tile + canon(t * 8 + l, c * 16)) = *reinterpret_cast<const uint4*>(st + l * 64 + c * 16);
+        if (lane < 4 * kTcLimbs) {
+            const uint32_t l = lane >> 2, c = lane & 3;  // lane stores chunk c of limb l's row
+            *reinterpret_cast<uint4*>(tile + canon(l * kTcTokens + t, c * 16)) =
+                *reinterpret_cast<const uint4*>(st + l * 64 + c * 16);
         }
         if (lane == 0) {
             long long* rec = reinterpret_cast<long long*>(tile + kTcN * 64);
@@ -286,7 +290,7 @@ __global__ void __launch_bounds__(kTcWsThreads, 1)
                 if (!mbar_wait_f(&full[s], (i / kTcStages) & 1, &s_fail, err)) break;
                 if (i >= 2 && !mbar_wait_f(&acce[a], ((i >> 1) - 1) & 1, &s_fail, err)) break;
                 asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
-                const uint32_t dcol = tmem + a * kTcN;
+                const uint32_t dcol = tmem + a * kTcAccCols;
 #pragma unroll
                 for (uint32_t kk = 0; kk < 2; ++kk) {  // K = 32 per MMA: two chunk planes of A
                     const uint64_t ad = mdesc_a(su32(sA + s * kTcATile) + kk * 4096);
@@ -329,48 +333,32 @@ __global__ void __launch_bounds__(kTcWsThreads, 1)
             // per token of this block (int8 only): the X sum, from the limb tile in global memory
             const int* tok = reinterpret_cast<const int*>(ltile + (size_t)b * kTcLimbTileBytes + kTcN * 64) +
                              (wg * kTcEpiTok) * 4;
-            // tokens in groups of kTok (8 for int4, 4 for int8: register pressure), one TMEM wait each
-            constexpr int kTok = 4, kLd = 1, kGroups = kTcEpiTok / kTok;
+            // limb l of the warpgroup's 8 tokens: 8 accumulator columns 32 l + 8 wg .. + 7, one load each
+            uint32_t d[kTcLimbs][8];
 #pragma unroll
-            for (int hh = 0; hh < kGroups; ++hh) {
-                uint32_t d[kLd][32];
+            for (uint32_t l = 0; l < kTcLimbs; ++l) {
+                const uint32_t ta = tmem + ((uint32_t)(32 * (warp & 3)) << 16) + a * kTcAccCols + l * kTcTokens + wg * kTcEpiTok;
+                asm volatile("tcgen05.ld.sync.aligned.32x32b.x8.b32 {%0,%1,%2,%3,%4,%5,%6,%7}, [%8];"
+                             : "=r"(d[l][0]), "=r"(d[l][1]), "=r"(d[l][2]), "=r"(d[l][3]), "=r"(d[l][4]), "=r"(d[l][5]),
+                               "=r"(d[l][6]), "=r"(d[l][7])
+                             : "r"(ta));
+            }
+            asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+            asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
+            __syncwarp();
+            if (lane == 0) mbar_arrive(&acce[a]);  // in registers: accumulator a may take block i + 2
 #pragma unroll
-                for (int tq = 0; tq < kLd; ++tq) {  // four tokens (32 accumulator columns) per TMEM load
-                    const uint32_t ta =
-                        tmem + ((uint32_t)(32 * (warp & 3)) << 16) + a * kTcN + (wg * kTcEpiTok + hh * kTok + tq * 4) * 8;
-                    asm volatile(
-                        "tcgen05.ld.sync.aligned.32x32b.x32.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,"
-                        "%16,%17,%18,%19,%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31}, [%32];"
-                        : "=r"(d[tq][0]), "=r"(d[tq][1]), "=r"(d[tq][2]), "=r"(d[tq][3]), "=r"(d[tq][4]),
-                          "=r"(d[tq][5]), "=r"(d[tq][6]), "=r"(d[tq][7]), "=r"(d[tq][8]), "=r"(d[tq][9]),
-                          "=r"(d[tq][10]), "=r"(d[tq][11]), "=r"(d[tq][12]), "=r"(d[tq][13]), "=r"(d[tq][14]),
-                          "=r"(d[tq][15]), "=r"(d[tq][16]), "=r"(d[tq][17]), "=r"(d[tq][18]), "=r"(d[tq][19]),
-                          "=r"(d[tq][20]), "=r"(d[tq][21]), "=r"(d[tq][22]), "=r"(d[tq][23]), "=r"(d[tq][24]),
-                          "=r"(d[tq][25]), "=r"(d[tq][26]), "=r"(d[tq][27]), "=r"(d[tq][28]), "=r"(d[tq][29]),
-                          "=r"(d[tq][30]), "=r"(d[tq][31])
-                        : "r"(ta));
+            for (int tt = 0; tt < kTcEpiTok; ++tt) {
+                // exact: each pair d_l + 256 d_(l+1) fits 32 bits
+                const long long a0 = (long long)((int)d[0][tt] + (int)d[1][tt] * 256);
+                const long long a1 = (long long)((int)d[2][tt] + (int)d[3][tt] * 256);
+                const long long a2 = (long long)((int)d[4][tt] + (int)d[5][tt] * 256);
+                long long T = a0 + a1 * 65536LL + a2 * 4294967296LL;
+                if (BITS == 8) {
+                    const int2 xs = __ldg(reinterpret_cast<const int2*>(tok + 4 * tt));
+                    T -= zc * (((long long)xs.y << 32) | (unsigned)xs.x);
                 }
-                asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
-                if (hh == kGroups - 1) {  // all the warp's tokens are in registers: accumulator a may take block i + 2
-                    asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
-                    __syncwarp();
-                    if (lane == 0) mbar_arrive(&acce[a]);
-                }
-#pragma unroll
-                for (int j = 0; j < kTok; ++j) {
-                    const int tt = hh * kTok + j;
-                    const int* dl = reinterpret_cast<const int*>(&d[j >> 2][8 * (j & 3)]);
-                    // exact: each pair d_l + 256 d_(l+1) fits 32 bits
-                    const long long a0 = (long long)(dl[0] + dl[1] * 256);
-                    const long long a1 = (long long)(dl[2] + dl[3] * 256);
-                    const long long a2 = (long long)(dl[4] + dl[5] * 256);
-                    long long T = a0 + a1 * 65536LL + a2 * 4294967296LL;
-                    if (BITS == 8) {
-                        const int2 xs = __ldg(reinterpret_cast<const int2*>(tok + 4 * tt));
-                        T -= zc * (((long long)xs.y << 32) | (unsigned)xs.x);
-                    }
-                    acc[tt] = fma((double)T, sc, acc[tt]);
-                }
+                acc[tt] = fma((double)T, sc, acc[tt]);
             }
         }
         if (!s_fail && rok && nblk) {

@@ -5,9 +5,10 @@
 
 namespace enx {
 
-// Bytes of one (32-token group, 64-element block) limb tile: 256 rows x 64 int8 limbs, then per
-// token the block sum of the scaled activations (int64) and its scale 2^-F (double).
-constexpr uint32_t kTcLimbTileBytes = 256 * 64 + 32 * 16;
+// Bytes of one (32-token group, 64-element block) limb tile: 192 rows (limb l of token t in row
+// 32 l + t) x 64 int8 values, then per token the block sum of the scaled activations (int64) and
+// its scale 2^-F (double).
+constexpr uint32_t kTcLimbTileBytes = 192 * 64 + 32 * 16;
 
 // Workspace for launch_gemm_tc: the limb tiles of m tokens over k and the split-K partials.
 size_t gemm_tc_workspace_bytes(uint32_t m, uint32_t k);
