@@ -177,23 +177,20 @@ __device__ __forceinline__ void mbar_arrive(uint64_t* bar) {
 }
 
 // Code tiles arrive by TMA from a byte matrix [rows][K] (int8 codes as stored; int4 as the signed
-// bytes q - z prepared by k_codes_i8): per block four 2D boxes of 16 bytes x 128 rows, one per
-// 16-byte chunk of the block, land as four chunk planes.  Each 8-row x 16-byte core matrix is then
-// contiguous, K-adjacent core matrices are 2048 bytes apart and row-adjacent ones 128 bytes apart,
-// which is the K-major, unswizzled layout the MMA descriptor below describes.
+// bytes q - z prepared by k_codes_i8): one 2D box of 64 bytes x 128 rows per block, written with
+// the 64-byte swizzle, which is the K-major SWIZZLE_64B layout the MMA reads directly (rows of
+// 64 bytes, 8-row groups 512 bytes apart; the second K = 32 half starts 32 bytes in).
 __device__ __forceinline__ uint64_t mdesc_a(uint32_t addr) {
-    return (uint64_t)((addr >> 4) & 0x3FFF) | ((uint64_t)(2048 >> 4) << 16) | ((uint64_t)(128 >> 4) << 32) | (1ull << 46);
+    return (uint64_t)((addr >> 4) & 0x3FFF) | (1ull << 16) | ((uint64_t)(512 >> 4) << 32) | (1ull << 46) | (4ull << 61);
 }
 
 __device__ __forceinline__ void tma_codes(uint8_t* dst, const CUtensorMap* map, uint32_t block, uint32_t row,
                                           uint64_t* bar) {
-#pragma unroll
-    for (uint32_t c = 0; c < 4; ++c)  // x = 64 * block + 16 * c bytes: 16-byte aligned
-        asm volatile(
-            "cp.async.bulk.tensor.2d.shared::cluster.global.tile.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3}], [%4];" ::"r"(
-                su32(dst + c * 2048)),
-            "l"(map), "r"(block * 64 + c * 16), "r"(row), "r"(su32(bar))
-            : "memory");
+    asm volatile(
+        "cp.async.bulk.tensor.2d.shared::cluster.global.tile.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3}], [%4];" ::"r"(
+            su32(dst)),
+        "l"(map), "r"(block * 64), "r"(row), "r"(su32(bar))  // x = 64 * block bytes: 16-byte aligned
+        : "memory");
 }
 
 // int4 codes to the byte matrix the GEMM reads: per row and 64-element block, the signed bytes
@@ -292,8 +289,8 @@ __global__ void __launch_bounds__(kTcWsThreads, 1)
                 asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
                 const uint32_t dcol = tmem + a * kTcAccCols;
 #pragma unroll
-                for (uint32_t kk = 0; kk < 2; ++kk) {  // K = 32 per MMA: two chunk planes of A
-                    const uint64_t ad = mdesc_a(su32(sA + s * kTcATile) + kk * 4096);
+                for (uint32_t kk = 0; kk < 2; ++kk) {  // K = 32 per MMA: the two halves of A's 64-byte rows
+                    const uint64_t ad = mdesc_a(su32(sA + s * kTcATile) + kk * 32);
                     const uint64_t bd = mdesc(su32(sB + s * kTcLimbTileBytes) + kk * 256);
                     asm volatile("{\n .reg .pred p;\n setp.ne.b32 p, %4, 0;\n tcgen05.mma.cta_group::1.kind::i8 [%0], %1, %2, %3, p;\n}\n" ::"r"(
                                      dcol),
@@ -482,17 +479,17 @@ cudaError_t launch_gemm_tc(int bits, const float* x, uint32_t ld, const QW& w, c
                                                                                           workspace);
     e = cudaGetLastError();
     if (e != cudaSuccess) return e;
-    // the code bytes as a 2D tensor (K bytes x rows); a box is one 16-byte chunk of 128 rows
+    // the code bytes as a 2D tensor (K bytes x rows); a box is one 64-element block of 128 rows
     CUtensorMap cmap;
     {
         const cuuint64_t dims[2] = {w.cols, w.rows};
         const cuuint64_t strides[1] = {w.cols};
-        const cuuint32_t box[2] = {16, kTcRows};
+        const cuuint32_t box[2] = {64, kTcRows};
         const cuuint32_t estr[2] = {1, 1};
         const EncodeTiledFn encode = encode_tiled();
         if (!encode) return cudaErrorNotSupported;
         const CUresult r = encode(&cmap, CU_TENSOR_MAP_DATA_TYPE_UINT8, 2, (void*)codes8, dims, strides, box, estr,
-                                  CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE,
+                                  CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_64B,
                                   CU_TENSOR_MAP_L2_PROMOTION_L2_128B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
         if (r != CUDA_SUCCESS) return cudaErrorInvalidValue;
     }
