@@ -903,11 +903,11 @@ static const uint8_t* codes_of(const enx_ctx* c, const QW& w) {
 
 // A projection of m prefill rows: tensor cores for m >= kTcMinTokens, CUDA cores below.
 static cudaError_t proj(enx_ctx* c, int bits, const float* x, const QW& w, const float* bias, float* out, uint32_t m,
-                        uint32_t stride, uint32_t offset, cudaStream_t st) {
+                        uint32_t stride, uint32_t offset, cudaStream_t st, bool same_x = false) {
     if (m >= kTcMinTokens && c->pf_ws && bits == 4 && !codes_of(c, w)) return cudaErrorInvalidValue;  // never prepared
     if (m >= kTcMinTokens && c->pf_ws)
         return launch_gemm_tc(bits, x, w.cols, w, bits == 4 ? codes_of(c, w) : nullptr, bias, out, m, stride, offset,
-                              c->pf_ws, &c->d_step->err, st);
+                              c->pf_ws, &c->d_step->err, st, same_x);
     return launch_matmul(bits, x, w, bias, out, m, stride, offset, st, false);
 }
 
@@ -974,8 +974,8 @@ extern "C" enx_status enx_prefill(enx_ctx* c, uint32_t seq, const uint32_t* ids,
             const LayerArgs& L = c->layers[l];
             ENX_CUDA(launch_rmsnorm(c->pf_x, L.norm_in, c->pf_n, m, H, C.rms_norm_eps, st));
             ENX_CUDA(proj(c, 4, c->pf_n, L.wq, L.bq, c->pf_q, m, H, 0, st));
-            ENX_CUDA(proj(c, 4, c->pf_n, L.wk, L.bk, c->pf_k, m, kv, 0, st));
-            ENX_CUDA(proj(c, 4, c->pf_n, L.wv, L.bv, c->pf_v, m, kv, 0, st));
+            ENX_CUDA(proj(c, 4, c->pf_n, L.wk, L.bk, c->pf_k, m, kv, 0, st, true));  // limbs of pf_n reused
+            ENX_CUDA(proj(c, 4, c->pf_n, L.wv, L.bv, c->pf_v, m, kv, 0, st, true));
             ENX_CUDA(launch_rope_d(c->pf_q, c->pf_q2, c->rope_cos, c->rope_sin, m, C.heads, C.head_dim, begin, 0, st));
             ENX_CUDA(launch_rope_d(c->pf_k, c->pf_k2, c->rope_cos, c->rope_sin, m, C.kv_heads, C.head_dim, begin, 0, st));
             ENX_CUDA(launch_cache_pack(c->pf_k2, c->kcache + S.cache_offset(seq, l, begin), m * kv, 0, st));
@@ -985,7 +985,7 @@ extern "C" enx_status enx_prefill(enx_ctx* c, uint32_t seq, const uint32_t* ids,
             ENX_CUDA(launch_add(c->pf_x, c->pf_t, c->pf_x, m * H, st));
             ENX_CUDA(launch_rmsnorm(c->pf_x, L.norm_post, c->pf_n, m, H, C.rms_norm_eps, st));
             ENX_CUDA(proj(c, 4, c->pf_n, L.wg, nullptr, c->pf_g, m, I, 0, st));
-            ENX_CUDA(proj(c, 4, c->pf_n, L.wu, nullptr, c->pf_u, m, I, 0, st));
+            ENX_CUDA(proj(c, 4, c->pf_n, L.wu, nullptr, c->pf_u, m, I, 0, st, true));
             ENX_CUDA(launch_silu_mul(c->pf_g, c->pf_u, c->pf_g, m * I, st));
             ENX_CUDA(proj(c, 4, c->pf_g, L.wd, nullptr, c->pf_t, m, H, 0, st));
             ENX_CUDA(launch_add(c->pf_x, c->pf_t, c->pf_x, m * H, st));
@@ -1088,11 +1088,11 @@ static bool mega_eligible(enx_ctx* c, uint32_t B, const StepArgs& S, MegaArgs& A
 
 // A projection of B batched tokens: tensor cores from kTcMinTokens tokens, CUDA cores below.
 static cudaError_t proj_b(enx_ctx* c, int bits, const float* x, const QW& w, const float* bias, float* out, uint32_t B,
-                          uint32_t stride, cudaStream_t st) {
+                          uint32_t stride, cudaStream_t st, bool same_x = false) {
     if (B >= kTcMinTokens && bits == 4 && !codes_of(c, w)) return cudaErrorInvalidValue;  // never prepared
     if (B >= kTcMinTokens)
         return launch_gemm_tc(bits, x, w.cols, w, bits == 4 ? codes_of(c, w) : nullptr, bias, out, B, stride, 0, c->b_ws,
-                              c->d_bb + c->bl.err(), st);
+                              c->d_bb + c->bl.err(), st, same_x);
     return launch_matmul(bits, x, w, bias, out, B, stride, 0, st, false);
 }
 
@@ -1115,15 +1115,15 @@ static cudaError_t batch_body(enx_ctx* c, uint32_t B, cudaStream_t st) {
         const LayerArgs& L = c->layers[l];
         e = launch_rmsnorm(c->b_x, L.norm_in, c->b_xn, B, H, C.rms_norm_eps, st);
         if (e == cudaSuccess) e = proj_b(c, 4, c->b_xn, L.wq, L.bq, c->b_q, B, H, st);
-        if (e == cudaSuccess) e = proj_b(c, 4, c->b_xn, L.wk, L.bk, c->b_k, B, kvd, st);
-        if (e == cudaSuccess) e = proj_b(c, 4, c->b_xn, L.wv, L.bv, c->b_v, B, kvd, st);
+        if (e == cudaSuccess) e = proj_b(c, 4, c->b_xn, L.wk, L.bk, c->b_k, B, kvd, st, true);  // limbs of b_xn reused
+        if (e == cudaSuccess) e = proj_b(c, 4, c->b_xn, L.wv, L.bv, c->b_v, B, kvd, st, true);
         if (e == cudaSuccess) e = launch_rope_cache_batch(S, l, c->b_q, c->b_k, c->b_v, B, st);
         if (e == cudaSuccess) e = launch_attn(S, l, B, c->b_att, st, false);
         if (e == cudaSuccess) e = proj_b(c, 4, c->b_att, L.wo, nullptr, c->b_t, B, H, st);
         if (e == cudaSuccess) e = launch_add(c->b_x, c->b_t, c->b_x, B * H, st);
         if (e == cudaSuccess) e = launch_rmsnorm(c->b_x, L.norm_post, c->b_xn, B, H, C.rms_norm_eps, st);
         if (e == cudaSuccess) e = proj_b(c, 4, c->b_xn, L.wg, nullptr, c->b_g, B, I, st);
-        if (e == cudaSuccess) e = proj_b(c, 4, c->b_xn, L.wu, nullptr, c->b_u, B, I, st);
+        if (e == cudaSuccess) e = proj_b(c, 4, c->b_xn, L.wu, nullptr, c->b_u, B, I, st, true);
         if (e == cudaSuccess) e = launch_silu_mul(c->b_g, c->b_u, c->b_g, B * I, st);
         if (e == cudaSuccess) e = proj_b(c, 4, c->b_g, L.wd, nullptr, c->b_t, B, H, st);
         if (e == cudaSuccess) e = launch_add(c->b_x, c->b_t, c->b_x, B * H, st);
@@ -1171,8 +1171,8 @@ static enx_status batch_profile(enx_ctx* c, uint32_t B, float* ms, uint32_t coun
         e = section(1, [&] { return launch_rmsnorm(c->b_x, L.norm_in, c->b_xn, B, H, C.rms_norm_eps, st); });
         if (e == cudaSuccess) e = section(2, [&] {
             cudaError_t r = proj_b(c, 4, c->b_xn, L.wq, L.bq, c->b_q, B, H, st);
-            if (r == cudaSuccess) r = proj_b(c, 4, c->b_xn, L.wk, L.bk, c->b_k, B, kvd, st);
-            return r == cudaSuccess ? proj_b(c, 4, c->b_xn, L.wv, L.bv, c->b_v, B, kvd, st) : r;
+            if (r == cudaSuccess) r = proj_b(c, 4, c->b_xn, L.wk, L.bk, c->b_k, B, kvd, st, true);
+            return r == cudaSuccess ? proj_b(c, 4, c->b_xn, L.wv, L.bv, c->b_v, B, kvd, st, true) : r;
         });
         if (e == cudaSuccess) e = section(3, [&] { return launch_rope_cache_batch(S, l, c->b_q, c->b_k, c->b_v, B, st); });
         if (e == cudaSuccess) {
@@ -1191,7 +1191,7 @@ static enx_status batch_profile(enx_ctx* c, uint32_t B, float* ms, uint32_t coun
         if (e == cudaSuccess) e = section(1, [&] { return launch_rmsnorm(c->b_x, L.norm_post, c->b_xn, B, H, C.rms_norm_eps, st); });
         if (e == cudaSuccess) e = section(6, [&] {
             cudaError_t r = proj_b(c, 4, c->b_xn, L.wg, nullptr, c->b_g, B, I, st);
-            if (r == cudaSuccess) r = proj_b(c, 4, c->b_xn, L.wu, nullptr, c->b_u, B, I, st);
+            if (r == cudaSuccess) r = proj_b(c, 4, c->b_xn, L.wu, nullptr, c->b_u, B, I, st, true);
             return r == cudaSuccess ? launch_silu_mul(c->b_g, c->b_u, c->b_g, B * I, st) : r;
         });
         if (e == cudaSuccess) e = section(7, [&] {

@@ -464,7 +464,7 @@ static EncodeTiledFn encode_tiled() {
 
 cudaError_t launch_gemm_tc(int bits, const float* x, uint32_t ld, const QW& w, const uint8_t* codes8, const float* bias,
                            float* out, uint32_t m, uint32_t out_stride, uint32_t out_offset, uint8_t* workspace,
-                           uint32_t* err, cudaStream_t st) {
+                           uint32_t* err, cudaStream_t st, bool limbs_ready) {
     const uint32_t groups = (m + kTcTokens - 1) / kTcTokens, nb = w.cols / kBlock;
     cudaError_t e;
     if (bits == 8) {
@@ -475,10 +475,12 @@ cudaError_t launch_gemm_tc(int bits, const float* x, uint32_t ld, const QW& w, c
         if (e != cudaSuccess) return e;
         codes8 = conv;
     }
-    k_limbs<<<dim3(groups * (kTcTokens / 8), (nb + kLimbChunk - 1) / kLimbChunk), 256, 0, st>>>(x, ld, m, w.cols, bits,
-                                                                                          workspace);
-    e = cudaGetLastError();
-    if (e != cudaSuccess) return e;
+    if (!limbs_ready) {  // else: the workspace holds the limbs of this x from the previous call
+        k_limbs<<<dim3(groups * (kTcTokens / 8), (nb + kLimbChunk - 1) / kLimbChunk), 256, 0, st>>>(x, ld, m, w.cols,
+                                                                                              bits, workspace);
+        e = cudaGetLastError();
+        if (e != cudaSuccess) return e;
+    }
     // the code bytes as a 2D tensor (K bytes x rows); a box is one 64-element block of 128 rows
     CUtensorMap cmap;
     {

@@ -23,9 +23,10 @@ cudaError_t launch_codes_i8(const QW& w, uint8_t* out, cudaStream_t st);
 // out[t * out_stride + out_offset + n] = float(x[t] . W[n] (+ bias[n])) for t < m, n < w.rows;
 // x rows ld floats apart.  bits 4 or 8; w.cols a multiple of 64.  codes8: the prepared int4 byte
 // matrix, or null to convert into the workspace (which then needs gemm_tc_codes_bytes more).
-// *err is raised to 3 if a bounded wait inside the kernel gives up.
+// *err is raised to 3 if a bounded wait inside the kernel gives up.  limbs_ready: the previous
+// call on this workspace had the same x, ld, m and w.cols, so its activation limbs are reused.
 cudaError_t launch_gemm_tc(int bits, const float* x, uint32_t ld, const QW& w, const uint8_t* codes8, const float* bias,
                            float* out, uint32_t m, uint32_t out_stride, uint32_t out_offset, uint8_t* workspace,
-                           uint32_t* err, cudaStream_t st);
+                           uint32_t* err, cudaStream_t st, bool limbs_ready = false);
 
 }  // namespace enx
