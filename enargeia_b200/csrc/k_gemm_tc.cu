@@ -5,29 +5,28 @@
 // cannot multiply doubles, but they can sum integers exactly, so the activations go in as
 // integers: each token's row of x is scaled by a power of two 2^F (F from the row's largest
 // exponent) to 46-bit integers X = rint(x * 2^F) -- exact unless a value is 2^-22 below the row's
-// largest -- split into six balanced int8 limbs.  One kind::i8 MMA pair per block gives, per (row, token,
-// limb), the exact int32 sum over the block of a * limb, where a is the code q (int8, unsigned) or
-// q - z (int4, a signed byte).  The epilogue joins the limbs into the exact int64 sum of a * X,
-// takes off z * sum(X) for int8, and adds s times that to a double accumulator (one rounding per
-// block where the reference rounds per product); 2^-F is applied once at the end, exactly.
+// largest -- split into six balanced int8 limbs (k_limbs).  The weights go in as a byte matrix:
+// int8 codes q as stored, int4 codes as q - z (a signed byte; k_codes_i8).  One kind::i8 MMA
+// pair per 64-element block gives, per (row, token, limb), the exact int32 sum over the block of
+// a * limb.  The epilogue joins the limbs into the exact int64 sum of a * X, takes off z * sum(X)
+// for int8, and adds s times that to a double accumulator (one rounding per block where the
+// reference rounds per product); 2^-F is applied once at the end, exactly.
 //
 // Layout: a CTA owns 128 weight rows (M = 128 of the MMA), 32 tokens (N = 6 limbs x 32 = 192,
-// limb-major) and
-// a range of 64-element blocks (split-K when the row tiles x token groups do not fill the GPU;
-// the splits' double partials are then summed in split order by a second kernel).  Token groups
-// of a row tile are adjacent in the grid, so they read the tile's codes from L2.
+// limb-major) and a range of 64-element blocks (split-K when the row tiles x token groups do not
+// fill the GPU; the splits' double partials are then summed in split order by a second kernel).
+// Token groups of a row tile are adjacent in the grid, so they read the tile's codes from L2.
 //
 // Warp roles, synchronised by mbarriers only:
 //   warps 0-15  epilogue: warpgroup wg drains tokens 8wg..8wg+7 of the accumulator the tensor
-//               cores are not writing (thread = row), then releases it;
+//               cores are not writing (thread = row, one 8-column TMEM load per limb), then
+//               releases it;
 //   warp 16     TMEM allocation; lane 0 issues the two MMAs of each block;
-//   warps 17-18 producer: a thread per two rows, fetches the rows' packed codes (and int4 zero
-//               words) four blocks ahead with cp.async, unpacks each block into a K-major
-//               shared-memory tile (int4: nibbles to bytes minus the zero
-//               code, even elements then odd ones -- the limb tile uses the same order); one
-//               thread also streams the block's limb tile in with a bulk copy.
-// Eight stages of (codes, limbs), two accumulators 256 TMEM columns apart.  Every wait is bounded; on
-// timeout the kernel records an error, every role stops, and the tensor memory is freed.
+//   warp 17     producer: lane 0 loads each block's codes (one 64-byte-swizzled TMA box of 128
+//               rows) and its limb tile (one bulk copy) into a stage.
+// Eight stages of (codes, limbs), two accumulators 256 TMEM columns apart.  Every wait is
+// bounded; on timeout the kernel records an error, every role stops, and the tensor memory is
+// freed.
 
 #include <cuda.h>
 
@@ -44,20 +43,20 @@ constexpr uint32_t kTcTokens = 32;    // tokens per CTA
 constexpr uint32_t kTcLimbs = 6;       // balanced int8 limbs of a 46-bit X
 constexpr uint32_t kTcN = kTcLimbs * kTcTokens;  // MMA N = 192, limb-major: column 32 l + t
 constexpr uint32_t kTcAccCols = 256;   // columns between the two accumulators
-constexpr uint32_t kTcTmemCols = 512;  // two accumulators of 256 columns
+constexpr uint32_t kTcTmemCols = 512;  // TMEM allocation: the two accumulators
 constexpr uint32_t kTcSpin = 1u << 24;
 
 __device__ __forceinline__ uint32_t su32(const void* p) { return static_cast<uint32_t>(__cvta_generic_to_shared(p)); }
 
-// Byte offset of (row, k-byte) in a K-major, unswizzled canonical tile of 64 k-bytes per row:
-// 8-row x 16-byte core matrices, the four k-chunks of a row group adjacent (128 B apart), row
-// groups 512 B apart.
+// Byte offset of (row, k-byte) in a K-major, unswizzled canonical tile of 64 k-bytes per row (the
+// limb tiles): 8-row x 16-byte core matrices, the four k-chunks of a row group adjacent (128 B
+// apart), row groups 512 B apart.
 __host__ __device__ __forceinline__ uint32_t canon(uint32_t r, uint32_t kb) {
     return (r >> 3) * 512 + (kb >> 4) * 128 + (r & 7) * 16 + (kb & 15);
 }
 
-// Shared-memory matrix descriptor: start, leading-byte offset 128, stride-byte offset 512,
-// version 1, no swizzle.
+// Shared-memory matrix descriptor of a limb tile: start, leading-byte offset 128, stride-byte
+// offset 512, version 1, no swizzle.
 __device__ __forceinline__ uint64_t mdesc(uint32_t addr) {
     return (uint64_t)((addr >> 4) & 0x3FFF) | ((uint64_t)(128 >> 4) << 16) | ((uint64_t)(512 >> 4) << 32) | (1ull << 46);
 }
