@@ -306,6 +306,28 @@ def run_enx(args, rank, world, local_rank):
 
 
 # ---------------------------------------------------------------------------------------------
+# launch counting
+
+
+def count_library_launches(fn) -> int:
+    """Kernels of libenx (all named enx::k_*) launched by fn(), counted from the CUDA activity
+    torch's profiler records; used for workloads whose API launches kernels eagerly."""
+    import torch
+    from torch.profiler import ProfilerActivity, profile
+
+    torch.cuda.synchronize()
+    with profile(activities=[ProfilerActivity.CUDA]) as prof:
+        fn()
+        torch.cuda.synchronize()
+    n = 0
+    for ev in prof.events():
+        name = ev.name or ""
+        if ev.device_type == torch.autograd.DeviceType.CUDA and ("enx::k_" in name or name.startswith("k_")):
+            n += 1
+    return n
+
+
+# ---------------------------------------------------------------------------------------------
 # config 3: chunked prefill (bench.py --workload config3)
 
 PREFILL_LEN, PREFILL_CHUNK = 2048, 256
@@ -354,6 +376,11 @@ def run_prefill(args, rank, world, local_rank):
     for _ in range(args.warmup):
         m.reset(0)
         m.prefill(0, prompt, PREFILL_CHUNK)
+    def one_prefill():
+        m.reset(0)
+        m.prefill(0, prompt, PREFILL_CHUNK)
+
+    launches_per_step = count_library_launches(one_prefill)  # an extra, untimed prefill
     with ClockSampler(local_rank) as clocks:
         barrier()
         dev_ms, wall = 0.0, 0.0
@@ -435,7 +462,8 @@ def run_prefill(args, rank, world, local_rank):
                      "useful_tflops": round(useful / (gemm_us / 1e6) / 1e12, 2), "launch_us": round(gemm_us, 2),
                      "peak_source": "2 x measured MEASURED_PEAKS.json bf16_tflops (dense int8 = 2x dense bf16)"},
         "step_tflops": round(step_flops / (dev_ms / steps / 1e3) / 1e12, 2),
-        "gpu_launches": None,
+        "gpu_launches": launches_per_step * steps,
+        "launches_per_step": launches_per_step,
         "clocks": clocks.summary(),
     }
     if rank == 0:
@@ -691,9 +719,11 @@ def run_sweep(args, rank, world, local_rank):
             io = m * k * 4 + m * n * 4
             gbs = (wbytes + io) / (us / 1e6) / 1e9
             tc = m >= 16
+            per_call = count_library_launches(lambda: launch(0))  # one enx_matmul_q4 call, counted
             c = {"shape": name, "n": n, "k": k, "m": m, "path": "tcgen05 limb GEMM" if tc else "CUDA-core matvec",
                  "us": round(us, 3), "hbm_gbs": round(gbs, 1), "hbm_frac": round(gbs / hbm, 4),
-                 "weight_bytes": wbytes, "e2e_us": round(e2e_us, 3), "launches": 2 if tc else 1}
+                 "weight_bytes": wbytes, "e2e_us": round(e2e_us, 3), "launches": per_call,
+                 "timed_launches": reps * per_call}
             if tc:
                 groups = -(-m // 32)
                 mma_ops = 2 * (-(-n // 128) * 128) * groups * 256 * k  # issued int8 MMA ops (8 limbs x 32 tokens)
@@ -738,7 +768,7 @@ def run_sweep(args, rank, world, local_rank):
                      "peak_source": f"{peak_src} MEASURED_PEAKS.json hbm_gbs (burst copy)"},
         "int8_peak_tops": i8_peak,
         "cases": cases,
-        "gpu_launches": sum(c["launches"] for c in base) * args.steps,
+        "gpu_launches": sum(c["timed_launches"] for c in cases),
     }
     if rank == 0:
         print(json.dumps(out), flush=True)
