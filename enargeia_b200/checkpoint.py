@@ -22,7 +22,7 @@ from typing import Dict, Iterator, List, Tuple
 
 import numpy as np
 
-from .format import EMBEDDING, EnargeiaFile, F32Tensor, QuantTensor, parse_enargeia, quantize_tensor, write_enargeia
+from .format import EMBEDDING, EnargeiaFile, quantize_tensor, write_enargeia
 
 
 @dataclass(frozen=True)

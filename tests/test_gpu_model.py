@@ -8,7 +8,7 @@ import pytest
 from conftest import GOLDEN
 from enargeia_b200.checkpoint import SMALL, TINY, build_model_file
 from enargeia_b200.format import read_enargeia
-from enargeia_b200.session import APP_SAMPLING, GREEDY, Model, SamplingParams, Session
+from enargeia_b200.session import APP_SAMPLING, GREEDY, Model, Session
 
 pytestmark = pytest.mark.gpu
 
