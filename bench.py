@@ -429,7 +429,7 @@ def run_prefill(args, rank, world, local_rank):
     bf16 = float(peaks.get("bf16_tflops", 1590.0))
     i8_peak = 2 * bf16
     groups = -(-PREFILL_CHUNK // 32)
-    mma_ops = 2 * (-(-g["rows"] // 128) * 128) * groups * 256 * g["cols"]
+    mma_ops = 2 * (-(-g["rows"] // 128) * 128) * groups * 192 * g["cols"]  # 6 limb columns x 32 tokens
     useful = 2 * PREFILL_CHUNK * g["rows"] * g["cols"]
     proj_macs = cfg.layers * (cfg.hidden * (cfg.hidden + 2 * cfg.kv_dim) + cfg.hidden * cfg.hidden
                               + 3 * cfg.hidden * cfg.intermediate)
@@ -726,7 +726,7 @@ def run_sweep(args, rank, world, local_rank):
                  "timed_launches": reps * per_call}
             if tc:
                 groups = -(-m // 32)
-                mma_ops = 2 * (-(-n // 128) * 128) * groups * 256 * k  # issued int8 MMA ops (8 limbs x 32 tokens)
+                mma_ops = 2 * (-(-n // 128) * 128) * groups * 192 * k  # issued int8 MMA ops (6 limbs x 32 tokens)
                 c["useful_tflops"] = round(2 * m * n * k / (us / 1e6) / 1e12, 2)
                 c["int8_mma_tops"] = round(mma_ops / (us / 1e6) / 1e12, 1)
                 c["tensor_frac_of_int8_peak"] = round(mma_ops / (us / 1e6) / 1e12 / i8_peak, 4)
