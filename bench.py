@@ -843,12 +843,27 @@ def run_head(args, rank, world, local_rank):
         logits = torch.empty((B, head.n), dtype=torch.float32, device=dev)
         out = torch.empty(B, dtype=torch.int32, device=dev)
         sampler = ShardedSampler(HEAD_VOCAB, rank, world, B, dev) if world > 1 else None
+        graph = None
+        if sampler is None:
+            # one GPU: the head and the fused sampler replayed as one CUDA graph over static input
+            # buffers (the sharded step's NCCL exchanges stay eager)
+            gx = torch.zeros((B, HEAD_HIDDEN), dtype=torch.float32, device=dev)
+            gp = params_dev[0].clone()
+            head.logits(gx, logits)
+            K.sample_batched(logits, history, hlen, gp, out)
+            torch.cuda.synchronize()
+            graph = torch.cuda.CUDAGraph()
+            with torch.cuda.graph(graph):
+                head.logits(gx, logits)
+                K.sample_batched(logits, history, hlen, gp, out)
 
         def step(i, x, prow_dev):
-            head.logits(x, logits)
-            if sampler is None:
-                K.sample_batched(logits, history, hlen, prow_dev, out)
+            if graph is not None:
+                gx.copy_(x, non_blocking=True)
+                gp.copy_(prow_dev, non_blocking=True)
+                graph.replay()
                 return out
+            head.logits(x, logits)
             return run_distributed(sampler, ShardInputs(logits, history, hlen, params[i]), params_dev=prow_dev)
 
         for i in range(warmup):
@@ -895,7 +910,7 @@ def run_head(args, rank, world, local_rank):
         return {"rows": B, "value": round(B / (ms / 1e3), 1), "ms_per_step": round(ms, 4),
                 "e2e": {"value": round(B / (e2e_ms / 1e3), 1), "unit": "rows/s",
                         "h2d_bytes_per_step": B * HEAD_HIDDEN * 4 + B * 16, "d2h_bytes_per_step": B * 4,
-                        "api": "ShardedHead.logits (enx_lm_head_q8) + enx_sample_batched / enx_shard_* phases"},
+                        "api": "enx_lm_head_q8 + enx_sample_batched (one CUDA graph) / enx_shard_* phases + NCCL"},
                 "head_roofline": {"kernel": "enx_lm_head_q8 over this rank's rows"
                                             + (" (tcgen05 limb GEMM)" if B >= 16 else " (CUDA-core matvec)"),
                                   "bound": "hbm", "achieved": round(achieved, 1), "peak": hbm, "unit": "GB/s",
