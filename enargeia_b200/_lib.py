@@ -97,6 +97,7 @@ SIGNATURES = {
     "enx_kv_alloc": (C.c_int32, [P, U32, U32]),
     "enx_kv_reset": (C.c_int32, [P, U32]),
     "enx_kv_filled": (C.c_int32, [P, U32, C.POINTER(U32)]),
+    "enx_raw_check": (C.c_int32, []),
     "enx_prefill": (C.c_int32, [P, U32, P, U32, U32]),
     "enx_sample_prefill": (C.c_int32, [P, U32, C.POINTER(SamplingC), F32, C.POINTER(U32)]),
     "enx_decode_step": (C.c_int32, [P, U32, P, C.POINTER(SamplingC), U32, P, P]),

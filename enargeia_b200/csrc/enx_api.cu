@@ -88,6 +88,24 @@ static enx_status tc_workspace(size_t bytes, uint8_t** ws, uint32_t** err) {
     return ENX_OK;
 }
 
+extern "C" enx_status enx_raw_check(void) {
+    int dev = 0;
+    ENX_CUDA(cudaGetDevice(&dev));
+    ENX_CUDA(cudaDeviceSynchronize());
+    uint32_t* err = nullptr;
+    {
+        std::lock_guard<std::mutex> lock(g_tc_mu);
+        if ((size_t)dev < g_tc_ws.size()) err = g_tc_ws[dev].err;
+    }
+    if (!err) return ENX_OK;
+    uint32_t code = 0;
+    ENX_CUDA(cudaMemcpy(&code, err, 4, cudaMemcpyDeviceToHost));
+    if (!code) return ENX_OK;
+    ENX_CUDA(cudaMemset(err, 0, 4));
+    return fail(ENX_ERR_TIMEOUT, "raw tensor-core GEMM: a bounded device wait gave up (code " +
+                                     std::to_string(code) + ")");
+}
+
 extern "C" enx_status enx_matmul_q4(const float* x, const uint32_t* packed, const float* scales,
                                     const uint32_t* zeros, const float* bias, float* out,
                                     const enx_matmul_q4_dims* d, void* stream) {
@@ -938,6 +956,8 @@ static enx_status ensure_prefill(enx_ctx* c, uint32_t chunk) {
     return ENX_OK;
 }
 
+static enx_status device_error(enx_ctx* c);
+
 extern "C" enx_status enx_prefill(enx_ctx* c, uint32_t seq, const uint32_t* ids, uint32_t n, uint32_t chunk) {
     CHECK_ARG(c && ids, "enx_prefill: null pointer");
     if (!c->loaded) return fail(ENX_ERR_STATE, "enx_prefill: no model loaded");
@@ -1000,7 +1020,7 @@ extern "C" enx_status enx_prefill(enx_ctx* c, uint32_t seq, const uint32_t* ids,
         }
     }
     ENX_CUDA(cudaStreamSynchronize(st));
-    return ENX_OK;
+    return device_error(c);  // the tensor-core GEMMs' bounded waits report through the step's error word
 }
 
 extern "C" enx_status enx_sample_prefill(enx_ctx* c, uint32_t seq, const enx_sampling* params, float random,

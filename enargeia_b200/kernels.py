@@ -46,6 +46,11 @@ def matmul_q4(x, packed, scales, zeros, bias, out, m, n, k, out_stride=None, out
     return out
 
 
+def raw_check():
+    """Synchronise the device and raise if a bounded wait of the raw tensor-core GEMM gave up."""
+    call("enx_raw_check")
+
+
 def lm_head_q8(x, packed, scales, zeros, out, rows, hidden, row_begin=0, out_offset=0, stream=None):
     """lm_head_q8 (src/kernels/embedding_variants.ts:135-180)."""
     d = EmbeddingDims(1, hidden, row_begin, rows, 64, hidden // 64, 0, out_offset, min(rows, 65535), 0, 0, 0)

@@ -72,6 +72,17 @@ ENX_API enx_status enx_matmul_q4(const float* x, const uint32_t* packed, const f
                          const uint32_t* zeros, const float* bias, float* out,
                          const enx_matmul_q4_dims* dims, void* stream);
 
+/* The raw tensor-core paths of enx_matmul_q4 (m >= 16) and enx_lm_head_q8 (seq >= 16) share one
+ * library-owned workspace per device (activation limbs, split-K partials, int8 weight codes),
+ * grown on demand: calls that overlap on the GPU (other streams, other threads) race on it, so
+ * serialise them.  Their bounded device waits record a sticky error word instead of hanging;
+ * enx_raw_check reads it. */
+
+/* Synchronise the current device and report (then clear) the sticky error word of the raw
+ * tensor-core entry points: ENX_ERR_TIMEOUT if a bounded wait gave up since the last check, whose
+ * outputs are then invalid.  No reference counterpart (WebGPU kernels have no device waits). */
+ENX_API enx_status enx_raw_check(void);
+
 /* embeddingDims, 48 bytes (src/kernels/embedding_variants.ts:76-90, 207-221). */
 typedef struct {
     uint32_t seq, hidden, row_begin, row_count;

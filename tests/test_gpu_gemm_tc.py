@@ -28,7 +28,7 @@ def run(x, t, bias, m, out_stride=None, out_offset=0):
     out = torch.zeros(m * stride + out_offset, dtype=torch.float32, device="cuda")
     K.matmul_q4(dev(x), K.to_device_u32(t.packed), dev(t.scales), K.to_device_u32(t.zeros),
                 None if bias is None else dev(bias), out, m, n, k, stride, out_offset)
-    torch.cuda.synchronize()
+    K.raw_check()  # synchronises; raises if a bounded device wait gave up
     return out.cpu().numpy()
 
 
