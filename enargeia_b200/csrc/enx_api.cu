@@ -106,6 +106,20 @@ extern "C" enx_status enx_raw_check(void) {
                                      std::to_string(code) + ")");
 }
 
+extern "C" enx_status enx_set_wait_limit(int device, uint32_t spins) {
+    int n = 0;
+    ENX_CUDA(cudaGetDeviceCount(&n));
+    if (device < 0 || device >= n) return fail(ENX_ERR_INVALID, "enx_set_wait_limit: no such device");
+    int prev = 0;
+    ENX_CUDA(cudaGetDevice(&prev));
+    ENX_CUDA(cudaSetDevice(device));
+    cudaError_t e = mega_set_spin(spins);
+    if (e == cudaSuccess) e = tc_set_spin(spins);
+    cudaSetDevice(prev);
+    ENX_CUDA(e);
+    return ENX_OK;
+}
+
 extern "C" enx_status enx_matmul_q4(const float* x, const uint32_t* packed, const float* scales,
                                     const uint32_t* zeros, const float* bias, float* out,
                                     const enx_matmul_q4_dims* d, void* stream) {
@@ -482,6 +496,13 @@ template <typename T>
 void dfree(T*& p) {
     if (p) cudaFree(p);
     p = nullptr;
+}
+
+// ENX_ERR_TIMEOUT with the caller's name and which wait gave up (codes of the device error words:
+// 1 grid barrier or readiness counter, 2 weight copy into the ring, 3 tensor-core GEMM pipeline).
+static enx_status timeout_error(const char* caller, uint32_t code) {
+    const char* what = code == 1 ? "grid barrier" : code == 2 ? "weight copy" : code == 3 ? "tensor-core GEMM wait" : "device wait";
+    return fail(ENX_ERR_TIMEOUT, std::string(caller) + ": a bounded device wait gave up (" + what + ")");
 }
 
 struct DeviceGuard {
@@ -956,7 +977,7 @@ static enx_status ensure_prefill(enx_ctx* c, uint32_t chunk) {
     return ENX_OK;
 }
 
-static enx_status device_error(enx_ctx* c);
+static enx_status device_error(enx_ctx* c, const char* caller);
 
 extern "C" enx_status enx_prefill(enx_ctx* c, uint32_t seq, const uint32_t* ids, uint32_t n, uint32_t chunk) {
     CHECK_ARG(c && ids, "enx_prefill: null pointer");
@@ -976,6 +997,7 @@ extern "C" enx_status enx_prefill(enx_ctx* c, uint32_t seq, const uint32_t* ids,
     ENX_TRY(ensure_prefill(c, chunk));
     cudaStream_t st = c->stream;
     const uint32_t H = C.hidden, kv = C.kv_heads * C.head_dim, I = C.intermediate;
+    const uint32_t filled0 = c->filled[seq];
     StepArgs S = step_args(c);
     S.seq_fixed = seq;
     S.q = c->pf_q2;
@@ -1020,7 +1042,11 @@ extern "C" enx_status enx_prefill(enx_ctx* c, uint32_t seq, const uint32_t* ids,
         }
     }
     ENX_CUDA(cudaStreamSynchronize(st));
-    return device_error(c);  // the tensor-core GEMMs' bounded waits report through the step's error word
+    // the tensor-core GEMMs' bounded waits report through the step's error word; on a timeout the
+    // cache rows this call wrote are not valid, so the sequence keeps its fill from before the call
+    const enx_status e = device_error(c, "enx_prefill");
+    if (e != ENX_OK) c->filled[seq] = filled0;
+    return e;
 }
 
 extern "C" enx_status enx_sample_prefill(enx_ctx* c, uint32_t seq, const enx_sampling* params, float random,
@@ -1454,8 +1480,7 @@ extern "C" enx_status enx_decode_step(enx_ctx* c, uint32_t batch, const uint32_t
         const uint32_t code = h->err;
         h->err = 0;
         cudaMemsetAsync(&c->d_step->err, 0, 4, c->stream);
-        return fail(ENX_ERR_TIMEOUT, std::string("decode step: a bounded device wait gave up (") +
-                                         (code == 1 ? "grid barrier" : "weight copy") + ")");
+        return timeout_error("enx_decode_step", code);
     }
     for (uint32_t b = 0; b < batch; ++b) {
         out_ids[b] = h->out[b];
@@ -1465,7 +1490,7 @@ extern "C" enx_status enx_decode_step(enx_ctx* c, uint32_t batch, const uint32_t
     return ENX_OK;
 }
 
-static enx_status device_error(enx_ctx* c);
+static enx_status device_error(enx_ctx* c, const char* caller);
 
 extern "C" enx_status enx_decode_loop(enx_ctx* c, uint32_t batch, const uint32_t* first_tokens,
                                       const enx_sampling* params, uint32_t params_count, uint32_t steps,
@@ -1507,20 +1532,19 @@ extern "C" enx_status enx_decode_loop(enx_ctx* c, uint32_t batch, const uint32_t
     c->last_launches = c->loop_launches[batch];
     if (sync) {
         ENX_CUDA(cudaStreamSynchronize(c->stream));
-        ENX_TRY(device_error(c));
+        ENX_TRY(device_error(c, "enx_decode_loop"));
         std::memcpy(out_ids, c->h_loop_ids, (size_t)steps * batch * 4);
     }
     return ENX_OK;
 }
 
 // Reads (and clears) the sticky device error word after the stream has drained.
-static enx_status device_error(enx_ctx* c) {
+static enx_status device_error(enx_ctx* c, const char* caller) {
     uint32_t code = 0;
     ENX_CUDA(cudaMemcpy(&code, &c->d_step->err, 4, cudaMemcpyDeviceToHost));
     if (!code) return ENX_OK;
     ENX_CUDA(cudaMemset(&c->d_step->err, 0, 4));
-    return fail(ENX_ERR_TIMEOUT, std::string("decode step: a bounded device wait gave up (") +
-                                     (code == 1 ? "grid barrier" : "weight copy") + ")");
+    return timeout_error(caller, code);
 }
 
 extern "C" enx_status enx_synchronize(enx_ctx* c) {
@@ -1532,7 +1556,7 @@ extern "C" enx_status enx_synchronize(enx_ctx* c) {
         ENX_CUDA(cudaMemcpy(&code, c->d_bb + c->bl.err(), 4, cudaMemcpyDeviceToHost));
         if (code) return batch_error(c, code);
     }
-    return c->d_step ? device_error(c) : ENX_OK;
+    return c->d_step ? device_error(c, "enx_synchronize") : ENX_OK;
 }
 
 extern "C" enx_status enx_loop_ids(enx_ctx* c, uint32_t* out_ids, uint32_t count) {

@@ -44,7 +44,11 @@ constexpr uint32_t kTcLimbs = 6;       // balanced int8 limbs of a 46-bit X
 constexpr uint32_t kTcN = kTcLimbs * kTcTokens;  // MMA N = 192, limb-major: column 32 l + t
 constexpr uint32_t kTcAccCols = 256;   // columns between the two accumulators
 constexpr uint32_t kTcTmemCols = 512;  // TMEM allocation: the two accumulators
-constexpr uint32_t kTcSpin = 1u << 24;
+constexpr uint32_t kTcSpin = 1u << 24;  // default wait limit, and the limit of the drain waits
+
+// Spins a wait may take before it gives up (enx_set_wait_limit; per device).  Drain waits (copies
+// and MMAs still in flight when the CTA stops) always use kTcSpin.
+__device__ uint32_t g_tc_spin = kTcSpin;
 
 __device__ __forceinline__ uint32_t su32(const void* p) { return static_cast<uint32_t>(__cvta_generic_to_shared(p)); }
 
@@ -156,8 +160,9 @@ constexpr uint32_t kTcATile = kTcRows * 64;               // 8 KB of codes per b
 constexpr uint32_t kTcMaxSplit = 16;
 
 // Bounded wait on an mbarrier phase that gives up early when another role has failed.
-__device__ __forceinline__ bool mbar_wait_f(uint64_t* bar, uint32_t parity, volatile int* fail, uint32_t* err) {
-    for (uint32_t it = 0; it < kTcSpin; ++it) {
+__device__ __forceinline__ bool mbar_wait_f(uint64_t* bar, uint32_t parity, volatile int* fail, uint32_t* err,
+                                            uint32_t limit) {
+    for (uint32_t it = 0; it < limit; ++it) {
         uint32_t ok;
         asm volatile("{\n .reg .pred p;\n mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n selp.u32 %0, 1, 0, p;\n}\n"
                      : "=r"(ok)
@@ -169,6 +174,19 @@ __device__ __forceinline__ bool mbar_wait_f(uint64_t* bar, uint32_t parity, vola
     atomicMax(err, 3u);
     *fail = 1;
     return false;
+}
+
+// Waits (bounded by kTcSpin, ignoring other roles' failure) until a phase has completed: the drain
+// of copies or MMAs this thread issued, before the CTA may release its shared memory and TMEM.
+__device__ __forceinline__ void mbar_drain(uint64_t* bar, uint32_t parity) {
+    for (uint32_t it = 0; it < kTcSpin; ++it) {
+        uint32_t ok;
+        asm volatile("{\n .reg .pred p;\n mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n selp.u32 %0, 1, 0, p;\n}\n"
+                     : "=r"(ok)
+                     : "r"(su32(bar)), "r"(parity)
+                     : "memory");
+        if (ok) return;
+    }
 }
 
 __device__ __forceinline__ void mbar_arrive(uint64_t* bar) {
@@ -258,13 +276,15 @@ __global__ void __launch_bounds__(kTcWsThreads, 1)
     __syncthreads();
     asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
     const uint32_t tmem = tmem_base;
+    const uint32_t spin = g_tc_spin;
 
     if (warp == kTcProdWarp) {
         // ---- producer: one thread, a TMA box of codes and a bulk copy of limbs per block ------------
         if (lane == 0) {
+            uint32_t issued = 0;
             for (uint32_t i = 0; i < nblk; ++i) {
                 const uint32_t s = i % kTcStages;
-                if (i >= kTcStages && !mbar_wait_f(&empty[s], ((i / kTcStages) - 1) & 1, &s_fail, err)) break;
+                if (i >= kTcStages && !mbar_wait_f(&empty[s], ((i / kTcStages) - 1) & 1, &s_fail, err, spin)) break;
                 asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(su32(&full[s])),
                              "r"(kTcATile + kTcLimbTileBytes)
                              : "memory");
@@ -274,17 +294,22 @@ __global__ void __launch_bounds__(kTcWsThreads, 1)
                                  su32(sB + s * kTcLimbTileBytes)),
                              "l"(ltile + (size_t)(kb0 + i) * kTcLimbTileBytes), "r"(kTcLimbTileBytes), "r"(su32(&full[s]))
                              : "memory");
+                issued = i + 1;
             }
+            // no copy may still be landing when the CTA releases its shared memory (error path)
+            for (uint32_t i = issued > kTcStages ? issued - kTcStages : 0; i < issued; ++i)
+                mbar_drain(&full[i % kTcStages], (i / kTcStages) & 1);
         }
         __syncwarp();
     } else if (warp == kTcMmaWarp) {
         // ---- MMA issue: one thread ----------------------------------------------------------------
         pdl_wait();
         if (lane == 0) {
+            uint32_t mmas = 0;
             for (uint32_t i = 0; i < nblk; ++i) {
                 const uint32_t s = i % kTcStages, a = i & 1;
-                if (!mbar_wait_f(&full[s], (i / kTcStages) & 1, &s_fail, err)) break;
-                if (i >= 2 && !mbar_wait_f(&acce[a], ((i >> 1) - 1) & 1, &s_fail, err)) break;
+                if (!mbar_wait_f(&full[s], (i / kTcStages) & 1, &s_fail, err, spin)) break;
+                if (i >= 2 && !mbar_wait_f(&acce[a], ((i >> 1) - 1) & 1, &s_fail, err, spin)) break;
                 asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
                 const uint32_t dcol = tmem + a * kTcAccCols;
 #pragma unroll
@@ -301,7 +326,10 @@ __global__ void __launch_bounds__(kTcWsThreads, 1)
                 asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(
                                  su32(&accf[a]))
                              : "memory");
+                mmas = i + 1;
             }
+            // every issued MMA complete before TMEM is freed (its last commit tracks all of them)
+            if (mmas) mbar_drain(&accf[(mmas - 1) & 1], ((mmas - 1) >> 1) & 1);
         }
         __syncwarp();
     } else {
@@ -323,7 +351,7 @@ __global__ void __launch_bounds__(kTcWsThreads, 1)
                 if (BITS == 8) z_next = zero_code<BITS>(w.zeros, grow * bpr + b + 1);
             }
             int ok = 1;
-            if (lane == 0) ok = mbar_wait_f(&accf[a], (i >> 1) & 1, &s_fail, err);
+            if (lane == 0) ok = mbar_wait_f(&accf[a], (i >> 1) & 1, &s_fail, err, spin);
             if (!__shfl_sync(0xffffffffu, ok, 0)) break;
             asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
             // per token of this block (int8 only): the X sum, from the limb tile in global memory
@@ -384,6 +412,11 @@ __global__ void __launch_bounds__(kTcWsThreads, 1)
     asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
     if (warp == kTcMmaWarp)
         asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(kTcTmemCols));
+}
+
+cudaError_t tc_set_spin(uint32_t spins) {
+    const uint32_t v = spins ? spins : kTcSpin;
+    return cudaMemcpyToSymbol(g_tc_spin, &v, sizeof(v));
 }
 
 // Split-K: out = float(sum of the splits' partials in split order + bias).

@@ -29,4 +29,8 @@ cudaError_t launch_gemm_tc(int bits, const float* x, uint32_t ld, const QW& w, c
                            float* out, uint32_t m, uint32_t out_stride, uint32_t out_offset, uint8_t* workspace,
                            uint32_t* err, cudaStream_t st, bool limbs_ready = false);
 
+// Spins a bounded wait of the tensor-core GEMM takes before it gives up (current device; 0 = the
+// default 2^24).
+cudaError_t tc_set_spin(uint32_t spins);
+
 }  // namespace enx

@@ -37,6 +37,10 @@ constexpr int kMWarps = 16;                  // consumer warps
 constexpr int kMConsumers = kMWarps * 32;    // consumer threads (named barrier 1)
 constexpr int kMThreads = kMConsumers + 32;  // + one producer warp
 constexpr uint32_t kSpinLimit = 1u << 24;    // bounded waits (well under a minute), then an error
+
+// Spins a wait may take before it gives up (enx_set_wait_limit; per device).  The producer's final
+// drain of its copies in flight always uses kSpinLimit.
+__device__ uint32_t g_mega_spin = kSpinLimit;
 constexpr uint32_t kKvHalfs = 16384;         // f16 staging of cached K and V rows (32 KB)
 constexpr int kMaxRes = 96;                  // rows per token exchanged in shared memory (C, D)
 constexpr int kHeadDimMax = 64;
@@ -64,8 +68,8 @@ __device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
                  : "memory");
     return ok != 0;
 }
-__device__ __forceinline__ bool mbar_wait_bounded(uint64_t* bar, uint32_t parity) {
-    for (uint32_t it = 0; it < kSpinLimit; ++it)
+__device__ __forceinline__ bool mbar_wait_bounded(uint64_t* bar, uint32_t parity, uint32_t limit) {
+    for (uint32_t it = 0; it < limit; ++it)
         if (mbar_try_wait(bar, parity)) return true;
     return false;
 }
@@ -102,7 +106,7 @@ __device__ __forceinline__ void stamp_a(const MegaArgs& A, uint32_t l, uint32_t 
 // ---------------------------------------------------------------------------------------------
 // grid barrier (consumer threads only; bounded)
 
-__device__ bool grid_sync(const MegaArgs& A, uint32_t& index, volatile int* s_fail) {
+__device__ bool grid_sync(const MegaArgs& A, uint32_t& index, volatile int* s_fail, uint32_t spin) {
     cbar();
     if (threadIdx.x == 0) {
         const unsigned long long target = (unsigned long long)(index + 1) * gridDim.x;
@@ -111,7 +115,7 @@ __device__ bool grid_sync(const MegaArgs& A, uint32_t& index, volatile int* s_fa
             unsigned long long v;
             asm volatile("ld.acquire.gpu.global.u64 %0, [%1];" : "=l"(v) : "l"(A.bar) : "memory");
             if (v >= target) break;
-            if (it > kSpinLimit) {
+            if (it > spin) {
                 atomicMax(A.err, 1u);
                 *s_fail = 1;
                 break;
@@ -456,6 +460,13 @@ __device__ void attend(const MegaArgs& A, uint32_t l, uint32_t t, uint32_t g, ui
 // ---------------------------------------------------------------------------------------------
 // the kernel
 
+// A consumer leaves early (a bounded wait gave up): its own cp.async copies land first.
+#define BAIL()               \
+    do {                     \
+        cp_async_wait_all(); \
+        return;              \
+    } while (0)
+
 template <int MT, int HB>
 __global__ void __launch_bounds__(kMThreads, 1) k_mega(const __grid_constant__ MegaArgs A) {
     extern __shared__ __align__(128) uint8_t smem[];
@@ -472,6 +483,7 @@ __global__ void __launch_bounds__(kMThreads, 1) k_mega(const __grid_constant__ M
     const uint32_t H = A.hidden, I = A.intermediate, hd = A.head_dim, half = hd / 2;
     const uint32_t NS = A.nslots, SB = A.slot_bytes;
     const uint32_t group = A.heads / A.kv_heads;
+    const uint32_t spin = g_mega_spin;
 
     uint64_t* full = reinterpret_cast<uint64_t*>(smem);
     uint64_t* empty = full + kMegaSlots;
@@ -521,7 +533,7 @@ __global__ void __launch_bounds__(kMThreads, 1) k_mega(const __grid_constant__ M
             const uint32_t slot = i % NS;
             int ok = 1;
             if (lane == 0) {
-                if (i >= NS && !mbar_wait_bounded(empty + slot, ((i / NS) - 1) & 1u)) {
+                if (i >= NS && !mbar_wait_bounded(empty + slot, ((i / NS) - 1) & 1u, spin)) {
                     atomicMax(A.err, 2u);
                     ok = 0;
                 }
@@ -547,7 +559,8 @@ __global__ void __launch_bounds__(kMThreads, 1) k_mega(const __grid_constant__ M
         }
         // no copy may still be writing into shared memory when the CTA retires
         if (lane == 0)
-            for (uint32_t i = issued > NS ? issued - NS : 0; i < issued; ++i) mbar_wait_bounded(full + i % NS, (i / NS) & 1u);
+            for (uint32_t i = issued > NS ? issued - NS : 0; i < issued; ++i)
+                mbar_wait_bounded(full + i % NS, (i / NS) & 1u, kSpinLimit);
         return;
     }
 
@@ -556,13 +569,13 @@ __global__ void __launch_bounds__(kMThreads, 1) k_mega(const __grid_constant__ M
     // Thread 0 alone waits (bounded) so that every consumer takes the same branch; the others
     // then observe the completed phase themselves, which orders the copied bytes before their reads.
     auto wait_slice = [&]() -> bool {
-        if (tid == 0 && !mbar_wait_bounded(full + slice % NS, (slice / NS) & 1u)) {
+        if (tid == 0 && !mbar_wait_bounded(full + slice % NS, (slice / NS) & 1u, spin)) {
             atomicMax(A.err, 2u);
             s_fail = 1;
         }
         cbar();
         if (s_fail) return false;
-        if (tid != 0) mbar_wait_bounded(full + slice % NS, (slice / NS) & 1u);
+        if (tid != 0) mbar_wait_bounded(full + slice % NS, (slice / NS) & 1u, spin);
         return true;
     };
     auto release_slice = [&]() {
@@ -599,7 +612,7 @@ __global__ void __launch_bounds__(kMThreads, 1) k_mega(const __grid_constant__ M
             }
             cp_async_commit();
         }
-        if (!wait_slice()) return;
+        if (!wait_slice()) BAIL();
         stamp(A, 3 * (kMegaStages * l + 0) + 1);
         {
             const MegaSlice& D = sdesc[slice % NS];
@@ -678,7 +691,7 @@ __global__ void __launch_bounds__(kMThreads, 1) k_mega(const __grid_constant__ M
                     uint32_t v;
                     asm volatile("ld.acquire.gpu.global.u32 %0, [%1];" : "=r"(v) : "l"(flag) : "memory");
                     if (v >= target) break;
-                    if (it > kSpinLimit) {
+                    if (it > spin) {
                         atomicMax(A.err, 1u);
                         s_fail = 1;
                         break;
@@ -686,7 +699,7 @@ __global__ void __launch_bounds__(kMThreads, 1) k_mega(const __grid_constant__ M
                 }
             }
             cbar();
-            if (s_fail) return;
+            if (s_fail) BAIL();
             stamp_a(A, l, 2);
             const uint32_t kvd = A.kv_heads * hd, row8 = hd / 8;
             for (uint32_t d = tid; d < hd; d += kMConsumers) hs.qd[d] = (double)__ldcg(A.S.q + (size_t)at * H + ah * hd + d);
@@ -714,7 +727,7 @@ __global__ void __launch_bounds__(kMThreads, 1) k_mega(const __grid_constant__ M
                     uint32_t v;
                     asm volatile("ld.acquire.gpu.global.u32 %0, [%1];" : "=r"(v) : "l"(A.done + t) : "memory");
                     if (v >= target) break;
-                    if (it > kSpinLimit) {
+                    if (it > spin) {
                         atomicMax(A.err, 1u);
                         s_fail = 1;
                         break;
@@ -722,13 +735,13 @@ __global__ void __launch_bounds__(kMThreads, 1) k_mega(const __grid_constant__ M
                 }
         }
         cbar();
-        if (s_fail) return;
+        if (s_fail) BAIL();
         stamp_a(A, l, 5);
         for (uint32_t t = 0; t < MT; ++t)
             for (uint32_t k = tid; k < H; k += kMConsumers) Xd[xd_index<4>(t, k, H / 32)] = (double)__ldcg(A.S.attn_out + t * H + k);
         cbar();
         stage_xsum<4, MT>(Xd, xsum, H / 32);
-        if (!wait_slice()) return;
+        if (!wait_slice()) BAIL();
         {
             const MegaSlice& D = sdesc[slice % NS];
             if (D.nrange) {
@@ -757,11 +770,11 @@ __global__ void __launch_bounds__(kMThreads, 1) k_mega(const __grid_constant__ M
         release_slice();
         stamp_a(A, l, 6);
         stamp(A, 3 * (kMegaStages * l + 0) + 2);
-        if (!grid_sync(A, bar_index, &s_fail)) return;
+        if (!grid_sync(A, bar_index, &s_fail, spin)) BAIL();
 
         // ---------------- C: residual + RMSNorm + gate|up + SiLU ----------------------------
         stamp(A, 3 * (kMegaStages * l + 1));
-        if (!wait_slice()) return;
+        if (!wait_slice()) BAIL();
         stamp(A, 3 * (kMegaStages * l + 1) + 1);
         {
             const MegaSlice& D = sdesc[slice % NS];
@@ -790,7 +803,7 @@ __global__ void __launch_bounds__(kMThreads, 1) k_mega(const __grid_constant__ M
         }
         release_slice();
         stamp(A, 3 * (kMegaStages * l + 1) + 2);
-        if (!grid_sync(A, bar_index, &s_fail)) return;
+        if (!grid_sync(A, bar_index, &s_fail, spin)) BAIL();
 
         // ---------------- D: down + residual ------------------------------------------------
         stamp(A, 3 * (kMegaStages * l + 2));
@@ -814,7 +827,7 @@ __global__ void __launch_bounds__(kMThreads, 1) k_mega(const __grid_constant__ M
             cbar();
             stage_xsum<4, MT>(Xd, xsum, nchunk);
         }
-        if (!wait_slice()) return;
+        if (!wait_slice()) BAIL();
         stamp(A, 3 * (kMegaStages * l + 2) + 1);
         {
             const MegaSlice& D = sdesc[slice % NS];
@@ -843,7 +856,7 @@ __global__ void __launch_bounds__(kMThreads, 1) k_mega(const __grid_constant__ M
         }
         release_slice();
         stamp(A, 3 * (kMegaStages * l + 2) + 2);
-        if (!grid_sync(A, bar_index, &s_fail)) return;
+        if (!grid_sync(A, bar_index, &s_fail, spin)) BAIL();
     }
 
     // ---------------- final RMSNorm + tied head ---------------------------------------------
@@ -854,7 +867,7 @@ __global__ void __launch_bounds__(kMThreads, 1) k_mega(const __grid_constant__ M
     auto now = []() { unsigned long long t; asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t)); return t; };
     if (A.trace && c == 0 && tid == 0) tmark = now();
     while (slice < total) {
-        if (!wait_slice()) return;
+        if (!wait_slice()) BAIL();
         if (A.trace && c == 0 && tid == 0) { const unsigned long long t = now(); tw += t - tmark; tmark = t; }
         const MegaSlice& D = sdesc[slice % NS];
         const uint8_t* slot = slot_ptr();
@@ -1136,6 +1149,11 @@ MegaGeometry mega_geometry(uint32_t mt, const MegaArgs& A) {
         A.kv_heads * (size_t)mt > 64)
         g.nslots = 0;
     return g;
+}
+
+cudaError_t mega_set_spin(uint32_t spins) {
+    const uint32_t v = spins ? spins : kSpinLimit;
+    return cudaMemcpyToSymbol(g_mega_spin, &v, sizeof(v));
 }
 
 cudaError_t launch_mega(uint32_t mt, const MegaArgs& A, const MegaGeometry& g, cudaStream_t st) {

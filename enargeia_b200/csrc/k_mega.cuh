@@ -83,6 +83,9 @@ void mega_build_table(uint32_t mt, const MegaArgs& A, const QW& head_slices, con
 constexpr uint32_t kHeadSlice = 32;
 size_t mega_head_slices_bytes(uint32_t vocab, uint32_t hidden, int bits);
 cudaError_t mega_head_slices(const QW& head, int bits, uint8_t* out, QW* view, cudaStream_t st);
+// Spins a bounded wait of the persistent kernel takes before it gives up (current device; 0 = the
+// default 2^24).
+cudaError_t mega_set_spin(uint32_t spins);
 cudaError_t launch_mega(uint32_t mt, const MegaArgs& A, const MegaGeometry& g, cudaStream_t st);
 
 }  // namespace enx

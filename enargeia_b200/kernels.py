@@ -38,12 +38,17 @@ def _u32(t: torch.Tensor):
 
 
 def matmul_q4(x, packed, scales, zeros, bias, out, m, n, k, out_stride=None, out_offset=0, stream=None):
-    """matmul_q4_decode / matmul_q4_prefill (src/kernels/matmul_q4.ts:151-191)."""
+    """matmul_q4_decode / matmul_q4_prefill (src/kernels/matmul_q4.ts:50-64)."""
     d = MatmulQ4Dims(m, n, k, 1 if bias is not None else 0, 64, k // 64, n if out_stride is None else out_stride,
                      out_offset, min(n, 65535), 0, 0, 0)
     call("enx_matmul_q4", _ptr(x), _u32(packed), _ptr(scales), _u32(zeros), _ptr(bias), _ptr(out), C.byref(d),
          _stream(stream))
     return out
+
+
+def set_wait_limit(spins: int, device: int = 0) -> None:
+    """Polls a bounded device wait makes before it gives up (0: the default)."""
+    call("enx_set_wait_limit", device, spins)
 
 
 def raw_check():

@@ -56,7 +56,7 @@ ENX_API const char* enx_version(void);
  * Raw kernels.  Dims structs are the reference's uniform blocks, byte for byte.
  * ---------------------------------------------------------------------------------------- */
 
-/* matmulQ4Dims, 48 bytes (src/kernels/matmul_q4.ts:151-165). */
+/* matmulQ4Dims, 48 bytes (src/kernels/matmul_q4.ts:50-64). */
 typedef struct {
     uint32_t m, n, k, use_bias;
     uint32_t block_size, blocks_per_row, out_stride, out_offset;
@@ -78,10 +78,21 @@ ENX_API enx_status enx_matmul_q4(const float* x, const uint32_t* packed, const f
  * serialise them.  Their bounded device waits record a sticky error word instead of hanging;
  * enx_raw_check reads it. */
 
-/* Synchronise the current device and report (then clear) the sticky error word of the raw
- * tensor-core entry points: ENX_ERR_TIMEOUT if a bounded wait gave up since the last check, whose
- * outputs are then invalid.  No reference counterpart (WebGPU kernels have no device waits). */
+/* Report (then clear) the sticky error word of the raw tensor-core entry points:
+ * ENX_ERR_TIMEOUT if a bounded wait gave up since the last check, whose outputs are then
+ * invalid.  It first waits for ALL work on the current device (cudaDeviceSynchronize), including
+ * the streams of other enx contexts and of other libraries on that device, so it must not be
+ * called while any stream of the device is being captured into a CUDA graph.  No reference
+ * counterpart (WebGPU kernels have no device waits). */
 ENX_API enx_status enx_raw_check(void);
+
+/* How many polls a bounded device-side wait (grid barrier, readiness counter, ring or pipeline
+ * mbarrier of the persistent decode kernel and of the tensor-core GEMM) makes on `device` before
+ * it gives up and the call reports ENX_ERR_TIMEOUT; 0 restores the default (2^24 polls, well
+ * under a minute).  A waiting CTA that gives up still waits, with the default limit, for the
+ * copies and MMAs it issued before it exits.  Applies to launches made after the call (CUDA graphs
+ * already captured included).  No reference counterpart: a hook to exercise the timeout path. */
+ENX_API enx_status enx_set_wait_limit(int device, uint32_t spins);
 
 /* embeddingDims, 48 bytes (src/kernels/embedding_variants.ts:76-90, 207-221). */
 typedef struct {
@@ -118,8 +129,10 @@ typedef struct {
  * then greedy argmax (temperature <= 0) or temperature / top-p / seeded draw; writes one id to
  * out[0].  Bindings: logits (read_write), history, out, dims.  Probabilities, bisection masses
  * and the running draw total are computed in double (the oracle's exact-arithmetic rule).
- * `workspace` is unused and may be NULL (the kernel keeps its state in shared memory); the
- * argument exists so the call shape matches the batched entry point. */
+ * `workspace` is an EXTENSION of the reference's binding list (logits, history, out, dims;
+ * src/kernels/sample.ts:24-52): it is unused and may be NULL (the kernel keeps its state in
+ * shared memory), and is kept so the raw entry points share one call shape (inputs, output,
+ * dims, workspace, stream). */
 ENX_API enx_status enx_sample(float* logits, const uint32_t* history, uint32_t* out,
                       const enx_sample_dims* dims, void* workspace, void* stream);
 

@@ -527,6 +527,13 @@ orc_model* orc_model_create(const orc_config* cfg, const orc_weights* w, int64_t
 }
 
 void orc_model_destroy(orc_model* m) { delete m; }
+// A copy of `src` with the same weights and the same cache contents and fill: one shared prompt
+// prefilled once, then continued as several independent sequences (test speed only).
+orc_model* orc_model_fork(const orc_model* src) {
+    orc_model* m = new orc_model(*src);
+    m->w.layers = m->layers.data();
+    return m;
+}
 void orc_model_reset(orc_model* m) { m->filled = 0; }
 int64_t orc_model_filled(const orc_model* m) { return m->filled; }
 

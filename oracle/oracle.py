@@ -104,6 +104,8 @@ def _declare(L):
     L.orc_model_create.restype = P
     L.orc_model_create.argtypes = [C.POINTER(Config), C.POINTER(Weights), I64]
     L.orc_model_destroy.argtypes = [P]
+    L.orc_model_fork.restype = P
+    L.orc_model_fork.argtypes = [P]
     L.orc_model_reset.argtypes = [P]
     L.orc_model_filled.restype = I64
     L.orc_model_filled.argtypes = [P]
@@ -307,6 +309,14 @@ class OracleModel:
         c = Config(cfg.layers, cfg.hidden, cfg.heads, cfg.kv_heads, cfg.head_dim, cfg.intermediate, cfg.vocab,
                    cfg.rms_norm_eps, cfg.rope_theta)
         self._h = lib().orc_model_create(C.byref(c), C.byref(w), max_context)
+
+    def fork(self) -> "OracleModel":
+        """An independent copy of this model's state (same weights, same cache and fill)."""
+        other = OracleModel.__new__(OracleModel)
+        other.f, other.cfg, other.max_context = self.f, self.cfg, self.max_context
+        other._keep, other._layers = self._keep, self._layers
+        other._h = lib().orc_model_fork(self._h)
+        return other
 
     def __del__(self):
         h = getattr(self, "_h", None)
