@@ -77,6 +77,7 @@ SIGNATURES = {
     "enx_version": (C.c_char_p, []),
     "enx_matmul_q4": (C.c_int32, [P, P, P, P, P, P, C.POINTER(MatmulQ4Dims), P]),
     "enx_set_wait_limit": (C.c_int32, [C.c_int, U32]),
+    "enx_nll": (C.c_int32, [P, U32, U32, C.POINTER(C.c_double)]),
     "enx_lm_head_q8": (C.c_int32, [P, P, P, P, P, C.POINTER(EmbeddingDims), P]),
     "enx_embed_gather_q8": (C.c_int32, [P, P, P, P, P, C.POINTER(EmbeddingDims), P]),
     "enx_sample": (C.c_int32, [P, P, P, C.POINTER(SampleDims), P, P]),

@@ -326,9 +326,18 @@ struct StepBlock {
     uint32_t err;  // sticky device error of the persistent kernel (read back with `out`)
 };
 
-__global__ void k_step_prep(StepBlock* blk, uint32_t* history, uint32_t max_ctx, uint32_t batch) {
+// Before each launch of the persistent step kernel (see k_mega.cu, tagged activations): its tag
+// epoch (low half of word 0) one more.
+__device__ __forceinline__ void mega_prep_counters(unsigned long long* bar) {
+    if (threadIdx.x == 0) *reinterpret_cast<uint32_t*>(bar) += 1;
+}
+
+__global__ void k_bump_epoch(unsigned long long* bar) { mega_prep_counters(bar); }
+
+__global__ void k_step_prep(StepBlock* blk, uint32_t* history, uint32_t max_ctx, uint32_t batch, unsigned long long* bar) {
     uint32_t b = threadIdx.x;
     if (b < batch) history[(size_t)b * max_ctx + blk->pos[b]] = blk->tokens[b];
+    mega_prep_counters(bar);
 }
 
 // State of a device-fed decode loop: step counter, start positions, first tokens, params.
@@ -340,8 +349,9 @@ struct LoopState {
 };
 
 __global__ void k_loop_prep(LoopState* L, StepBlock* blk, const float* randoms, const uint32_t* ids,
-                            uint32_t* history, uint32_t max_ctx, uint32_t batch) {
+                            uint32_t* history, uint32_t max_ctx, uint32_t batch, unsigned long long* bar) {
     uint32_t b = threadIdx.x;
+    mega_prep_counters(bar);
     if (b >= batch) return;
     uint32_t i = L->i;
     uint32_t tok = i == 0 ? L->first[b] : ids[(size_t)(i - 1) * batch + b];
@@ -445,7 +455,9 @@ struct enx_ctx {
     uint32_t* d_loop_ids = nullptr;
     uint32_t* h_loop_ids = nullptr;
     uint32_t loop_cap = 0, loop_count = 0;
-    unsigned long long* d_bar = nullptr;  // grid-barrier counter of the persistent step kernel
+    unsigned long long* d_bar = nullptr;  // step counters; word 0: tag epoch of the persistent step kernel
+    unsigned long long* d_ll = nullptr;   // tagged stage outputs of the persistent step kernel
+    double* d_nll = nullptr;              // enx_nll's result
     unsigned long long* d_trace = nullptr;  // stage stamps when tracing is on
     uint32_t trace_len = 0;
     bool graph_mega[kMaxStepBatch + 1] = {};
@@ -555,7 +567,7 @@ void free_kv(enx_ctx* c) {
     dfree(c->d_step);
     if (c->h_step) cudaFreeHost(c->h_step);
     c->h_step = nullptr;
-    dfree(c->d_loop); dfree(c->d_loop_rand); dfree(c->d_loop_ids); dfree(c->d_bar);
+    dfree(c->d_loop); dfree(c->d_loop_rand); dfree(c->d_loop_ids); dfree(c->d_bar); dfree(c->d_ll); dfree(c->d_nll);
     if (c->h_loop) cudaFreeHost(c->h_loop);
     if (c->h_loop_ids) cudaFreeHost(c->h_loop_ids);
     c->h_loop = nullptr;
@@ -838,7 +850,9 @@ extern "C" enx_status enx_kv_alloc(enx_ctx* c, uint32_t max_context, uint32_t ba
     std::memset(c->h_step, 0, sizeof(StepBlock));
     // device-fed loop: room for every step the caches can hold
     c->loop_cap = max_context * B;
-    ENX_TRY(dalloc(&c->d_bar, kMegaBarWords, "barrier counters"));
+    ENX_TRY(dalloc(&c->d_nll, 1, "nll result"));
+    ENX_TRY(dalloc(&c->d_bar, kMegaBarWords, "step counters"));
+    ENX_CUDA(cudaMemsetAsync(c->d_bar, 0, kMegaBarWords * sizeof(unsigned long long), c->stream));
     ENX_CUDA(cudaMemsetAsync(c->d_step, 0, sizeof(StepBlock), c->stream));
     ENX_TRY(dalloc(&c->d_loop, 1, "loop state"));
     ENX_TRY(dalloc(&c->d_loop_rand, c->loop_cap, "loop randoms"));
@@ -1091,12 +1105,19 @@ static bool mega_eligible(enx_ctx* c, uint32_t B, const StepArgs& S, MegaArgs& A
     A.final_norm = c->head.norm;
     A.S = S;
     A.tokens = c->d_step->tokens;
-    A.bar = c->d_bar;
-    A.ready = reinterpret_cast<uint32_t*>(c->d_bar + 8);
-    A.done = A.ready + 64;
-    A.x_mid = c->x_mid;
+    if (!c->d_ll) {  // tagged stage outputs, zero tags (never a live tag: epochs start at 1)
+        const size_t words = mega_ll_words(kMegaMaxTokens, C.hidden, C.kv_heads * C.head_dim, C.intermediate);
+        if (dalloc(&c->d_ll, words, "tagged stage outputs") != ENX_OK ||
+            cudaMemsetAsync(c->d_ll, 0, words * 8, c->stream) != cudaSuccess) {
+            dfree(c->d_ll);
+            return false;
+        }
+    }
+    A.ll = c->d_ll;
+    A.ll_epoch = reinterpret_cast<const uint32_t*>(c->d_bar);
     A.err = &c->d_step->err;
     A.trace = c->d_trace;
+    if (const char* tc = std::getenv("ENX_TRACE_CTA")) A.trace_cta = (uint32_t)std::atoi(tc);  // default CTA 0
     geo = mega_geometry(B, A);
     if (geo.nslots < 2 || c->max_ctx > geo.max_positions) return false;
     A.nslots = geo.nslots;
@@ -1388,19 +1409,19 @@ static enx_status capture_step(enx_ctx* c, uint32_t B, bool loop) {
     ENX_CUDA(cudaStreamBeginCapture(st, cudaStreamCaptureModeThreadLocal));
     cudaError_t e = cudaSuccess;
     if (loop) {
-        k_loop_prep<<<1, 32, 0, st>>>(c->d_loop, c->d_step, c->d_loop_rand, c->d_loop_ids, c->history, c->max_ctx, B);
+        k_loop_prep<<<1, 32, 0, st>>>(c->d_loop, c->d_step, c->d_loop_rand, c->d_loop_ids, c->history, c->max_ctx, B,
+                                      c->d_bar);
         e = cudaGetLastError();
     } else {
         e = cudaMemcpyAsync(c->d_step, c->h_step, in_bytes, cudaMemcpyHostToDevice, st);
         if (e == cudaSuccess) {
-            k_step_prep<<<1, 32, 0, st>>>(c->d_step, c->history, c->max_ctx, B);
+            k_step_prep<<<1, 32, 0, st>>>(c->d_step, c->history, c->max_ctx, B, c->d_bar);
             e = cudaGetLastError();
         }
     }
     if (e == cudaSuccess) {
         if (mega) {
-            e = cudaMemsetAsync(c->d_bar, 0, kMegaBarWords * sizeof(unsigned long long), st);
-            if (e == cudaSuccess) e = launch_mega(B, A, geo, st);
+            e = launch_mega(B, A, geo, st);  // the prep kernel above bumped the tag epoch
         } else {
             e = launch_embed(c->d_step->tokens, c->head.embed, c->head.bits, c->x, B, 0, c->cfg.vocab, c->cfg.hidden,
                              st, true);
@@ -1582,6 +1603,17 @@ extern "C" enx_status enx_logits(enx_ctx* c, uint32_t seq, float* out) {
     return ENX_OK;
 }
 
+extern "C" enx_status enx_nll(enx_ctx* c, uint32_t seq, uint32_t target, double* out) {
+    CHECK_ARG(c && out, "enx_nll: null pointer");
+    if (!c->logits || seq >= c->batch) return fail(ENX_ERR_RANGE, "enx_nll: sequence outside the cache");
+    if (target >= c->cfg.vocab) return fail(ENX_ERR_INVALID, "enx_nll: target id outside the vocabulary");
+    DeviceGuard g(c->device);
+    ENX_CUDA(launch_nll(c->logits + (size_t)seq * c->cfg.vocab, c->cfg.vocab, target, c->d_nll, c->stream));
+    ENX_CUDA(cudaMemcpyAsync(out, c->d_nll, 8, cudaMemcpyDeviceToHost, c->stream));
+    ENX_CUDA(cudaStreamSynchronize(c->stream));
+    return ENX_OK;
+}
+
 extern "C" enx_status enx_hidden(enx_ctx* c, uint32_t seq, float* out) {
     CHECK_ARG(c && out, "enx_hidden: null pointer");
     if (!c->normed || seq >= c->batch) return fail(ENX_ERR_RANGE, "enx_hidden: sequence outside the cache");
@@ -1665,7 +1697,8 @@ extern "C" enx_status enx_launch_step_kernel(enx_ctx* c, uint32_t batch, uint32_
     MegaGeometry geo{};
     if (!mega_eligible(c, batch, S, A, geo)) return fail(ENX_ERR_STATE, "enx_launch_step_kernel: not eligible");
     for (uint32_t i = 0; i < count; ++i) {
-        ENX_CUDA(cudaMemsetAsync(c->d_bar, 0, kMegaBarWords * sizeof(unsigned long long), c->stream));
+        k_bump_epoch<<<1, 32, 0, c->stream>>>(c->d_bar);
+        ENX_CUDA(cudaGetLastError());
         ENX_CUDA(launch_mega(batch, A, geo, c->stream));
     }
     return ENX_OK;

@@ -9,9 +9,16 @@ namespace enx {
 
 constexpr uint32_t kMaxLayers = 32;
 constexpr uint32_t kMegaSlots = 8;   // upper bound on ring slots
-constexpr uint32_t kMegaStages = 3;  // grid-barrier stages per layer (attention, gate/up, down)
-constexpr uint32_t kMegaTraceDetail = 8;  // extra stamps per layer inside stage A
-constexpr uint32_t kMegaBarWords = 64;    // u64 words of barrier + ready counters (zeroed per launch)
+constexpr uint32_t kMegaStages = 3;  // traced stages per layer (attention + o, gate/up, down)
+constexpr uint32_t kMegaTraceDetail = 12;  // extra stamps per layer inside stage A
+constexpr uint32_t kMegaBarWords = 64;    // u64 words of step counters (word 0: the tag epoch, then arrival counters)
+constexpr uint32_t kMegaMaxTokens = 4;    // tokens per launch the tagged buffers are sized for
+
+// 64-bit words of the tagged stage outputs for `mt` tokens: two layer-parity copies of x, q, k|v,
+// attention output, x after the o-projection and the gated activations.
+inline size_t mega_ll_words(uint32_t mt, uint32_t hidden, uint32_t kv_dim, uint32_t intermediate) {
+    return 2 * (size_t)mt * (4 * (size_t)hidden + 2 * (size_t)kv_dim + intermediate);
+}
 
 // One bulk copy of a slice: global source, size, destination offset inside the slot.
 struct MegaCopy {
@@ -53,16 +60,15 @@ struct MegaArgs {
     const float* final_norm;
     StepArgs S;                   // activations, caches, RoPE table, positions
     const uint32_t* tokens;       // [MT] ids fed this step (device)
-    unsigned long long* bar;      // grid-barrier arrival counter, zeroed before each launch
-    uint32_t* ready;              // [MT][kv_heads] q|k|v units done (monotonic over layers), zeroed too
-    uint32_t* done;               // [MT] attention heads done (monotonic over layers), zeroed too
-    float* x_mid;                 // [MT][hidden] residual after attention (x stays readable meanwhile)
-    uint32_t* err;                // sticky error: 1 barrier timeout, 2 copy timeout
+    unsigned long long* ll;       // tagged stage outputs (mega_ll_words(kMaxStepTokens, ...) words, zeroed once)
+    const uint32_t* ll_epoch;     // launch counter of the tags, bumped before each launch
+    uint32_t* err;                // sticky error: 1 activation wait timeout, 2 copy timeout
     const MegaSlice* table;       // [grid][table_stride] slices, built on the host
     const uint32_t* nslices;      // [grid] slices per CTA
     uint32_t table_stride;
     uint32_t nslots, slot_bytes, x4_floats;
-    unsigned long long* trace;    // optional: globaltimer stamps of CTA 0, 3 per stage
+    unsigned long long* trace;    // optional: globaltimer stamps of CTA trace_cta, 3 per stage
+    uint32_t trace_cta;
 };
 
 struct MegaGeometry {

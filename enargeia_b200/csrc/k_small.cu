@@ -114,4 +114,37 @@ cudaError_t launch_add(const float* a, const float* b, float* out, uint32_t n, c
     return cudaGetLastError();
 }
 
+// Negative log-likelihood of `target` under the softmax of one logits row, in double, as the
+// reference's perplexity harness computes it (test/parity/quality.test.ts:93-99): max over the
+// float logits, sum of exp(logit - max) in double, -((logit[target] - max) - log(sum)).  One
+// block; the partial sums are combined in a fixed order (deterministic).
+__global__ void k_nll(const float* __restrict__ logits, uint32_t vocab, uint32_t target, double* __restrict__ out) {
+    __shared__ float redf[32];
+    __shared__ double redd[32];
+    const uint32_t lane = threadIdx.x & 31, warp = threadIdx.x >> 5, nw = blockDim.x >> 5;
+    float m = -INFINITY;
+    for (uint32_t i = threadIdx.x; i < vocab; i += blockDim.x) m = fmaxf(m, logits[i]);
+    m = warp_max(m);
+    if (lane == 0) redf[warp] = m;
+    __syncthreads();
+    m = -INFINITY;
+    for (uint32_t w = 0; w < nw; ++w) m = fmaxf(m, redf[w]);
+    const double md = (double)m;
+    double s = 0.0;
+    for (uint32_t i = threadIdx.x; i < vocab; i += blockDim.x) s += exp((double)logits[i] - md);
+    s = warp_sum_d(s);
+    if (lane == 0) redd[warp] = s;
+    __syncthreads();
+    if (threadIdx.x == 0) {
+        double t = 0.0;
+        for (uint32_t w = 0; w < nw; ++w) t += redd[w];
+        *out = -(((double)logits[target] - md) - log(t));
+    }
+}
+
+cudaError_t launch_nll(const float* logits, uint32_t vocab, uint32_t target, double* out, cudaStream_t st) {
+    k_nll<<<1, 1024, 0, st>>>(logits, vocab, target, out);
+    return cudaGetLastError();
+}
+
 }  // namespace enx

@@ -17,6 +17,9 @@ cudaError_t launch_cache_pack(const float* src, uint16_t* dst, uint32_t count, u
 cudaError_t launch_silu_mul(const float* g, const float* u, float* out, uint32_t n, cudaStream_t st);
 cudaError_t launch_add(const float* a, const float* b, float* out, uint32_t n, cudaStream_t st);
 
+// -log softmax(logits)[target] in double (one row, one block): the perplexity harness's nll.
+cudaError_t launch_nll(const float* logits, uint32_t vocab, uint32_t target, double* out, cudaStream_t st);
+
 // Per-row sampling parameters on the device.
 struct SampleRow {
     float temperature, top_p, repetition_penalty, random;

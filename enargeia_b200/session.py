@@ -10,6 +10,7 @@ GenerateTiming fields.  All device work is libenx's; there is no CPU path.
 from __future__ import annotations
 
 import ctypes as C
+import math
 import time
 from dataclasses import dataclass, field
 from pathlib import Path
@@ -152,6 +153,12 @@ class Model:
         call("enx_logits", self._h, seq, out.ctypes.data)
         return out
 
+    def nll(self, target: int, seq: int = 0) -> float:
+        """-log softmax(current logits of `seq`)[target], computed on the device (enx_nll)."""
+        out = C.c_double()
+        call("enx_nll", self._h, seq, int(target), C.byref(out))
+        return out.value
+
     def hidden(self, seq: int = 0) -> np.ndarray:
         out = np.empty(self.config.hidden, dtype=np.float32)
         call("enx_hidden", self._h, seq, out.ctypes.data)
@@ -183,7 +190,7 @@ class Model:
         stage waited for its barrier+weights and how long it computed (kernel-group telemetry of
         src/runtime/telemetry.ts, at stage granularity)."""
         L = self.config.layers
-        n = 3 * (3 * L + 1) + 8 * L + 2
+        n = 3 * (3 * L + 1) + 12 * L + 2
         buf = np.zeros(n, dtype=np.uint64)
         cnt = C.c_uint32()
         call("enx_trace", self._h, buf.ctypes.data, n, C.byref(cnt))
@@ -201,7 +208,7 @@ class Model:
         out["total"] = t[3 * L, 2] - t[0, 0]
         # inside the attention stage (first CTA): weights + norm, q|k|v units, wait for the kv
         # head's units, q and current k/v loads, attention, wait for every head, o rows
-        d = buf[3 * (3 * L + 1):3 * (3 * L + 1) + 8 * L].astype(np.float64).reshape(L, 8) / 1e3
+        d = buf[3 * (3 * L + 1):3 * (3 * L + 1) + 12 * L].astype(np.float64).reshape(L, 12) / 1e3
         if d.any():
             marks = ["norm", "units", "ready_wait", "q_load", "attention", "done_wait", "o_rows+end"]
             d = d[:, :6]
@@ -210,7 +217,7 @@ class Model:
             seq = np.concatenate([starts[:, None], d, ends[:, None]], axis=1)
             for j, m in enumerate(marks):
                 out[f"attn.{m}"] = float(np.sum(seq[:, j + 1] - seq[:, j]))
-            full = buf[3 * (3 * L + 1):3 * (3 * L + 1) + 8 * L].astype(np.float64).reshape(L, 8)[1:] / 1e3
+            full = buf[3 * (3 * L + 1):3 * (3 * L + 1) + 12 * L].astype(np.float64).reshape(L, 12)[1:] / 1e3
             t1 = t[3:3 * L:3, 1]
             out["norm.loads"] = float(np.sum(full[:, 6] - t1))
             out["norm.rs"] = float(np.sum(full[:, 7] - full[:, 6]))
@@ -299,6 +306,23 @@ class Session:
         self.model.decode_step([token], [self.sampling], [self._draw()])
         self.tokens.append(token)
         return self.model.logits(self.seq)
+
+    def perplexity(self, tokens: Sequence[int]) -> float:
+        """exp(mean nll) of tokens[2:] given their prefixes, the reference's cached evaluation
+        (test/parity/quality.test.ts:111-139): prime with tokens[0], then for each later position
+        one decode step (logitsAfter) and the nll of the next token, read back as 8 bytes (enx_nll)
+        rather than the whole logits row.  Resets the session first."""
+        if len(tokens) < 3:
+            raise ValueError("perplexity needs at least 3 tokens")
+        self.reset()
+        self.prime(tokens[:1])
+        total, counted = 0.0, 0
+        for i in range(1, len(tokens) - 1):
+            self.model.decode_step([tokens[i]], [self.sampling], [self._draw()])
+            self.tokens.append(tokens[i])
+            total += self.model.nll(tokens[i + 1], self.seq)
+            counted += 1
+        return math.exp(total / counted)
 
     def generate(self, prompt: Sequence[int], max_tokens: int, stop_tokens: Sequence[int] = (),
                  on_token: Optional[Callable[[int, int], None]] = None,

@@ -283,6 +283,13 @@ ENX_API enx_status enx_loop_ids(enx_ctx* ctx, uint32_t* out_ids, uint32_t count)
  * place, as in the reference. */
 ENX_API enx_status enx_logits(enx_ctx* ctx, uint32_t seq, float* out);
 
+/* Negative log-likelihood of `target` under the softmax of sequence `seq`'s current logits, in
+ * double: -((logit[target] - max) - log(sum_i exp(logit[i] - max))), the per-position term of the
+ * reference's perplexity harness (test/parity/quality.test.ts:93-99, over the logits that
+ * Session.logitsAfter returns, src/runtime/session.ts:385-401).  Computed on the device, so a
+ * perplexity evaluation reads 8 bytes per position instead of the whole logits row. */
+ENX_API enx_status enx_nll(enx_ctx* ctx, uint32_t seq, uint32_t target, double* out);
+
 /* Final-norm hidden state of the last step of sequence `seq` (hidden floats, host). */
 ENX_API enx_status enx_hidden(enx_ctx* ctx, uint32_t seq, float* out);
 

@@ -610,6 +610,18 @@ int orc_decode(orc_model* M, uint32_t token, float* logits, float* final_normed)
     return 0;
 }
 
+// -log softmax(logits)[target] as the reference's perplexity harness computes it
+// (test/parity/quality.test.ts:93-99): max of the float logits, a sequential double sum of
+// exp(logit - max), then -((logit[target] - max) - log(sum)).
+double orc_nll(const float* logits, int64_t n, uint32_t target) {
+    float m = -INFINITY;
+    for (int64_t i = 0; i < n; ++i)
+        if (logits[i] > m) m = logits[i];
+    double sum = 0.0;
+    for (int64_t i = 0; i < n; ++i) sum += std::exp((double)logits[i] - (double)m);
+    return -(((double)logits[target] - (double)m) - std::log(sum));
+}
+
 // Copies of the f16 cache, for parity checks: [max_context][kv*hd] of one layer.
 void orc_model_kv(const orc_model* M, uint32_t layer, uint16_t* k_out, uint16_t* v_out) {
     int64_t per = M->max_context * (int64_t)M->cfg.kv_heads * M->cfg.head_dim;

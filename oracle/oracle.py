@@ -114,6 +114,8 @@ def _declare(L):
     L.orc_decode.restype = C.c_int
     L.orc_decode.argtypes = [P, C.c_uint32, P, P]
     L.orc_model_kv.argtypes = [P, C.c_uint32, P, P]
+    L.orc_nll.restype = C.c_double
+    L.orc_nll.argtypes = [P, I64, C.c_uint32]
 
 
 def _p(a: Optional[np.ndarray]):
@@ -253,6 +255,12 @@ def attention_f16(q, kcache_bits, vcache_bits, begin, heads, kv_heads, head_dim)
     lib().orc_attention_f16(_p(q), _p(_c(kcache_bits, np.uint16)), _p(_c(vcache_bits, np.uint16)),
                             queries, begin, heads, kv_heads, head_dim, _p(out))
     return out
+
+
+def nll(logits: np.ndarray, target: int) -> float:
+    """-log softmax(logits)[target] (the perplexity harness's per-position term)."""
+    lg = _c(logits, np.float32)
+    return float(lib().orc_nll(_p(lg), lg.size, int(target)))
 
 
 def sample(logits: np.ndarray, history: Sequence[int], temperature: float, top_p: float,

@@ -152,3 +152,26 @@ def test_small_real_head_geometry(gpu, oracle, tmp_path):
     prompt = list(np.random.default_rng(16).integers(0, SMALL.vocab, 32))
     run_pair(oracle, path, f, SMALL, prompt, 12, GREEDY, 1, ctx=128)
     run_pair(oracle, path, f, SMALL, prompt, 12, APP_SAMPLING, 9, ctx=128)
+
+
+def test_perplexity_matches_oracle(gpu, oracle, tiny_file):
+    """The cached perplexity evaluation (test/parity/quality.test.ts:111-139): prime with the
+    first token, one logitsAfter step per position, nll of the next token.  The device's nll
+    (enx_nll, 8 bytes read back per position) against the oracle's on the oracle's logits."""
+    tokens = [int(v) for v in np.random.default_rng(17).integers(0, TINY.vocab, 48)]
+    m = gpu_model(GOLDEN / "tiny_q8.enargeia", TINY, 64)
+    s = Session(m, GREEDY, seed=1)
+    ppl = s.perplexity(tokens)
+    om = oracle.OracleModel(tiny_file, TINY, 64)
+    om.prefill(tokens[:1])
+    total = 0.0
+    for i in range(1, len(tokens) - 1):
+        lg = om.decode(tokens[i])
+        total += oracle.nll(lg, tokens[i + 1])
+        # the device nll of the device logits equals the oracle formula on the same logits
+        if i == len(tokens) - 2:
+            dl = m.logits()
+            assert abs(m.nll(tokens[i + 1]) - oracle.nll(dl, tokens[i + 1])) <= 1e-12 * abs(oracle.nll(dl, tokens[i + 1])) + 1e-12
+    want = np.exp(total / (len(tokens) - 2))
+    assert abs(ppl - want) <= 1e-6 * want, (ppl, want)
+    m.close()

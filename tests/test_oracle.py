@@ -196,3 +196,17 @@ def test_sampler_fallback_and_draw_order(oracle):
         logits = np.zeros(V, np.float32)
         tok = oracle.sample(logits, [], 1.0, 1.0, 1.0, r)
         assert tok == min(int(np.ceil(r * V)) - 1 if r > 0 else 0, V - 1) or tok == int(r * V)
+
+
+def test_nll_matches_the_harness_formula(oracle):
+    """-log softmax[target] of test/parity/quality.test.ts:93-99 (max of the floats, double sum)."""
+    rng = np.random.default_rng(31)
+    for scale in (0.5, 3.0, 30.0):
+        lg = (rng.standard_normal(5000) * scale).astype(np.float32)
+        t = int(rng.integers(0, lg.size))
+        m = float(lg.max())
+        s = 0.0
+        for v in lg.astype(np.float64):
+            s += np.exp(v - m)
+        want = -((float(lg[t]) - m) - np.log(s))
+        assert abs(oracle.nll(lg, t) - want) <= 1e-12 * abs(want) + 1e-12
