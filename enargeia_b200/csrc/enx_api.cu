@@ -161,6 +161,20 @@ extern "C" enx_status enx_lm_head_q8(const float* x, const uint32_t* packed, con
                                 as_stream(stream)));
         return ENX_OK;
     }
+    if (d->seq <= 4 && d->hidden <= 1024) {  // decode rows: the tensor-core head (exact limbs)
+        uint8_t* ws = nullptr;
+        uint32_t* err = nullptr;
+        ENX_TRY(tc_workspace(0, &ws, &err));
+        HeadTcArgs h{};
+        h.x = x;
+        h.w = w;
+        h.out = out + d->out_offset;
+        h.out_stride = stride;
+        h.ntok = d->seq;
+        h.err = err;
+        ENX_CUDA(launch_head_tc(h, as_stream(stream), false));
+        return ENX_OK;
+    }
     ENX_CUDA(launch_matmul(8, x, w, nullptr, out, d->seq, stride, d->out_offset, as_stream(stream), false));
     return ENX_OK;
 }
@@ -466,8 +480,6 @@ struct enx_ctx {
     MegaSlice* d_table[kMaxStepBatch + 1] = {};
     uint32_t* d_nslices[kMaxStepBatch + 1] = {};
     uint32_t table_stride[kMaxStepBatch + 1] = {};
-    uint8_t* d_head_slices = nullptr;
-    QW head_slices{};
     uint32_t last_launches = 0;
     // prefill buffers (chunk-sized)
     uint32_t pf_chunk = 0;
@@ -548,7 +560,6 @@ void free_graphs(enx_ctx* c) {
         dfree(c->d_nslices[b]);
         c->table_stride[b] = 0;
     }
-    dfree(c->d_head_slices);
 }
 
 void free_prefill(enx_ctx* c) {
@@ -1123,20 +1134,11 @@ static bool mega_eligible(enx_ctx* c, uint32_t B, const StepArgs& S, MegaArgs& A
     A.nslots = geo.nslots;
     A.slot_bytes = geo.slot_bytes;
     A.x4_floats = geo.x4_floats;
-    if (!c->d_head_slices) {  // slice-major copy of the tied head (built once)
-        const size_t hb = mega_head_slices_bytes(C.vocab, C.hidden, c->head.bits);
-        if (dalloc(&c->d_head_slices, hb, "head by slices") != ENX_OK ||
-            mega_head_slices(c->head.embed, c->head.bits, c->d_head_slices, &c->head_slices, c->stream) != cudaSuccess ||
-            cudaStreamSynchronize(c->stream) != cudaSuccess) {
-            dfree(c->d_head_slices);
-            return false;
-        }
-    }
     if (!c->d_table[B]) {
         std::vector<MegaSlice> table;
         std::vector<uint32_t> counts;
         uint32_t stride = 0;
-        mega_build_table(B, A, c->head_slices, geo, table, counts, stride);
+        mega_build_table(B, A, geo, table, counts, stride);
         if (dalloc(&c->d_table[B], table.size(), "mega table") != ENX_OK ||
             dalloc(&c->d_nslices[B], counts.size(), "mega counts") != ENX_OK ||
             cudaMemcpy(c->d_table[B], table.data(), table.size() * sizeof(MegaSlice), cudaMemcpyHostToDevice) != cudaSuccess ||
@@ -1397,6 +1399,26 @@ static enx_status decode_batch_loop(enx_ctx* c, uint32_t B, const uint32_t* firs
     return ENX_OK;
 }
 
+// The final RMSNorm and the tied head of a persistent step (after k_mega, which leaves the last
+// layer's x in S.x): the tensor-core head for an int8 table (its weight stream starts while k_mega
+// drains), the CUDA-core head kernel otherwise.
+static cudaError_t launch_step_head(enx_ctx* c, uint32_t B, const StepArgs& S, cudaStream_t st) {
+    if (c->head.bits == 8) {
+        HeadTcArgs h{};
+        h.x = c->x;
+        h.gain = c->head.norm;
+        h.eps = c->cfg.rms_norm_eps;
+        h.normed_out = c->normed;
+        h.w = c->head.embed;
+        h.out = c->logits;
+        h.out_stride = c->cfg.vocab;
+        h.ntok = B;
+        h.err = &c->d_step->err;
+        return launch_head_tc(h, st, true);
+    }
+    return launch_head(B, c->head.bits, c->head, S, st);
+}
+
 static enx_status capture_step(enx_ctx* c, uint32_t B, bool loop) {
     cudaStream_t st = c->stream;
     StepArgs S = step_args(c);
@@ -1422,6 +1444,7 @@ static enx_status capture_step(enx_ctx* c, uint32_t B, bool loop) {
     if (e == cudaSuccess) {
         if (mega) {
             e = launch_mega(B, A, geo, st);  // the prep kernel above bumped the tag epoch
+            if (e == cudaSuccess) e = launch_step_head(c, B, S, st);
         } else {
             e = launch_embed(c->d_step->tokens, c->head.embed, c->head.bits, c->x, B, 0, c->cfg.vocab, c->cfg.hidden,
                              st, true);

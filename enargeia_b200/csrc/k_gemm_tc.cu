@@ -563,4 +563,349 @@ cudaError_t launch_gemm_tc(int bits, const float* x, uint32_t ld, const QW& w, c
     return cudaGetLastError();
 }
 
+// ---------------------------------------------------------------------------------------------
+// The tied int8 head for a few tokens (decode): logits[t][row] = x_t . W[row] over every row.
+//
+// Same exact-limb arithmetic as k_gemm_tc, shaped for 1-4 tokens: the weight rows are the MMA's
+// M (128 per tile) and the activation limbs its N (6 limbs x NT tokens, padded to 16 or 32), so
+// the tensor pipe does 16 (or 32) columns of work per weight byte and the kernel streams the
+// table instead of spending a DFMA per weight.  Each 64-column block of a tile accumulates into
+// its own TMEM columns (the per-block scale is applied in the epilogue), so a tile of 128 rows x
+// 14 blocks holds 14 x N columns; tiles alternate between two accumulators.
+//
+// Persistent: one CTA per SM walks row tiles blockIdx.x, + gridDim.x, ...  Warp 0 streams the
+// codes with TMA (they do not depend on the previous kernel, so with programmatic dependent launch
+// the weight stream starts while that kernel drains); warps 1-9 then build the limb tile of the
+// activations in shared memory (optionally normalised here with the final-norm gain); warp 1
+// issues the MMAs; warps 2-9 (two per TMEM lane quadrant, a thread per row and half of the blocks)
+// join limbs, take off z * sum(X), scale per block in double, and add the two halves in order.
+constexpr uint32_t kHtStages = 20;      // 8 KB code boxes in flight (160 KB)
+constexpr uint32_t kHtEpiWarps = 8;     // two per TMEM lane quadrant (block halves)
+constexpr uint32_t kHtThreads = 32 * (2 + kHtEpiWarps);
+constexpr uint32_t kHtMaxBlocks = 16;   // K <= 1024
+
+template <int NT>  // token capacity: 2 (N = 16) or 4 (N = 32)
+__global__ void __launch_bounds__(kHtThreads, 1) k_head_tc(const __grid_constant__ CUtensorMap cmap, const HeadTcArgs a) {
+    constexpr uint32_t N = NT <= 2 ? 16 : 32;
+    extern __shared__ __align__(1024) uint8_t smem[];
+    uint8_t* sA = smem;                                 // [stages][8 KB] code boxes
+    uint8_t* sB = smem + kHtStages * kTcATile;          // [blocks][N x 64] limb tiles (canonical)
+    __shared__ __align__(8) uint64_t full[kHtStages], empty[kHtStages], accf[2], acce[2];
+    __shared__ long long xsumb[kHtMaxBlocks][NT];      // per block and token: sum of X
+    __shared__ double scal[NT];                         // per token: 2^-F
+    __shared__ float xs[NT][1024];
+    __shared__ double red[NT][kHtThreads / 32];
+    __shared__ float amaxs[NT][kHtThreads / 32];
+    __shared__ double hsum[2 * 2 * kTcRows * NT];       // [tile parity][half][row][token] partial sums
+    __shared__ uint32_t tmem_base;
+    __shared__ volatile int s_fail;
+
+    const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+    const uint32_t K = a.w.cols, nb = K / kBlock, rows = a.w.rows;
+    const uint32_t ntiles = (rows + kTcRows - 1) / kTcRows;
+    const uint32_t cols_per_tile = nb * N;
+    const uint32_t nacc = 2 * cols_per_tile <= 512 ? 2 : 1;
+    const uint32_t spin = g_tc_spin;
+
+    if (warp == 1) {
+        asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(su32(&tmem_base)), "r"(512));
+        asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;");
+    }
+    if (tid == 0) {
+        s_fail = 0;
+        for (uint32_t i = 0; i < kHtStages; ++i) {
+            asm volatile("mbarrier.init.shared::cta.b64 [%0], 1;" ::"r"(su32(&full[i])));
+            asm volatile("mbarrier.init.shared::cta.b64 [%0], 1;" ::"r"(su32(&empty[i])));
+        }
+        for (int i = 0; i < 2; ++i) {
+            asm volatile("mbarrier.init.shared::cta.b64 [%0], 1;" ::"r"(su32(&accf[i])));
+            asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(su32(&acce[i])), "r"(kHtEpiWarps));
+        }
+        asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+    }
+    asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
+    __syncthreads();
+    asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+    const uint32_t tmem = tmem_base;
+
+    if (warp == 0) {
+        // ---- producer: a TMA box of 128 rows x 64 code bytes per (tile, block) -------------------
+        if (lane == 0) {
+            uint32_t issued = 0;
+            for (uint32_t tile = blockIdx.x; tile < ntiles && !s_fail; tile += gridDim.x)
+                for (uint32_t b = 0; b < nb; ++b, ++issued) {
+                    const uint32_t s = issued % kHtStages;
+                    if (issued >= kHtStages && !mbar_wait_f(&empty[s], ((issued / kHtStages) - 1) & 1, &s_fail, a.err, spin))
+                        goto produced;
+                    asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(su32(&full[s])), "r"(kTcATile)
+                                 : "memory");
+                    tma_codes(sA + s * kTcATile, &cmap, b, tile * kTcRows, &full[s]);
+                }
+        produced:
+            // no copy may still be landing when the CTA releases its shared memory (error path)
+            for (uint32_t i = issued > kHtStages ? issued - kHtStages : 0; i < issued; ++i)
+                mbar_drain(&full[i % kHtStages], (i / kHtStages) & 1);
+        }
+        __syncwarp();
+    } else {
+        // ---- warps 1-9: the activation limbs (after the previous kernel's results are visible) ---
+        pdl_wait();
+        const uint32_t t5 = tid - 32, n5 = kHtThreads - 32, w5 = t5 >> 5;
+        auto bar5 = [&]() { asm volatile("bar.sync 1, %0;" ::"n"(kHtThreads - 32) : "memory"); };
+        for (uint32_t i = t5; i < NT * K; i += n5) {
+            const uint32_t t = i / K, k = i % K;
+            xs[t][k] = t < a.ntok ? a.x[(size_t)t * K + k] : 0.f;
+        }
+        bar5();
+        if (a.gain) {  // the final RMSNorm (test/reference/ops.ts:30-51), one rounding per value
+            double ss[NT];
+#pragma unroll
+            for (int t = 0; t < NT; ++t) ss[t] = 0.0;
+            for (uint32_t k = t5; k < K; k += n5)
+#pragma unroll
+                for (int t = 0; t < NT; ++t) ss[t] = fma((double)xs[t][k], (double)xs[t][k], ss[t]);
+#pragma unroll
+            for (int t = 0; t < NT; ++t) {
+                const double v = warp_sum_d(ss[t]);
+                if (lane == 0) red[t][w5] = v;
+            }
+            bar5();
+            double rs[NT];
+#pragma unroll
+            for (int t = 0; t < NT; ++t) {
+                double tot = 0.0;
+                for (uint32_t w = 0; w < n5 / 32; ++w) tot += red[t][w];
+                rs[t] = 1.0 / sqrt(tot / (double)K + (double)a.eps);
+            }
+            bar5();
+            for (uint32_t i = t5; i < NT * K; i += n5) {
+                const uint32_t t = i / K, k = i % K;
+                const float v = norm_value(xs[t][k], rs[t], a.gain[k]);
+                xs[t][k] = v;
+                if (blockIdx.x == 0 && a.normed_out && t < a.ntok) a.normed_out[(size_t)t * K + k] = v;
+            }
+            bar5();
+        }
+        // F per token from its largest |x|: X = rint(x 2^F) has |X| < 2^46 (exact unless an element
+        // is 2^-22 below the largest, as in k_limbs)
+        {
+            float m[NT];
+#pragma unroll
+            for (int t = 0; t < NT; ++t) m[t] = 0.f;
+            for (uint32_t k = t5; k < K; k += n5)
+#pragma unroll
+                for (int t = 0; t < NT; ++t) m[t] = fmaxf(m[t], fabsf(xs[t][k]));
+#pragma unroll
+            for (int t = 0; t < NT; ++t) {
+                const float v = warp_max(m[t]);
+                if (lane == 0) amaxs[t][w5] = v;
+            }
+        }
+        for (uint32_t i = t5; i < N * K / 4; i += n5) reinterpret_cast<uint32_t*>(sB)[i] = 0u;  // padding rows stay 0
+        bar5();
+        auto up_of = [&](uint32_t t) {
+            float am = 0.f;
+            for (uint32_t w = 0; w < n5 / 32; ++w) am = fmaxf(am, amaxs[t][w]);
+            const int e = am == 0.f ? 0 : (int)((__float_as_uint(am) >> 23) & 0xFF) - 126;
+            return 46 - e;  // F
+        };
+        // limb bytes: a thread per (token, element); balanced base-256 digits as in k_limbs
+        for (uint32_t i = t5; i < NT * K; i += n5) {
+            const uint32_t t = i / K, k = i % K, b = k / kBlock, j = k % kBlock;
+            const int F = up_of(t);
+            const long long X = __double2ll_rn((double)xs[t][k] * __hiloint2double((1023 + F) << 20, 0));
+            const unsigned long long u = (unsigned long long)(X + 0x808080808080LL);
+            uint8_t* tb = sB + b * (N * 64);
+#pragma unroll
+            for (uint32_t l = 0; l < kTcLimbs; ++l) tb[canon(l * NT + t, j)] = (uint8_t)(((u >> (8 * l)) & 0xFF) - 128u);
+            if (k == 0) scal[t] = __hiloint2double((1023 - F) << 20, 0);
+        }
+        // block sums of X: a warp per (block, token), fixed shuffle order
+        for (uint32_t bt = w5; bt < nb * NT; bt += n5 / 32) {
+            const uint32_t b = bt / NT, t = bt % NT;
+            const double up = __hiloint2double((1023 + up_of(t)) << 20, 0);
+            long long sx = __double2ll_rn((double)xs[t][b * kBlock + lane] * up) +
+                           __double2ll_rn((double)xs[t][b * kBlock + 32 + lane] * up);
+#pragma unroll
+            for (int o = 16; o > 0; o >>= 1) sx += __shfl_xor_sync(0xffffffffu, sx, o);
+            if (lane == 0) xsumb[b][t] = sx;
+        }
+        asm volatile("fence.proxy.async.shared::cta;" ::: "memory");  // limb bytes visible to the MMA
+        bar5();
+
+        if (warp == 1) {
+            // ---- MMA issue: one thread --------------------------------------------------------
+            if (lane == 0) {
+                uint32_t consumed = 0, t_i = 0, last = 0xFFFFFFFFu;
+                const uint32_t id = (2u << 4) | (1u << 10) | ((N >> 3) << 17) | ((kTcRows >> 4) << 24);
+                for (uint32_t tile = blockIdx.x; tile < ntiles && !s_fail; tile += gridDim.x, ++t_i) {
+                    const uint32_t acc = t_i % nacc;
+                    if (t_i >= nacc && !mbar_wait_f(&acce[acc], ((t_i / nacc) - 1) & 1, &s_fail, a.err, spin)) break;
+                    asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+                    bool ok = true;
+                    for (uint32_t b = 0; b < nb; ++b, ++consumed) {
+                        const uint32_t s = consumed % kHtStages;
+                        if (!mbar_wait_f(&full[s], (consumed / kHtStages) & 1, &s_fail, a.err, spin)) {
+                            ok = false;
+                            break;
+                        }
+                        asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+                        const uint32_t dcol = tmem + acc * cols_per_tile + b * N;
+#pragma unroll
+                        for (uint32_t kk = 0; kk < 2; ++kk) {
+                            const uint64_t ad = mdesc_a(su32(sA + s * kTcATile) + kk * 32);
+                            const uint64_t bd = mdesc(su32(sB + b * (N * 64)) + kk * 256);
+                            asm volatile("{\n .reg .pred p;\n setp.ne.b32 p, %4, 0;\n tcgen05.mma.cta_group::1.kind::i8 [%0], %1, %2, %3, p;\n}\n" ::"r"(
+                                             dcol),
+                                         "l"(ad), "l"(bd), "r"(id), "r"(kk));
+                        }
+                        asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(
+                                         su32(&empty[s]))
+                                     : "memory");
+                    }
+                    // (also after a failed wait: the drain below then covers the MMAs issued so far)
+                    asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(
+                                     su32(&accf[acc]))
+                                 : "memory");
+                    last = t_i;
+                    if (!ok) break;
+                }
+                // every issued MMA complete before TMEM is freed
+                if (last != 0xFFFFFFFFu) mbar_drain(&accf[last % nacc], (last / nacc) & 1);
+            }
+            __syncwarp();
+        } else {
+            // ---- epilogue: warps 2-9, thread = row 32 (warp % 4) + lane of the tile; warps 2-5 take
+            // the first half of the blocks, warps 6-9 the second; the halves meet in shared memory
+            const uint32_t quad = warp & 3, erow = 32 * quad + lane, half = (warp - 2) >> 2;
+            const uint32_t hb = (nb + 1) / 2, b0 = half * hb, b1 = min(nb, b0 + hb);
+            uint32_t t_i = 0;
+            for (uint32_t tile = blockIdx.x; tile < ntiles; tile += gridDim.x, ++t_i) {
+                const uint32_t acc = t_i % nacc, row = tile * kTcRows + erow;
+                const bool live = row < rows;
+                // this row's scales and zero points of the half, in flight while the tile's MMAs run
+                // (zero points are bytes of the packed words, little-endian: byte row * nb + b)
+                float sreg[kHtMaxBlocks / 2];
+                uint32_t zreg[kHtMaxBlocks / 2];
+                const uint8_t* zb = reinterpret_cast<const uint8_t*>(a.w.zeros) + (size_t)row * nb;
+#pragma unroll
+                for (uint32_t bb = 0; bb < kHtMaxBlocks / 2; ++bb) {
+                    const bool use = live && b0 + bb < b1;
+                    sreg[bb] = use ? __ldg(a.w.scales + (size_t)row * nb + b0 + bb) : 0.f;
+                    zreg[bb] = use ? (uint32_t)__ldg(zb + b0 + bb) : 0u;
+                }
+                int ok = 1;
+                if (lane == 0) ok = mbar_wait_f(&accf[acc], (t_i / nacc) & 1, &s_fail, a.err, spin);
+                if (!__shfl_sync(0xffffffffu, ok, 0)) break;
+                asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+                double sum[NT];
+#pragma unroll
+                for (int t = 0; t < NT; ++t) sum[t] = 0.0;
+                // one block's limb columns -> sum[t] += s * (sum_l d_l 256^l - z * sum(X))
+                auto fold = [&](const uint32_t* d, uint32_t bb) {
+                    const double sc = (double)sreg[bb];
+                    const long long zc = (long long)zreg[bb];
+#pragma unroll
+                    for (int t = 0; t < NT; ++t) {
+                        // exact: each pair d_l + 256 d_(l+1) fits 32 bits
+                        const long long a0 = (long long)((int)d[0 * NT + t] + (int)d[1 * NT + t] * 256);
+                        const long long a1 = (long long)((int)d[2 * NT + t] + (int)d[3 * NT + t] * 256);
+                        const long long a2 = (long long)((int)d[4 * NT + t] + (int)d[5 * NT + t] * 256);
+                        const long long T = a0 + a1 * 65536LL + a2 * 4294967296LL - zc * xsumb[b0 + bb][t];
+                        sum[t] = fma((double)T, sc, sum[t]);
+                    }
+                };
+                auto ld16 = [&](uint32_t* d, uint32_t ta) {
+                    asm volatile("tcgen05.ld.sync.aligned.32x32b.x16.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15}, [%16];"
+                                 : "=r"(d[0]), "=r"(d[1]), "=r"(d[2]), "=r"(d[3]), "=r"(d[4]), "=r"(d[5]), "=r"(d[6]),
+                                   "=r"(d[7]), "=r"(d[8]), "=r"(d[9]), "=r"(d[10]), "=r"(d[11]), "=r"(d[12]), "=r"(d[13]),
+                                   "=r"(d[14]), "=r"(d[15])
+                                 : "r"(ta));
+                };
+                const uint32_t tbase = tmem + (quad * 32u << 16) + acc * cols_per_tile;
+                if constexpr (N == 16) {  // two blocks per wait
+#pragma unroll
+                    for (uint32_t bb = 0; bb < kHtMaxBlocks / 2; bb += 2) {
+                        if (b0 + bb >= b1) break;
+                        uint32_t d0[16], d1[16];
+                        ld16(d0, tbase + (b0 + bb) * N);
+                        if (b0 + bb + 1 < b1) ld16(d1, tbase + (b0 + bb + 1) * N);
+                        asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+                        fold(d0, bb);
+                        if (b0 + bb + 1 < b1) fold(d1, bb + 1);
+                    }
+                } else {
+#pragma unroll
+                    for (uint32_t bb = 0; bb < kHtMaxBlocks / 2; ++bb) {
+                        if (b0 + bb >= b1) break;
+                        uint32_t d[32];
+                        ld16(d, tbase + (b0 + bb) * N);
+                        ld16(d + 16, tbase + (b0 + bb) * N + 16);
+                        asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+                        fold(d, bb);
+                    }
+                }
+                asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
+                __syncwarp();
+                if (lane == 0) asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(su32(&acce[acc])) : "memory");
+                double* hs = hsum + (size_t)(t_i & 1) * 2 * kTcRows * NT;
+#pragma unroll
+                for (int t = 0; t < NT; ++t) hs[(half * kTcRows + erow) * NT + t] = sum[t];
+                asm volatile("bar.sync 2, %0;" ::"n"(kHtEpiWarps * 32) : "memory");
+                if (half == 0 && live)
+#pragma unroll
+                    for (int t = 0; t < NT; ++t)
+                        if ((uint32_t)t < a.ntok)
+                            a.out[(size_t)t * a.out_stride + row] =
+                                (float)((hs[erow * NT + t] + hs[(kTcRows + erow) * NT + t]) * scal[t]);
+            }
+        }
+    }
+    asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
+    __syncthreads();
+    asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+    if (warp == 1) asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(512));
+}
+
+cudaError_t launch_head_tc(const HeadTcArgs& args, cudaStream_t st, bool pdl) {
+    const uint32_t nb = args.w.cols / kBlock, N = args.ntok <= 2 ? 16u : 32u;
+    if (args.ntok == 0 || args.ntok > 4 || args.w.cols % kBlock || nb > kHtMaxBlocks || nb * N > 512)
+        return cudaErrorInvalidValue;
+    CUtensorMap cmap;
+    {
+        const cuuint64_t dims[2] = {args.w.cols, args.w.rows};
+        const cuuint64_t strides[1] = {args.w.cols};
+        const cuuint32_t box[2] = {64, kTcRows};
+        const cuuint32_t estr[2] = {1, 1};
+        const EncodeTiledFn encode = encode_tiled();
+        if (!encode) return cudaErrorNotSupported;
+        const CUresult r = encode(&cmap, CU_TENSOR_MAP_DATA_TYPE_UINT8, 2, (void*)args.w.packed, dims, strides, box, estr,
+                                  CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_64B,
+                                  CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+        if (r != CUDA_SUCCESS) return cudaErrorInvalidValue;
+    }
+    const uint32_t ntiles = (args.w.rows + kTcRows - 1) / kTcRows;
+    const uint32_t sms = (uint32_t)num_sms();
+    const size_t smem = (size_t)kHtStages * kTcATile + (size_t)nb * N * 64;
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(ntiles < sms ? ntiles : sms);
+    cfg.blockDim = dim3(kHtThreads);
+    cfg.dynamicSmemBytes = smem;
+    cfg.stream = st;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = pdl ? 1 : 0;
+    cudaError_t e;
+    if (args.ntok <= 2) {
+        e = cudaFuncSetAttribute(k_head_tc<2>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+        if (e == cudaSuccess) e = cudaLaunchKernelEx(&cfg, k_head_tc<2>, cmap, args);
+    } else {
+        e = cudaFuncSetAttribute(k_head_tc<4>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+        if (e == cudaSuccess) e = cudaLaunchKernelEx(&cfg, k_head_tc<4>, cmap, args);
+    }
+    return e == cudaSuccess ? cudaGetLastError() : e;
+}
+
 }  // namespace enx

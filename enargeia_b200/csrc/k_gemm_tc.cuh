@@ -29,6 +29,24 @@ cudaError_t launch_gemm_tc(int bits, const float* x, uint32_t ld, const QW& w, c
                            float* out, uint32_t m, uint32_t out_stride, uint32_t out_offset, uint8_t* workspace,
                            uint32_t* err, cudaStream_t st, bool limbs_ready = false);
 
+// The tied int8 head for 1-4 tokens on the tensor cores (exact limbs, like launch_gemm_tc):
+// out[t * out_stride + row] = float(x_t . W[row]) for row < w.rows, t < ntok; with `gain`, x is
+// first RMS-normalised in the kernel (and CTA 0 writes the normalised rows to normed_out).
+// w.cols <= 1024, a multiple of 64.  pdl: launched as a programmatic dependent of the previous
+// kernel (the weight stream starts before it finishes).  *err is raised to 3 if a bounded wait
+// gives up.
+struct HeadTcArgs {
+    const float* x;                 // [ntok][K] activations
+    const float* gain;              // final-norm gain: RMSNorm x here first; null: x is normalised
+    float eps;
+    float* normed_out;              // with gain: CTA 0 writes the normalised rows here (may be null)
+    QW w;                           // int8 table (rows of this call)
+    float* out;
+    uint32_t out_stride, ntok;
+    uint32_t* err;
+};
+cudaError_t launch_head_tc(const HeadTcArgs& args, cudaStream_t st, bool pdl);
+
 // Spins a bounded wait of the tensor-core GEMM takes before it gives up (current device; 0 = the
 // default 2^24).
 cudaError_t tc_set_spin(uint32_t spins);

@@ -18,8 +18,8 @@
 //   O  every CTA: reads the attention output -> its rows of the o-projection + residual (x_mid)
 //   C  every CTA: reads x_mid -> RMSNorm -> its gate|up rows -> SiLU(gate)*up (gated)
 //   D  every CTA: reads gated -> its down-projection rows + residual (x)
-// then the final RMSNorm and this CTA's slice of the tied head rows, streamed in chunks.  Norm
-// gains and q|k|v biases travel in the slices with the weights.
+// The final RMSNorm and the tied head follow in a separate kernel (launch_head_tc).  Norm gains
+// and q|k|v biases travel in the slices with the weights.
 // Arithmetic is the faithful double-sum, float-store scheme of k_matvec.cuh.
 //
 // Every wait is bounded and reports through `err` instead of hanging; the producer waits for its
@@ -897,6 +897,7 @@ __global__ void __launch_bounds__(kMThreads, 1) k_mega(const __grid_constant__ M
                     for (uint32_t p = 0; p < parts; ++p) v += res[(i * parts + p) * MT + t];  // fixed order
                     const float xn = xs[(size_t)t * H + Rr.r0 + i] + (float)v;
                     ll_store(V.x(l) + (size_t)t * H + Rr.r0 + i, __float_as_uint(xn), tag);
+                    if (l + 1 == A.layers) A.S.x[(size_t)t * H + Rr.r0 + i] = xn;  // for the head kernel
                 }
             }
         }
@@ -904,95 +905,10 @@ __global__ void __launch_bounds__(kMThreads, 1) k_mega(const __grid_constant__ M
         stamp(A, 3 * (kMegaStages * l + 2) + 2);
     }
 
-    // ---------------- final RMSNorm + tied head ---------------------------------------------
+    // the final RMSNorm and the tied head run in the next kernel (the tensor-core head, or the
+    // CUDA-core head for an int4 table), which reads the last layer's x from S.x
     stamp(A, 3 * (kMegaStages * A.layers));
-    const uint32_t nchunk = H / Geom<HB>::E;
-    {  // the last layer's x, every row
-        const bool ok = ll_read(V.x(A.layers - 1), MT * H, ll_tag(epoch, A.layers - 1), spin, A.err,
-                                [&](uint32_t i, uint32_t v) { xs[i] = __uint_as_float(v); });
-        if (!ll_done(ok)) BAIL();
-    }
-    bool first = true;
-    unsigned long long tw = 0, tc = 0, tmark = 0;  // CTA 0 thread 0: time waiting / computing (trace)
-    auto now = []() { unsigned long long t; asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t)); return t; };
-    if (A.trace && c == A.trace_cta && tid == 0) tmark = now();
-    while (slice < total) {
-        if (!wait_slice()) BAIL();
-        if (A.trace && c == A.trace_cta && tid == 0) { const unsigned long long t = now(); tw += t - tmark; tmark = t; }
-        const MegaSlice& D = sdesc[slice % NS];
-        const uint8_t* slot = slot_ptr();
-        if (first) {  // the first head slice carries the final-norm gain
-            const float* gain = reinterpret_cast<const float*>(slot + D.off_v);
-            load_norm<HB, MT>(Xd, xsum, xs, true, H, gain, A.eps, rs, red);
-            if (c == 0)
-                for (uint32_t i = tid; i < MT * H; i += kMConsumers) A.S.normed[i] = norm_value(xs[i], rs[i / H], gain[i % H]);
-            first = false;
-        }
-        if (D.nrange) {
-            // a lane per row of the 32-row slice ([chunk][row] codes), the chunks split over the
-            // warps (every lane of a warp on the same activation chunk: broadcast reads), the
-            // warps' partial sums added in a fixed order
-            constexpr int CPB = Geom<HB>::CPB;
-            const MegaRange& Rr = D.range[0];
-            const uint32_t nr = Rr.r1 - Rr.r0;
-            const uint32_t k0 = nchunk * warp / kMWarps, k1 = nchunk * (warp + 1) / kMWarps;
-            double* hpart = reinterpret_cast<double*>(kst);  // [32 rows][17 (16 warps + pad)][MT]
-            if ((uint32_t)lane < nr) {
-                const uint4* P = reinterpret_cast<const uint4*>(slot + Rr.off_p);
-                const float* sc = reinterpret_cast<const float*>(slot + Rr.off_s);
-                const uint8_t* zb = slot + Rr.off_z;
-                double acc[1][MT];
-#pragma unroll
-                for (int t = 0; t < MT; ++t) acc[0][t] = 0.0;
-                for (uint32_t cc = k0; cc < k1; ++cc) {
-                    const uint4 q[1] = {P[cc * kHeadSlice + lane]};
-                    const uint32_t b = cc / CPB;
-                    const float s[1] = {sc[b * kHeadSlice + lane]};
-                    const uint32_t zc[1] = {zb[b * kHeadSlice + lane]};
-                    chunk_dot_b<HB, MT, 1>(q, s, zc, XD, xsum, nchunk, cc, acc);
-                }
-#pragma unroll
-                for (int t = 0; t < MT; ++t) hpart[(lane * 17 + warp) * MT + t] = acc[0][t];
-            }
-            cbar();
-            // 16 partials per row: thread (row i = tid / 16, warp part w = tid % 16), a 16-lane tree
-            {
-                const uint32_t i = tid >> 4, w = tid & 15;
-#pragma unroll
-                for (int t = 0; t < MT; ++t) {
-                    double v = i < nr ? hpart[(i * 17 + w) * MT + t] : 0.0;
-                    v += __shfl_xor_sync(0xffffffffu, v, 8);
-                    v += __shfl_xor_sync(0xffffffffu, v, 4);
-                    v += __shfl_xor_sync(0xffffffffu, v, 2);
-                    v += __shfl_xor_sync(0xffffffffu, v, 1);
-                    if (w == 0 && i < nr) A.S.logits[(size_t)t * A.vocab + Rr.r0 + i] = (float)v;
-                }
-            }
-        }
-        release_slice();
-        if (A.trace && c == A.trace_cta && tid == 0) { const unsigned long long t = now(); tc += t - tmark; tmark = t; }
-    }
-    if (A.trace && c == A.trace_cta && tid == 0) {
-        A.trace[3 * (kMegaStages * A.layers + 1) + kADetail * A.layers] = tw;
-        A.trace[3 * (kMegaStages * A.layers + 1) + kADetail * A.layers + 1] = tc;
-    }
     stamp(A, 3 * (kMegaStages * A.layers) + 2);
-}
-
-// Slice-major copy of the tied head (see mega_head_slices): a thread per (slice, chunk, row).
-__global__ void k_head_slices(QW head, int bits, uint32_t nslices, uint4* P, float* S, uint8_t* Z) {
-    const uint32_t H = head.cols, nchunk = H * bits / 128, bpr = H / kBlock;
-    const size_t idx = (size_t)blockIdx.x * blockDim.x + threadIdx.x;
-    if (idx >= (size_t)nslices * nchunk * kHeadSlice) return;
-    const uint32_t i = idx % kHeadSlice, cch = (idx / kHeadSlice) % nchunk, s = (uint32_t)(idx / ((size_t)kHeadSlice * nchunk));
-    const uint32_t row = s * kHeadSlice + i;
-    const bool live = row < head.rows;
-    P[idx] = live ? reinterpret_cast<const uint4*>(head.packed)[(size_t)row * nchunk + cch] : make_uint4(0, 0, 0, 0);
-    if (cch < bpr) {  // the block-th thread of the row also moves its scale and zero-point
-        const size_t o = ((size_t)s * bpr + cch) * kHeadSlice + i, blk = (size_t)row * bpr + cch;
-        S[o] = live ? head.scales[blk] : 0.f;
-        Z[o] = live ? (uint8_t)(bits == 4 ? zero_code<4>(head.zeros, (uint32_t)blk) : zero_code<8>(head.zeros, (uint32_t)blk)) : 0;
-    }
 }
 
 // ---------------------------------------------------------------------------------------------
@@ -1004,23 +920,6 @@ static uint32_t split_lo(uint32_t total, uint32_t parts, uint32_t i, uint32_t gr
 }
 
 static size_t align256(size_t v) { return (v + 255) & ~size_t(255); }
-
-size_t mega_head_slices_bytes(uint32_t vocab, uint32_t hidden, int bits) {
-    const size_t ns = (vocab + kHeadSlice - 1) / kHeadSlice, rows = ns * kHeadSlice;
-    return align256(rows * hidden * bits / 8) + align256(rows * (hidden / kBlock) * 4) + align256(rows * (hidden / kBlock));
-}
-
-cudaError_t mega_head_slices(const QW& head, int bits, uint8_t* out, QW* view, cudaStream_t st) {
-    const uint32_t ns = (head.rows + kHeadSlice - 1) / kHeadSlice, rows = ns * kHeadSlice;
-    const uint32_t nchunk = head.cols * bits / 128, bpr = head.cols / kBlock;
-    uint4* P = reinterpret_cast<uint4*>(out);
-    float* S = reinterpret_cast<float*>(out + align256((size_t)rows * head.cols * bits / 8));
-    uint8_t* Z = out + align256((size_t)rows * head.cols * bits / 8) + align256((size_t)rows * bpr * 4);
-    const size_t n = (size_t)ns * nchunk * kHeadSlice;
-    k_head_slices<<<(unsigned)((n + 255) / 256), 256, 0, st>>>(head, bits, ns, P, S, Z);
-    *view = QW{reinterpret_cast<const uint32_t*>(P), S, reinterpret_cast<const uint32_t*>(Z), head.rows, head.cols};
-    return cudaGetLastError();
-}
 
 static uint32_t up16(uint32_t v) { return (v + 15) & ~15u; }
 
@@ -1062,13 +961,11 @@ static uint32_t plan_range(MegaSlice& S, const QW& w, int bits, uint32_t r0, uin
     return cursor;
 }
 
-void mega_build_table(uint32_t mt, const MegaArgs& A, const QW& head_slices, const MegaGeometry& g,
+void mega_build_table(uint32_t mt, const MegaArgs& A, const MegaGeometry& g,
                       std::vector<MegaSlice>& table, std::vector<uint32_t>& counts, uint32_t& stride) {
     const uint32_t G = g.grid, L = A.layers, hd = A.head_dim, half = hd / 2, per_slot = half / 4;
     const uint32_t units = (A.heads + 2 * A.kv_heads) * per_slot;
-    const uint32_t nsl = (A.vocab + kHeadSlice - 1) / kHeadSlice;
-    const uint32_t max_head = (nsl + G - 1) / G;
-    stride = 4 * L + (max_head ? max_head : 1);
+    stride = 4 * L;
     table.assign((size_t)G * stride, MegaSlice{});
     counts.assign(G, 0);
     for (uint32_t c = 0; c < G; ++c) {
@@ -1114,29 +1011,7 @@ void mega_build_table(uint32_t mt, const MegaArgs& A, const QW& head_slices, con
                 ++i;
             }
         }
-        const uint32_t s0 = split_lo(nsl, G, c, 1), s1 = split_lo(nsl, G, c + 1, 1);
-        {  // the first head slice carries the final-norm gain (even when this CTA has no rows)
-            MegaSlice& S = T[i];
-            S.off_v = 0;
-            plan_copy(S, A.final_norm, A.hidden * 4, 0);
-        }
-        uint32_t j = 0;
-        const uint32_t nchunk = A.hidden * A.head_bits / 128, bpr = A.hidden / kBlock;
-        for (uint32_t sl = s0; sl < s1; ++sl, ++j) {  // 32-row slices of the slice-major head copy
-            MegaSlice& S = T[i + j];
-            MegaRange& R = S.range[S.nrange++];
-            R.r0 = sl * kHeadSlice;
-            R.r1 = R.r0 + kHeadSlice < A.vocab ? R.r0 + kHeadSlice : A.vocab;
-            uint32_t cur = j == 0 ? up16(A.hidden * 4) : 0;
-            R.off_p = cur;
-            cur = plan_copy(S, reinterpret_cast<const uint8_t*>(head_slices.packed) + (size_t)sl * nchunk * kHeadSlice * 16,
-                            nchunk * kHeadSlice * 16, cur);
-            R.off_s = cur;
-            cur = plan_copy(S, head_slices.scales + (size_t)sl * bpr * kHeadSlice, bpr * kHeadSlice * 4, cur);
-            R.off_z = cur;
-            plan_copy(S, reinterpret_cast<const uint8_t*>(head_slices.zeros) + (size_t)sl * bpr * kHeadSlice, bpr * kHeadSlice, cur);
-        }
-        counts[c] = i + (j ? j : 1);
+        counts[c] = i;
     }
 }
 
@@ -1164,7 +1039,6 @@ MegaGeometry mega_geometry(uint32_t mt, const MegaArgs& A) {
     cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
     cudaDeviceGetAttribute(&maxsm, cudaDevAttrMaxSharedMemoryPerBlockOptin, dev);
     g.grid = (uint32_t)sms;
-    g.head_chunk = 32;
     const uint32_t x4 = A.intermediate > A.hidden ? A.intermediate : A.hidden;
     g.x4_floats = x4;
     auto range_bytes = [](uint32_t rows, uint32_t cols, uint32_t bits, uint32_t bpr) {
@@ -1176,9 +1050,8 @@ MegaGeometry mega_geometry(uint32_t mt, const MegaArgs& A) {
     const uint32_t units = (A.heads + 2 * A.kv_heads) * (A.head_dim / 8);
     const uint32_t upc = (units + g.grid - 1) / g.grid;  // q|k|v units per CTA
     uint32_t slot = gain + 2 * range_bytes(rows4, A.hidden, 4, bprH);
-    const uint32_t cand[4] = {range_bytes(rows5, A.intermediate, 4, bprI), gain + upc * 2 * range_bytes(4, A.hidden, 4, bprH),
-                              range_bytes(rows5, A.hidden, 4, bprH),
-                              gain + range_bytes(g.head_chunk, A.hidden, (uint32_t)A.head_bits, bprH)};
+    const uint32_t cand[3] = {range_bytes(rows5, A.intermediate, 4, bprI), gain + upc * 2 * range_bytes(4, A.hidden, 4, bprH),
+                              range_bytes(rows5, A.hidden, 4, bprH)};
     for (uint32_t v : cand) slot = v > slot ? v : slot;
     slot = (slot + 127) & ~127u;
     g.slot_bytes = slot;

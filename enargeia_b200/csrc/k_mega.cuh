@@ -72,23 +72,15 @@ struct MegaArgs {
 };
 
 struct MegaGeometry {
-    uint32_t grid, nslots, slot_bytes, x4_floats, max_positions, head_chunk;
+    uint32_t grid, nslots, slot_bytes, x4_floats, max_positions;
     size_t smem;
 };
 
 // Grid, ring and shared-memory geometry for `mt` tokens; nslots < 2 means the shape is not supported.
 MegaGeometry mega_geometry(uint32_t mt, const MegaArgs& A);
 // The per-CTA slice table for `mt` tokens (host side): table[c * stride + i], counts[c].
-// head_slices is the slice-major copy of the tied head (mega_head_slices).
-void mega_build_table(uint32_t mt, const MegaArgs& A, const QW& head_slices, const MegaGeometry& g,
-                      std::vector<MegaSlice>& table, std::vector<uint32_t>& counts, uint32_t& stride);
-// Bytes of the tied head re-laid out in slices of 32 rows, and the kernel that writes it: slice
-// s holds, chunk-major, the 16-byte code chunks of its 32 rows ([chunk][row]), then its scales
-// ([block][row] floats) and zero-points ([block][row] bytes).  A lane per row then reads its
-// codes free of bank conflicts while every lane reads the same activation chunk.
-constexpr uint32_t kHeadSlice = 32;
-size_t mega_head_slices_bytes(uint32_t vocab, uint32_t hidden, int bits);
-cudaError_t mega_head_slices(const QW& head, int bits, uint8_t* out, QW* view, cudaStream_t st);
+void mega_build_table(uint32_t mt, const MegaArgs& A, const MegaGeometry& g, std::vector<MegaSlice>& table,
+                      std::vector<uint32_t>& counts, uint32_t& stride);
 // Spins a bounded wait of the persistent kernel takes before it gives up (current device; 0 = the
 // default 2^24).
 cudaError_t mega_set_spin(uint32_t spins);

@@ -108,6 +108,28 @@ def test_lm_head_q8(gpu, oracle, rows):
     within(out.cpu().numpy(), oracle.linear_q(t, x))
 
 
+@pytest.mark.parametrize("rows,seq,h", [(151936, 1, 896), (151936, 2, 896), (1000, 3, 896), (4099, 4, 896), (1000, 2, 128)])
+def test_lm_head_q8_tensor_core_rows(gpu, oracle, rows, seq, h):
+    """1-4 decode rows take the tensor-core head (exact activation limbs, int8 codes as stored):
+    the reference's per-product double sum to within BASELINE's tolerance, bit-identical for all
+    but rare last-bit roundings, and no bounded wait may have given up."""
+    rng = np.random.default_rng(rows + seq)
+    w = rng.standard_normal((rows, h), dtype=np.float32) * np.float32(0.02)
+    t = quantize_tensor("e", w, 8)
+    x = rng.standard_normal(seq * h, dtype=np.float32).reshape(seq, h)
+    out = torch.zeros(seq * rows, dtype=torch.float32, device="cuda")
+    p, s, z = qdev(t)
+    xd = dev(x)
+    d = K.EmbeddingDims(seq, h, 0, rows, 64, h // 64, rows, 0, min(rows, 65535), 0, 0, 0)
+    K.call("enx_lm_head_q8", xd.data_ptr(), p.data_ptr(), s.data_ptr(), z.data_ptr(), out.data_ptr(), K.C.byref(d), None)
+    K.raw_check()
+    got = out.cpu().numpy().reshape(seq, rows)
+    for i in range(seq):
+        want = oracle.linear_q(t, x[i])
+        within(got[i], want)
+        assert np.mean(got[i] == want) >= 0.999
+
+
 def test_embed_gather_q8(gpu, oracle):
     V, h = 5000, 896
     rng = np.random.default_rng(3)
