@@ -227,10 +227,10 @@ def run_enx(args, rank, world, local_rank):
     e2e_value = world * args.steps / (e2e_ms / 1e3)
     consistent = api_ids == loop_ids
 
-    # --- roofline: the persistent decode kernel (the step's dominant kernel) ------------------
-    # One decode step at position PROMPT + 1, then the kernel alone, `reps` times back to back on
-    # the context stream (enx_launch_step_kernel: no sampler, no host copies), timed with events
-    # on that stream.  Each launch streams every weight once (351 MB > 126 MB L2).
+    # --- roofline: the step's weight-streaming kernels (persistent layers + tensor-core head) ----
+    # One decode step at position PROMPT + 1, then those two kernels alone, `reps` times back to
+    # back on the context stream (enx_launch_step_kernel: no sampler, no host copies), timed with
+    # events on that stream.  Each pass streams every weight once (351 MB > 126 MB L2).
     restart_tok = restart()
     Session(m, GREEDY).decode_step(restart_tok)
     torch.cuda.synchronize()
@@ -285,7 +285,7 @@ def run_enx(args, rank, world, local_rank):
                    "step_bytes": step_bytes + kv_bytes},
         "e2e": {"value": round(e2e_value, 2), "unit": "tok/s", "h2d_bytes_per_step": 116, "d2h_bytes_per_step": 4,
                 "api": "Session.decode_step -> enx_decode_step (pinned step block in, 4-byte id out)"},
-        "roofline": {"kernel": "k_mega<1,8> (persistent decode step: 24 layers + tied int8 head, batch 1)",
+        "roofline": {"kernel": "k_mega<1,8> (persistent decode: 24 layers) + k_head_tc<2> (tied int8 head, tcgen05), batch 1",
                      "bound": "hbm", "achieved": round(achieved, 1), "peak": hbm, "unit": "GB/s",
                      "frac": round(achieved / hbm, 4), "traffic": traffic,
                      "algorithmic_bytes_per_launch": kern_bytes, "launch_us": round(kern_us, 2),

@@ -161,7 +161,7 @@ extern "C" enx_status enx_lm_head_q8(const float* x, const uint32_t* packed, con
                                 as_stream(stream)));
         return ENX_OK;
     }
-    if (d->seq <= 4 && d->hidden <= 1024) {  // decode rows: the tensor-core head (exact limbs)
+    if (d->seq <= 4 && d->hidden <= 1024 && d->hidden % 128 == 0) {  // decode rows: tensor-core head
         uint8_t* ws = nullptr;
         uint32_t* err = nullptr;
         ENX_TRY(tc_workspace(0, &ws, &err));
@@ -1403,7 +1403,7 @@ static enx_status decode_batch_loop(enx_ctx* c, uint32_t B, const uint32_t* firs
 // layer's x in S.x): the tensor-core head for an int8 table (its weight stream starts while k_mega
 // drains), the CUDA-core head kernel otherwise.
 static cudaError_t launch_step_head(enx_ctx* c, uint32_t B, const StepArgs& S, cudaStream_t st) {
-    if (c->head.bits == 8) {
+    if (c->head.bits == 8 && c->cfg.hidden % 128 == 0 && c->cfg.hidden <= 1024) {
         HeadTcArgs h{};
         h.x = c->x;
         h.gain = c->head.norm;
@@ -1723,6 +1723,7 @@ extern "C" enx_status enx_launch_step_kernel(enx_ctx* c, uint32_t batch, uint32_
         k_bump_epoch<<<1, 32, 0, c->stream>>>(c->d_bar);
         ENX_CUDA(cudaGetLastError());
         ENX_CUDA(launch_mega(batch, A, geo, c->stream));
+        ENX_CUDA(launch_step_head(c, batch, S, c->stream));
     }
     return ENX_OK;
 }

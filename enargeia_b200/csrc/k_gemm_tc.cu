@@ -563,13 +563,22 @@ cudaError_t launch_gemm_tc(int bits, const float* x, uint32_t ld, const QW& w, c
     return cudaGetLastError();
 }
 
+// A tile of 128 rows x 128 code bytes (two 64-element blocks) written by TMA with the 128-byte
+// swizzle: the K-major SWIZZLE_128B layout (rows of 128 bytes, 8-row groups 1024 bytes apart);
+// the K = 32 steps inside a row start 32 bytes apart.
+__device__ __forceinline__ uint64_t mdesc_a128(uint32_t addr) {
+    return (uint64_t)((addr >> 4) & 0x3FFF) | (1ull << 16) | ((uint64_t)(1024 >> 4) << 32) | (1ull << 46) | (2ull << 61);
+}
+
 // ---------------------------------------------------------------------------------------------
 // The tied int8 head for a few tokens (decode): logits[t][row] = x_t . W[row] over every row.
 //
 // Same exact-limb arithmetic as k_gemm_tc, shaped for 1-4 tokens: the weight rows are the MMA's
 // M (128 per tile) and the activation limbs its N (6 limbs x NT tokens, padded to 16 or 32), so
 // the tensor pipe does 16 (or 32) columns of work per weight byte and the kernel streams the
-// table instead of spending a DFMA per weight.  Each 64-column block of a tile accumulates into
+// table instead of spending a DFMA per weight.  Code boxes are 128 bytes wide (two blocks, 128-byte
+// swizzle): with 64-byte boxes the same kernel streamed at 3.2 TB/s whatever its ring depth,
+// epilogue or L2 promotion (measured), so the box rows are what the table stream costs.  Each 64-column block of a tile accumulates into
 // its own TMEM columns (the per-block scale is applied in the epilogue), so a tile of 128 rows x
 // 14 blocks holds 14 x N columns; tiles alternate between two accumulators.
 //
@@ -579,7 +588,8 @@ cudaError_t launch_gemm_tc(int bits, const float* x, uint32_t ld, const QW& w, c
 // activations in shared memory (optionally normalised here with the final-norm gain); warp 1
 // issues the MMAs; warps 2-9 (two per TMEM lane quadrant, a thread per row and half of the blocks)
 // join limbs, take off z * sum(X), scale per block in double, and add the two halves in order.
-constexpr uint32_t kHtStages = 20;      // 8 KB code boxes in flight (160 KB)
+constexpr uint32_t kHtStages = 10;      // 16 KB code boxes in flight (160 KB)
+constexpr uint32_t kHtBox = kTcRows * 128;  // a box: 128 rows x two 64-byte blocks
 constexpr uint32_t kHtEpiWarps = 8;     // two per TMEM lane quadrant (block halves)
 constexpr uint32_t kHtThreads = 32 * (2 + kHtEpiWarps);
 constexpr uint32_t kHtMaxBlocks = 16;   // K <= 1024
@@ -588,8 +598,8 @@ template <int NT>  // token capacity: 2 (N = 16) or 4 (N = 32)
 __global__ void __launch_bounds__(kHtThreads, 1) k_head_tc(const __grid_constant__ CUtensorMap cmap, const HeadTcArgs a) {
     constexpr uint32_t N = NT <= 2 ? 16 : 32;
     extern __shared__ __align__(1024) uint8_t smem[];
-    uint8_t* sA = smem;                                 // [stages][8 KB] code boxes
-    uint8_t* sB = smem + kHtStages * kTcATile;          // [blocks][N x 64] limb tiles (canonical)
+    uint8_t* sA = smem;                                 // [stages][16 KB] code boxes
+    uint8_t* sB = smem + kHtStages * kHtBox;            // [blocks][N x 64] limb tiles (canonical)
     __shared__ __align__(8) uint64_t full[kHtStages], empty[kHtStages], accf[2], acce[2];
     __shared__ long long xsumb[kHtMaxBlocks][NT];      // per block and token: sum of X
     __shared__ double scal[NT];                         // per token: 2^-F
@@ -633,13 +643,13 @@ __global__ void __launch_bounds__(kHtThreads, 1) k_head_tc(const __grid_constant
         if (lane == 0) {
             uint32_t issued = 0;
             for (uint32_t tile = blockIdx.x; tile < ntiles && !s_fail; tile += gridDim.x)
-                for (uint32_t b = 0; b < nb; ++b, ++issued) {
+                for (uint32_t bx = 0; bx < nb / 2; ++bx, ++issued) {
                     const uint32_t s = issued % kHtStages;
                     if (issued >= kHtStages && !mbar_wait_f(&empty[s], ((issued / kHtStages) - 1) & 1, &s_fail, a.err, spin))
                         goto produced;
-                    asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(su32(&full[s])), "r"(kTcATile)
+                    asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(su32(&full[s])), "r"(kHtBox)
                                  : "memory");
-                    tma_codes(sA + s * kTcATile, &cmap, b, tile * kTcRows, &full[s]);
+                    tma_codes(sA + s * kHtBox, &cmap, 2 * bx, tile * kTcRows, &full[s]);  // x = 128 bx bytes
                 }
         produced:
             // no copy may still be landing when the CTA releases its shared memory (error path)
@@ -743,21 +753,22 @@ __global__ void __launch_bounds__(kHtThreads, 1) k_head_tc(const __grid_constant
                     if (t_i >= nacc && !mbar_wait_f(&acce[acc], ((t_i / nacc) - 1) & 1, &s_fail, a.err, spin)) break;
                     asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
                     bool ok = true;
-                    for (uint32_t b = 0; b < nb; ++b, ++consumed) {
+                    for (uint32_t bx = 0; bx < nb / 2; ++bx, ++consumed) {
                         const uint32_t s = consumed % kHtStages;
                         if (!mbar_wait_f(&full[s], (consumed / kHtStages) & 1, &s_fail, a.err, spin)) {
                             ok = false;
                             break;
                         }
                         asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
-                        const uint32_t dcol = tmem + acc * cols_per_tile + b * N;
 #pragma unroll
-                        for (uint32_t kk = 0; kk < 2; ++kk) {
-                            const uint64_t ad = mdesc_a(su32(sA + s * kTcATile) + kk * 32);
-                            const uint64_t bd = mdesc(su32(sB + b * (N * 64)) + kk * 256);
+                        for (uint32_t kk = 0; kk < 4; ++kk) {  // K = 32 steps: blocks 2 bx (kk < 2), 2 bx + 1
+                            const uint32_t b = 2 * bx + kk / 2;
+                            const uint32_t dcol = tmem + acc * cols_per_tile + b * N;
+                            const uint64_t ad = mdesc_a128(su32(sA + s * kHtBox) + kk * 32);
+                            const uint64_t bd = mdesc(su32(sB + b * (N * 64)) + (kk & 1) * 256);
                             asm volatile("{\n .reg .pred p;\n setp.ne.b32 p, %4, 0;\n tcgen05.mma.cta_group::1.kind::i8 [%0], %1, %2, %3, p;\n}\n" ::"r"(
                                              dcol),
-                                         "l"(ad), "l"(bd), "r"(id), "r"(kk));
+                                         "l"(ad), "l"(bd), "r"(id), "r"(kk & 1));
                         }
                         asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(
                                          su32(&empty[s]))
@@ -794,9 +805,11 @@ __global__ void __launch_bounds__(kHtThreads, 1) k_head_tc(const __grid_constant
                     sreg[bb] = use ? __ldg(a.w.scales + (size_t)row * nb + b0 + bb) : 0.f;
                     zreg[bb] = use ? (uint32_t)__ldg(zb + b0 + bb) : 0u;
                 }
+                // a warp whose wait gives up still meets the others at the half-sum barrier below
+                // (a named barrier cannot time out), then every epilogue warp leaves together
                 int ok = 1;
                 if (lane == 0) ok = mbar_wait_f(&accf[acc], (t_i / nacc) & 1, &s_fail, a.err, spin);
-                if (!__shfl_sync(0xffffffffu, ok, 0)) break;
+                ok = __shfl_sync(0xffffffffu, ok, 0);
                 asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
                 double sum[NT];
 #pragma unroll
@@ -823,7 +836,8 @@ __global__ void __launch_bounds__(kHtThreads, 1) k_head_tc(const __grid_constant
                                  : "r"(ta));
                 };
                 const uint32_t tbase = tmem + (quad * 32u << 16) + acc * cols_per_tile;
-                if constexpr (N == 16) {  // two blocks per wait
+                if (!ok) {
+                } else if constexpr (N == 16) {  // two blocks per wait
 #pragma unroll
                     for (uint32_t bb = 0; bb < kHtMaxBlocks / 2; bb += 2) {
                         if (b0 + bb >= b1) break;
@@ -852,6 +866,7 @@ __global__ void __launch_bounds__(kHtThreads, 1) k_head_tc(const __grid_constant
 #pragma unroll
                 for (int t = 0; t < NT; ++t) hs[(half * kTcRows + erow) * NT + t] = sum[t];
                 asm volatile("bar.sync 2, %0;" ::"n"(kHtEpiWarps * 32) : "memory");
+                if (s_fail) break;  // set before the barrier by any warp that gave up
                 if (half == 0 && live)
 #pragma unroll
                     for (int t = 0; t < NT; ++t)
@@ -869,24 +884,24 @@ __global__ void __launch_bounds__(kHtThreads, 1) k_head_tc(const __grid_constant
 
 cudaError_t launch_head_tc(const HeadTcArgs& args, cudaStream_t st, bool pdl) {
     const uint32_t nb = args.w.cols / kBlock, N = args.ntok <= 2 ? 16u : 32u;
-    if (args.ntok == 0 || args.ntok > 4 || args.w.cols % kBlock || nb > kHtMaxBlocks || nb * N > 512)
+    if (args.ntok == 0 || args.ntok > 4 || args.w.cols % (2 * kBlock) || nb > kHtMaxBlocks || nb * N > 512)
         return cudaErrorInvalidValue;
     CUtensorMap cmap;
     {
         const cuuint64_t dims[2] = {args.w.cols, args.w.rows};
         const cuuint64_t strides[1] = {args.w.cols};
-        const cuuint32_t box[2] = {64, kTcRows};
+        const cuuint32_t box[2] = {128, kTcRows};
         const cuuint32_t estr[2] = {1, 1};
         const EncodeTiledFn encode = encode_tiled();
         if (!encode) return cudaErrorNotSupported;
         const CUresult r = encode(&cmap, CU_TENSOR_MAP_DATA_TYPE_UINT8, 2, (void*)args.w.packed, dims, strides, box, estr,
-                                  CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_64B,
+                                  CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
                                   CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
         if (r != CUDA_SUCCESS) return cudaErrorInvalidValue;
     }
     const uint32_t ntiles = (args.w.rows + kTcRows - 1) / kTcRows;
     const uint32_t sms = (uint32_t)num_sms();
-    const size_t smem = (size_t)kHtStages * kTcATile + (size_t)nb * N * 64;
+    const size_t smem = (size_t)kHtStages * kHtBox + (size_t)nb * N * 64;
     cudaLaunchConfig_t cfg = {};
     cfg.gridDim = dim3(ntiles < sms ? ntiles : sms);
     cfg.blockDim = dim3(kHtThreads);

@@ -321,9 +321,10 @@ ENX_API enx_status enx_stream(enx_ctx* ctx, void** stream);
 /* Kernel launches issued by the last enx_decode_step (the captured step's node count). */
 ENX_API enx_status enx_step_launches(enx_ctx* ctx, uint32_t* launches);
 
-/* Measurement hook: enqueue on the context stream, `count` times, the persistent decode kernel
- * alone (with its barrier reset) for the `batch` tokens and positions of the last decode step,
- * without the sampler or any host copy.  Re-running a step rewrites the same cache rows and
+/* Measurement hook: enqueue on the context stream, `count` times, the weight-streaming kernels of
+ * a decode step -- the persistent layer kernel (after its tag-epoch bump) and the tied-head kernel
+ * -- for the `batch` tokens and positions of the last decode step, without the sampler or any
+ * host copy.  Re-running a step rewrites the same cache rows and
  * logits.  ENX_ERR_STATE if no step ran yet or the step did not use the persistent kernel. */
 ENX_API enx_status enx_launch_step_kernel(enx_ctx* ctx, uint32_t batch, uint32_t count);
 
