@@ -227,6 +227,20 @@ def run_enx(args, rank, world, local_rank):
     e2e_value = world * args.steps / (e2e_ms / 1e3)
     consistent = api_ids == loop_ids
 
+    # --- TTFT: a 32-id prompt in, the first sampled id out, through the public Session API ------
+    # (host ids -> enx_prefill -> enx_sample_prefill -> 4-byte id back), wall clock, median of 10
+    ttfts = []
+    for _ in range(12):
+        m.reset(0)
+        sess = Session(m, GREEDY)
+        torch.cuda.synchronize()
+        t0 = time.perf_counter()
+        sess.prime(prompt)
+        sess.sample_from_prefill()
+        ttfts.append(time.perf_counter() - t0)
+    ttft_ms = statistics.median(ttfts[2:]) * 1e3
+    ttft_ms = max_over_ranks(ttft_ms)
+
     # --- roofline: the step's weight-streaming kernels (persistent layers + tensor-core head) ----
     # One decode step at position PROMPT + 1, then those two kernels alone, `reps` times back to
     # back on the context stream (enx_launch_step_kernel: no sampler, no host copies), timed with
@@ -245,6 +259,7 @@ def run_enx(args, rank, world, local_rank):
     e1.record(stream)
     torch.cuda.synchronize()
     kern_us = e0.elapsed_time(e1) / reps * 1e3
+    shares = kernel_shares(m, stream, ms_total / args.steps * 1e3)
     kv_positions = PROMPT + 2  # positions attended by the step at position PROMPT + 1
     kern_bytes = weight_bytes + cfg.layers * 2 * kv_positions * cfg.kv_dim * 2
     peaks = {}
@@ -295,6 +310,9 @@ def run_enx(args, rank, world, local_rank):
                           "frac": round(step_achieved / hbm, 4)},
         "gpu_launches": launches_per_step * args.steps,
         "launches_per_step": launches_per_step,
+        "ttft": {"value": round(ttft_ms, 3), "unit": "ms", "prompt_ids": PROMPT,
+                 "api": "Session.prime + Session.sample_from_prefill (host ids in, first id out), median of 10"},
+        "kernel_shares": shares,
         "ids_consistent_loop_vs_api": consistent,
         "clocks": clocks.summary(),
     }
@@ -980,6 +998,46 @@ def head_cpu_baseline(table, budget_s=15.0):
 # TypeScript and cannot run on this box)
 
 
+def kernel_shares(m, stream, step_us):
+    """The reference's telemetry share table (src/runtime/telemetry.ts:12-20) for one decode step:
+    the traced stages of the layer kernel, plus CUDA-event times of the head kernel and the
+    sampler run alone on the model's own tensors (20 launches each)."""
+    import torch
+    from enargeia_b200 import kernels as K
+    from enargeia_b200._lib import EmbeddingDims, call
+    from enargeia_b200.session import GREEDY
+    from enargeia_b200.telemetry import step_shares
+
+    m.set_tracing(True)
+    tok = m.decode_step([7], [GREEDY], [0.5])[0]
+    stage = m.stage_times()
+    m.set_tracing(False)
+    cfg = m.config
+    hv = m.tensor_view("model.embed_tokens.weight")
+    x = torch.from_numpy(m.hidden(0)).cuda()
+    logits = torch.zeros(cfg.vocab, dtype=torch.float32, device="cuda")
+    d = EmbeddingDims(1, cfg.hidden, 0, cfg.vocab, 64, cfg.hidden // 64, cfg.vocab, 0, min(cfg.vocab, 65535), 0, 0, 0)
+    out = torch.zeros(1, dtype=torch.int32, device="cuda")
+    hist = torch.zeros(64, dtype=torch.int32, device="cuda")
+
+    def timed(fn, reps=20):
+        fn()
+        torch.cuda.synchronize()
+        a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        a.record()
+        for _ in range(reps):
+            fn()
+        b.record()
+        torch.cuda.synchronize()
+        return a.elapsed_time(b) / reps * 1e3
+
+    import ctypes as C
+    head_us = timed(lambda: call("enx_lm_head_q8", x.data_ptr(), hv["packed"], hv["scales"], hv["zeros"],
+                                 logits.data_ptr(), C.byref(d), None))
+    sample_us = timed(lambda: K.sample(logits, hist, out, 0.0, 1.0, 1.0, 0.5))
+    return step_shares(stage, head_us, sample_us, step_us)
+
+
 def cpu_baseline(f, prompt, budget_s=15.0, threads=None):
     from oracle import oracle as O
 
@@ -997,9 +1055,21 @@ def cpu_baseline(f, prompt, budget_s=15.0, threads=None):
         tok = O.argmax(logits)
         n += 1
     dt = time.perf_counter() - t0
+    # the same decode continued on one host thread (the reference's JS path is single-threaded)
+    O.set_threads(1)
+    n1 = 0
+    t1 = time.perf_counter()
+    while n1 < 2 or (n1 < GEN - 1 - n and time.perf_counter() - t1 < budget_s / 2):
+        logits = om.decode(tok)
+        tok = O.argmax(logits)
+        n1 += 1
+    dt1 = time.perf_counter() - t1
+    O.set_threads(cores)
     return {"value": round(n / dt, 4), "unit": "tok/s", "cores": cores, "kind": "port",
             "sample": f"{n} greedy decode steps of config 0 after a 32-id prefill (oracle/enx_oracle.cpp, "
-                      f"f64 accumulate, OpenMP over output rows), {dt:.1f} s"}
+                      f"f64 accumulate, OpenMP over output rows), {dt:.1f} s",
+            "single_thread": {"value": round(n1 / dt1, 4), "unit": "tok/s", "cores": 1,
+                              "sample": f"{n1} further decode steps on one host thread, {dt1:.1f} s"}}
 
 
 def run_reference(args, rank, world):

@@ -29,7 +29,7 @@ def _case(position, seed, heads=14, kvh=2, hd=64):
     return q, k, v
 
 
-def test_noalloc_matches_workspace_path_twice(gpu):
+def test_noalloc_matches_workspace_path_twice(gpu, oracle):
     from enargeia_b200 import _lib
     from enargeia_b200._lib import AttnDecodeDims
 
@@ -48,6 +48,12 @@ def test_noalloc_matches_workspace_path_twice(gpu):
         a, b = got.cpu().numpy().astype(np.float64), ref.cpu().numpy().astype(np.float64)
         ratio = np.abs(a - b) / (ATOL + RTOL * np.abs(b))
         assert np.isfinite(a).all() and ratio.max() <= 1.0, (call, float(ratio.max()))
+        # and independently against the CPU restatement of the reference's attention
+        kb = k.cpu().numpy().view(np.uint16)
+        vb = v.cpu().numpy().view(np.uint16)
+        want = oracle.attention_f16(q.cpu().numpy(), kb, vb, position, heads, kvh, hd).reshape(-1).astype(np.float64)
+        ratio = np.abs(a - want) / (ATOL + RTOL * np.abs(want))
+        assert ratio.max() <= 1.0, (call, "oracle", float(ratio.max()))
 
 
 def test_noalloc_rejects_oversize(gpu):
