@@ -318,9 +318,41 @@ def run_enx(args, rank, world, local_rank):
     }
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
         out["cpu_baseline"] = cpu_baseline(f, prompt, budget_s=args.cpu_budget)
+    m.close()
+    if not args.no_blocks:
+        # the work that shards, measured at this N beside the replicated headline: config 4 (DP
+        # sequences, 256/N per GPU, a bounded number of steps) and config 2 (vocab-sharded head)
+        out["dp_batched"] = scaling_block(run_batched(block_args(args, steps=BLOCK_STEPS + args.warmup + 8, batch=256),
+                                                      rank, world, local_rank, emit=False))
+        out["vocab_sharded"] = scaling_block(run_head(block_args(args, steps=50, batch=64), rank, world, local_rank,
+                                                      emit=False))
     if rank == 0:
         print(json.dumps(out), flush=True)
-    m.close()
+
+
+BLOCK_STEPS = 64  # timed config-4 steps in the default line's dp_batched block
+
+
+def block_args(args, **kw):
+    b = argparse.Namespace(**vars(args))
+    b.no_cpu_baseline = True
+    for k, v in kw.items():
+        setattr(b, k, v)
+    return b
+
+
+def scaling_block(line):
+    """The fields of a workload's own line that the scaling run compares across N."""
+    if line is None:
+        return None
+    keep = ["metric", "value", "unit", "n_gpus", "steps", "ms_per_step", "scaling"]
+    blk = {k: line[k] for k in keep if k in line}
+    blk["frac"] = line.get("roofline", {}).get("frac")
+    blk["roofline_kernel"] = line.get("roofline", {}).get("kernel")
+    blk["workload"] = line.get("config", {}).get("workload")
+    if "positions_timed" in line.get("config", {}):
+        blk["positions_timed"] = line["config"]["positions_timed"]
+    return blk
 
 
 # ---------------------------------------------------------------------------------------------
@@ -496,7 +528,7 @@ BATCH_PROMPT, BATCH_CTX = 512, 2048
 BATCH_METRIC = "batched sampled decode tok/s (256 sequences, prompt 512 -> context 2048, T 0.7 / top-p 0.9 / rp 1.1)"
 
 
-def run_batched(args, rank, world, local_rank):
+def run_batched(args, rank, world, local_rank, emit=True):
     """Independent sequences, data-parallel: each rank decodes its share of the 256 with its own
     weight replica and caches (strong scaling: total work fixed).  Projections and the tied head run
     on the tensor-core GEMM (exact integer block sums), attention reads each sequence's f16 cache."""
@@ -621,9 +653,10 @@ def run_batched(args, rank, world, local_rank):
         "launches_per_step": launches,
         "clocks": clocks.summary(),
     }
-    if rank == 0:
+    if rank == 0 and emit:
         print(json.dumps(out), flush=True)
     m.close()
+    return out
 
 
 # ---------------------------------------------------------------------------------------------
@@ -808,7 +841,7 @@ def head_table():
     return quantize_tensor("model.embed_tokens.weight", w, 8)
 
 
-def run_head(args, rank, world, local_rank):
+def run_head(args, rank, world, local_rank, emit=True):
     """Each rank holds the contiguous row range of the table its shard owns; one step computes the
     logits of B hidden states on every shard and samples B ids.  N = 1: the fused single-GPU
     sampler (one cluster per row); N > 1: the sharded sampler's phases with an NCCL allgather of
@@ -969,8 +1002,9 @@ def run_head(args, rank, world, local_rank):
     }
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
         out["cpu_baseline"] = head_cpu_baseline(table, budget_s=args.cpu_budget)
-    if rank == 0:
+    if rank == 0 and emit:
         print(json.dumps(out), flush=True)
+    return out
 
 
 def head_cpu_baseline(table, budget_s=15.0):
@@ -1125,6 +1159,8 @@ def main():
     ap.add_argument("--impl", choices=["enx", "reference"], default="enx")
     ap.add_argument("--cpu-budget", type=float, default=15.0)
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--no-blocks", action="store_true",
+                    help="config0: skip the dp_batched (config 4) and vocab_sharded (config 2) blocks")
     ap.add_argument("--workload", choices=["config0", "config1", "config2", "config3", "config4"], default="config0",
                     help="config0: greedy batch-1 decode (the headline); config1: int4 matvec/GEMM sweep; "
                          "config2: vocab-sharded LM head + sampling; config3: chunked prefill; "
