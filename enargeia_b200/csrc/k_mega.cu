@@ -70,7 +70,7 @@ __device__ __forceinline__ bool mbar_wait_bounded(uint64_t* bar, uint32_t parity
         if (mbar_try_wait(bar, parity)) return true;
     return false;
 }
-// Plain (non-multicast) bulk copy global -> this CTA's shared memory.
+// Plain bulk copy global -> this CTA's own shared memory (one destination CTA).
 __device__ __forceinline__ void bulk_copy(uint32_t dst_smem, unsigned long long src, uint32_t bytes, uint64_t* bar) {
     asm volatile("cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(dst_smem),
                  "l"(src), "r"(bytes), "r"(smem_u32(bar))
