@@ -825,6 +825,7 @@ __global__ void __launch_bounds__(kMThreads, 1) k_mega(const __grid_constant__ M
             const MegaSlice& D = sdesc[slice % NS];
             const uint8_t* slot = slot_ptr();
             load_norm<4, MT>(Xd, xsum, xs, true, H, reinterpret_cast<const float*>(slot + D.off_v), A.eps, rs, red);
+            stamp_a(A, l, 11);
             if (D.nrange) {
                 const MegaRange& Rg = D.range[0];
                 const MegaRange& Ru = D.range[1];
@@ -840,6 +841,7 @@ __global__ void __launch_bounds__(kMThreads, 1) k_mega(const __grid_constant__ M
                         }
                 }
                 cbar();
+                stamp_a(A, l, 12);
                 for (uint32_t e = tid; e < nr * MT; e += kMConsumers) {
                     const uint32_t i = e / MT, t = e % MT;
                     const float gv = silu_mul_value((float)res[i * MT + t], (float)res[(nr + i) * MT + t]);

@@ -10,7 +10,7 @@ namespace enx {
 constexpr uint32_t kMaxLayers = 32;
 constexpr uint32_t kMegaSlots = 8;   // upper bound on ring slots
 constexpr uint32_t kMegaStages = 3;  // traced stages per layer (attention + o, gate/up, down)
-constexpr uint32_t kMegaTraceDetail = 12;  // extra stamps per layer inside stage A
+constexpr uint32_t kMegaTraceDetail = 14;  // extra stamps per layer inside stage A
 constexpr uint32_t kMegaBarWords = 64;    // u64 words of step counters (word 0: the tag epoch, then arrival counters)
 constexpr uint32_t kMegaMaxTokens = 4;    // tokens per launch the tagged buffers are sized for
 

@@ -190,7 +190,7 @@ class Model:
         stage waited for its barrier+weights and how long it computed (kernel-group telemetry of
         src/runtime/telemetry.ts, at stage granularity)."""
         L = self.config.layers
-        n = 3 * (3 * L + 1) + 12 * L + 2
+        n = 3 * (3 * L + 1) + 14 * L + 2
         buf = np.zeros(n, dtype=np.uint64)
         cnt = C.c_uint32()
         call("enx_trace", self._h, buf.ctypes.data, n, C.byref(cnt))
@@ -208,7 +208,7 @@ class Model:
         out["total"] = t[3 * L, 2] - t[0, 0]
         # inside the attention stage (first CTA): weights + norm, q|k|v units, wait for the kv
         # head's units, q and current k/v loads, attention, wait for every head, o rows
-        d = buf[3 * (3 * L + 1):3 * (3 * L + 1) + 12 * L].astype(np.float64).reshape(L, 12) / 1e3
+        d = buf[3 * (3 * L + 1):3 * (3 * L + 1) + 14 * L].astype(np.float64).reshape(L, 14) / 1e3
         if d.any():
             marks = ["norm", "units", "ready_wait", "q_load", "attention", "done_wait", "o_rows+end"]
             d = d[:, :6]
@@ -217,7 +217,7 @@ class Model:
             seq = np.concatenate([starts[:, None], d, ends[:, None]], axis=1)
             for j, m in enumerate(marks):
                 out[f"attn.{m}"] = float(np.sum(seq[:, j + 1] - seq[:, j]))
-            full = buf[3 * (3 * L + 1):3 * (3 * L + 1) + 12 * L].astype(np.float64).reshape(L, 12)[1:] / 1e3
+            full = buf[3 * (3 * L + 1):3 * (3 * L + 1) + 14 * L].astype(np.float64).reshape(L, 14)[1:] / 1e3
             t1 = t[3:3 * L:3, 1]
             out["norm.loads"] = float(np.sum(full[:, 6] - t1))
             out["norm.rs"] = float(np.sum(full[:, 7] - full[:, 6]))
