@@ -851,7 +851,7 @@ def run_head(args, rank, world, local_rank, emit=True):
     import torch.distributed as dist
 
     from enargeia_b200 import build, kernels as K
-    from enargeia_b200.vocab_shard import ShardedHead, ShardedSampler, ShardInputs, run_distributed, \
+    from enargeia_b200.vocab_shard import PeerGather, ShardedHead, ShardedSampler, ShardInputs, run_distributed, \
         sampling_rows_tensor
 
     build.build()
@@ -894,6 +894,10 @@ def run_head(args, rank, world, local_rank, emit=True):
         logits = torch.empty((B, head.n), dtype=torch.float32, device=dev)
         out = torch.empty(B, dtype=torch.int32, device=dev)
         sampler = ShardedSampler(HEAD_VOCAB, rank, world, B, dev) if world > 1 else None
+        # the phase exchange: peer-memory stores over NVLink (default) or NCCL all-gathers
+        gather = None
+        if sampler is not None and os.environ.get("ENX_SHARD_EXCHANGE", "peer") == "peer":
+            gather = PeerGather(sampler.max_record_bytes())
         graph = None
         if sampler is None:
             # one GPU: the head and the fused sampler replayed as one CUDA graph over static input
@@ -915,7 +919,7 @@ def run_head(args, rank, world, local_rank, emit=True):
                 graph.replay()
                 return out
             head.logits(x, logits)
-            return run_distributed(sampler, ShardInputs(logits, history, hlen, params[i]), params_dev=prow_dev)
+            return run_distributed(sampler, ShardInputs(logits, history, hlen, params[i]), gather, params_dev=prow_dev)
 
         for i in range(warmup):
             step(i, xs[i], params_dev[i])
@@ -953,6 +957,10 @@ def run_head(args, rank, world, local_rank, emit=True):
         e1.record(stream)
         torch.cuda.synchronize()
         head_us = e0.elapsed_time(e1) / reps * 1e3
+        if gather is not None:
+            gather.check()
+            barrier()
+            gather.close()
         head_bytes = shard_bytes + B * HEAD_HIDDEN * 4 + B * head.n * 4
         achieved = head_bytes / (head_us / 1e6) / 1e9
         head_launches = 2 if B >= 16 else 1
@@ -969,6 +977,8 @@ def run_head(args, rank, world, local_rank, emit=True):
                                   "algorithmic_bytes_per_launch": int(head_bytes), "launch_us": round(head_us, 2),
                                   "peak_source": f"{peak_src} MEASURED_PEAKS.json hbm_gbs (burst copy)"},
                 "sampler_ms_per_step": round(ms - head_us / 1e3, 4),
+                "exchange": None if sampler is None else ("peer stores over NVLink (enx_peer_allgather)"
+                                                          if gather is not None else "NCCL all_gather_into_tensor"),
                 "gpu_launches": launches * steps, "launches_per_step": launches}
 
     steps = min(args.steps, 200)

@@ -78,6 +78,10 @@ SIGNATURES = {
     "enx_matmul_q4": (C.c_int32, [P, P, P, P, P, P, C.POINTER(MatmulQ4Dims), P]),
     "enx_set_wait_limit": (C.c_int32, [C.c_int, U32]),
     "enx_nll": (C.c_int32, [P, U32, U32, C.POINTER(C.c_double)]),
+    "enx_peer_alloc": (C.c_int32, [C.c_size_t, C.POINTER(P), P]),
+    "enx_peer_open": (C.c_int32, [P, C.POINTER(P)]),
+    "enx_peer_close": (C.c_int32, [P, C.c_int]),
+    "enx_peer_allgather": (C.c_int32, [P, C.c_size_t, P, U32, U32, C.c_uint64, P, P]),
     "enx_lm_head_q8": (C.c_int32, [P, P, P, P, P, C.POINTER(EmbeddingDims), P]),
     "enx_embed_gather_q8": (C.c_int32, [P, P, P, P, P, C.POINTER(EmbeddingDims), P]),
     "enx_sample": (C.c_int32, [P, P, P, C.POINTER(SampleDims), P, P]),

@@ -152,6 +152,11 @@ class ShardedSampler:
         self.pick_buf = torch.empty(R * S, dtype=torch.int32, device=dev)
         self.out = torch.empty(R, dtype=torch.int32, device=dev)
 
+    def max_record_bytes(self) -> int:
+        """The largest record one rank sends in one exchange (the top-p bucket masses)."""
+        R, S = self.rows, self.split
+        return max(R * S * 4 * 4, R * S * 8, R * S * 256 * 8, R * S * 4)
+
     @staticmethod
     def rounds_for(params) -> int:
         return ROUNDS if any(p[0] > 0.0 and p[1] < 1.0 for p in params) else 0
@@ -201,6 +206,91 @@ def torch_allgather(group=None) -> Callable[[torch.Tensor], torch.Tensor]:
         return torch.cat(parts)
 
     return gather
+
+
+class _DeviceView:
+    """A raw device range as a torch tensor (zero copy, __cuda_array_interface__)."""
+
+    def __init__(self, ptr: int, nbytes: int):
+        self.__cuda_array_interface__ = {"shape": (nbytes,), "typestr": "|u1", "data": (ptr, False), "version": 3,
+                                         "strides": None}
+
+
+class PeerGather:
+    """Rank-major all-gather over peer memory (enx_peer_allgather): each rank stores its records
+    straight into every other rank's exchange buffer over NVLink and raises an arrival word; one
+    launch per exchange, no collective library.  Drop-in for torch_allgather in run_distributed.
+
+    Each exchange lands in its own region of a ring of `regions`: the protocol reads a phase's
+    gathered records again several phases later (the candidates in `finish`), so a region must not
+    be overwritten by the next step's exchanges while it can still be read; 16 regions leave a
+    whole step of margin over the 8 exchanges of a top-p step.  `max_bytes`: the largest record of
+    one rank in one exchange."""
+
+    def __init__(self, max_bytes: int, group=None, regions: int = 16, stream=None):
+        import torch.distributed as dist
+
+        self.world, self.rank = dist.get_world_size(group), dist.get_rank(group)
+        self.region = -(-max_bytes // 16) * 16 * self.world
+        self.regions = regions
+        self.stream = stream
+        own = C.c_void_p()
+        handle = (C.c_uint8 * 64)()
+        call("enx_peer_alloc", self.region * regions, C.byref(own), handle)
+        self.own = own.value
+        handles = [None] * self.world
+        dist.all_gather_object(handles, bytes(handle), group=group)
+        self.mapped = []
+        addrs = []
+        for p, hb in enumerate(handles):
+            if p == self.rank:
+                addrs.append(self.own)
+                continue
+            ptr = C.c_void_p()
+            call("enx_peer_open", (C.c_uint8 * 64).from_buffer_copy(hb), C.byref(ptr))
+            self.mapped.append(ptr.value)
+            addrs.append(ptr.value)
+        self.err = torch.zeros(1, dtype=torch.int32, device="cuda")
+        # every region's world addresses, on the device once
+        self.peer_tabs = [torch.tensor([a + r * self.region for a in addrs], dtype=torch.int64, device="cuda")
+                          for r in range(regions)]
+        self.seq = 0
+        torch.cuda.synchronize()
+        dist.barrier(group=group)  # every buffer mapped everywhere before the first exchange
+
+    def __call__(self, t: torch.Tensor) -> torch.Tensor:
+        t = t.contiguous()
+        nb = t.numel() * t.element_size()
+        padded = -(-nb // 16) * 16
+        if padded * self.world > self.region:
+            raise ValueError("record larger than the exchange region")
+        src = t
+        if padded != nb:
+            src = torch.zeros(padded, dtype=torch.uint8, device=t.device)
+            src[:nb].copy_(t.view(torch.uint8).reshape(-1))
+        self.seq += 1
+        r = self.seq % self.regions
+        s = self.stream if self.stream is not None else torch.cuda.current_stream()
+        call("enx_peer_allgather", C.c_void_p(src.data_ptr()), padded, C.c_void_p(self.peer_tabs[r].data_ptr()),
+             self.world, self.rank, self.seq, C.c_void_p(self.err.data_ptr()), C.c_void_p(s.cuda_stream))
+        self._keep = src  # alive until the launch has read it (same stream)
+        raw = torch.as_tensor(_DeviceView(self.own + r * self.region + 512, padded * self.world), device=t.device)
+        if padded != nb:
+            raw = raw.view(self.world, padded)[:, :nb].contiguous().reshape(-1)
+        return raw.view(t.dtype)
+
+    def check(self) -> None:
+        """Raise if an exchange's bounded wait gave up (a peer never arrived)."""
+        if int(self.err.item()):
+            raise _lib.EnxError(5, "peer exchange: a bounded wait for a peer's arrival gave up")
+
+    def close(self) -> None:
+        for p in self.mapped:
+            _lib.load().enx_peer_close(C.c_void_p(p), 1)
+        self.mapped = []
+        if self.own:
+            _lib.load().enx_peer_close(C.c_void_p(self.own), 0)
+            self.own = None
 
 
 def run_distributed(sampler: ShardedSampler, x: ShardInputs, gather: Optional[Callable] = None,

@@ -94,6 +94,25 @@ ENX_API enx_status enx_raw_check(void);
  * already captured included).  No reference counterpart: a hook to exercise the timeout path. */
 ENX_API enx_status enx_set_wait_limit(int device, uint32_t spins);
 
+/* Peer-memory exchange between the GPUs of one box (the vocab-sharded sampler's per-phase
+ * all-gather without a collective library).  enx_peer_alloc allocates an exchange buffer of 512
+ * header bytes + `bytes` on the current device and returns its CUDA IPC handle (64 bytes);
+ * other ranks map it with enx_peer_open (lazy peer access) and unmap it with
+ * enx_peer_close(ptr, 1); the owner frees it with enx_peer_close(ptr, 0).  enx_peer_allgather
+ * copies `bytes` (a multiple of 16, 16-byte aligned) of `send` into slot `rank` of every rank's
+ * buffer (peers: device array of the world buffers' addresses as mapped here, peers[rank] =
+ * this rank's own), raises arrival word `rank` of every buffer to `seq`, and waits (bounded;
+ * *err raised to 4 on giving up) until all arrival words of this rank's buffer reach `seq`; the
+ * gathered region (world x bytes, rank-major) then starts 512 bytes into the own buffer.  `seq`
+ * must grow by one per exchange on every rank.  Replaces the NCCL all_gather_into_tensor of
+ * enargeia_b200/vocab_shard.py's protocol (no reference counterpart: the reference runs on one
+ * device). */
+ENX_API enx_status enx_peer_alloc(size_t bytes, void** ptr, uint8_t* handle);
+ENX_API enx_status enx_peer_open(const uint8_t* handle, void** ptr);
+ENX_API enx_status enx_peer_close(void* ptr, int opened);
+ENX_API enx_status enx_peer_allgather(const void* send, size_t bytes, const unsigned long long* peers, uint32_t world,
+                                      uint32_t rank, unsigned long long seq, uint32_t* err, void* stream);
+
 /* embeddingDims, 48 bytes (src/kernels/embedding_variants.ts:76-90, 207-221). */
 typedef struct {
     uint32_t seq, hidden, row_begin, row_count;

@@ -4,7 +4,9 @@ enx_lm_head_q8 and samples through the NCCL phase exchange.  Rank 0 writes the i
 rank's own ids, which must agree) to the JSON file given as argv[1].
 
     python -m torch.distributed.run --nproc-per-node 2 --master-addr 127.0.0.1 \\
-        tests/dist_vocab_shard.py out.json
+        tests/dist_vocab_shard.py out.json [peer]
+
+With "peer" the phases exchange through enx_peer_allgather (NVLink peer stores) instead of NCCL.
 """
 
 import json
@@ -19,7 +21,7 @@ import torch.distributed as dist
 sys.path.insert(0, str(Path(__file__).resolve().parents[1]))
 
 from enargeia_b200.format import quantize_tensor  # noqa: E402
-from enargeia_b200.vocab_shard import ShardedHead, ShardedSampler, ShardInputs, run_distributed  # noqa: E402
+from enargeia_b200.vocab_shard import PeerGather, ShardedHead, ShardedSampler, ShardInputs, run_distributed  # noqa: E402
 
 VOCAB, HIDDEN, ROWS, HIST = 151936, 896, 8, 2048
 
@@ -46,7 +48,20 @@ def main():
     s = ShardedSampler(VOCAB, rank, world, ROWS, dev)
     hist = torch.from_numpy(history.view(np.int32)).to(dev)
     hlen = torch.full((ROWS,), HIST, dtype=torch.int32, device=dev)
-    ids = run_distributed(s, ShardInputs(logits, hist, hlen, params))
+    logits0 = logits.clone()  # the sampler penalises in place
+    gather = None
+    if len(sys.argv) > 2 and sys.argv[2] == "peer":  # peer-memory exchange instead of NCCL
+        gather = PeerGather(s.max_record_bytes())
+    ids = run_distributed(s, ShardInputs(logits, hist, hlen, params), gather).clone()
+    if gather is not None:
+        torch.cuda.synchronize()
+        gather.check()
+        # a second step through the same buffers (the ring of exchange regions moves on)
+        ids2 = run_distributed(s, ShardInputs(logits0, hist, hlen, params), gather)
+        torch.cuda.synchronize()
+        gather.check()
+        assert torch.equal(ids, ids2), "second exchange step disagrees"
+        gather.close()
     mine = [int(v) for v in ids.cpu().numpy().view(np.uint32)]
     gathered = [None] * world
     dist.all_gather_object(gathered, mine)

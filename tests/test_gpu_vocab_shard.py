@@ -137,7 +137,8 @@ def test_sharded_sampler_edge_shapes(gpu, oracle):
     assert [int(v) for v in outs[0].cpu().numpy()] == want
 
 
-def test_nccl_exchange_across_gpus(gpu, oracle, table, tmp_path):
+@pytest.mark.parametrize("exchange", ["nccl", "peer"])
+def test_exchange_across_gpus(gpu, oracle, table, tmp_path, exchange):
     n = torch.cuda.device_count()
     if n < 2:
         pytest.skip("one GPU: the NCCL exchange runs on a box with two or more (lockstep covers the phases)")
@@ -146,7 +147,7 @@ def test_nccl_exchange_across_gpus(gpu, oracle, table, tmp_path):
     env = dict(os.environ, NCCL_NVLS_ENABLE="0")
     cmd = [sys.executable, "-m", "torch.distributed.run", "--nnodes=1", f"--nproc-per-node={world}",
            "--master-addr", "127.0.0.1", "--master-port", str(29600 + os.getpid() % 300),
-           str(ROOT / "tests" / "dist_vocab_shard.py"), str(out)]
+           str(ROOT / "tests" / "dist_vocab_shard.py"), str(out), exchange]
     r = subprocess.run(cmd, env=env, capture_output=True, text=True, timeout=600)
     assert r.returncode == 0, r.stderr[-3000:]
     res = json.loads(out.read_text())
