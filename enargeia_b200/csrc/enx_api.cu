@@ -966,6 +966,15 @@ static const uint8_t* codes_of(const enx_ctx* c, const QW& w) {
 }
 
 // A projection of m prefill rows: tensor cores for m >= kTcMinTokens, CUDA cores below.
+// out += float(x W^T): the residual add fused into the tensor-core GEMM's output (its epilogue or
+// split-K combine); below the tensor-core size, the projection into tmp and a separate add.
+static cudaError_t proj_add(enx_ctx* c, const float* x, const QW& w, float* out, float* tmp, uint32_t m, uint32_t n,
+                            cudaStream_t st, bool tc, uint8_t* ws, uint32_t* err) {
+    if (tc) return launch_gemm_tc(4, x, w.cols, w, codes_of(c, w), nullptr, out, m, n, 0, ws, err, st, false, out);
+    cudaError_t e = launch_matmul(4, x, w, nullptr, tmp, m, n, 0, st, false);
+    return e == cudaSuccess ? launch_add(out, tmp, out, m * n, st) : e;
+}
+
 static cudaError_t proj(enx_ctx* c, int bits, const float* x, const QW& w, const float* bias, float* out, uint32_t m,
                         uint32_t stride, uint32_t offset, cudaStream_t st, bool same_x = false) {
     if (m >= kTcMinTokens && c->pf_ws && bits == 4 && !codes_of(c, w)) return cudaErrorInvalidValue;  // never prepared
@@ -1048,14 +1057,13 @@ extern "C" enx_status enx_prefill(enx_ctx* c, uint32_t seq, const uint32_t* ids,
             ENX_CUDA(launch_cache_pack(c->pf_k2, c->kcache + S.cache_offset(seq, l, begin), m * kv, 0, st));
             ENX_CUDA(launch_cache_pack(c->pf_v, c->vcache + S.cache_offset(seq, l, begin), m * kv, 0, st));
             ENX_CUDA(launch_attn(S, l, m, c->pf_att, st, false));
-            ENX_CUDA(proj(c, 4, c->pf_att, L.wo, nullptr, c->pf_t, m, H, 0, st));
-            ENX_CUDA(launch_add(c->pf_x, c->pf_t, c->pf_x, m * H, st));
+            const bool tc = m >= kTcMinTokens && c->pf_ws && codes_of(c, L.wo);
+            ENX_CUDA(proj_add(c, c->pf_att, L.wo, c->pf_x, c->pf_t, m, H, st, tc, c->pf_ws, &c->d_step->err));
             ENX_CUDA(launch_rmsnorm(c->pf_x, L.norm_post, c->pf_n, m, H, C.rms_norm_eps, st));
             ENX_CUDA(proj(c, 4, c->pf_n, L.wg, nullptr, c->pf_g, m, I, 0, st));
             ENX_CUDA(proj(c, 4, c->pf_n, L.wu, nullptr, c->pf_u, m, I, 0, st, true));
             ENX_CUDA(launch_silu_mul(c->pf_g, c->pf_u, c->pf_g, m * I, st));
-            ENX_CUDA(proj(c, 4, c->pf_g, L.wd, nullptr, c->pf_t, m, H, 0, st));
-            ENX_CUDA(launch_add(c->pf_x, c->pf_t, c->pf_x, m * H, st));
+            ENX_CUDA(proj_add(c, c->pf_g, L.wd, c->pf_x, c->pf_t, m, H, st, tc, c->pf_ws, &c->d_step->err));
         }
         c->filled[seq] += m;
         if (begin0 + m >= n) {
@@ -1188,14 +1196,13 @@ static cudaError_t batch_body(enx_ctx* c, uint32_t B, cudaStream_t st) {
         if (e == cudaSuccess) e = proj_b(c, 4, c->b_xn, L.wv, L.bv, c->b_v, B, kvd, st, true);
         if (e == cudaSuccess) e = launch_rope_cache_batch(S, l, c->b_q, c->b_k, c->b_v, B, st);
         if (e == cudaSuccess) e = launch_attn(S, l, B, c->b_att, st, false);
-        if (e == cudaSuccess) e = proj_b(c, 4, c->b_att, L.wo, nullptr, c->b_t, B, H, st);
-        if (e == cudaSuccess) e = launch_add(c->b_x, c->b_t, c->b_x, B * H, st);
+        const bool tc = B >= kTcMinTokens && codes_of(c, L.wo);
+        if (e == cudaSuccess) e = proj_add(c, c->b_att, L.wo, c->b_x, c->b_t, B, H, st, tc, c->b_ws, c->d_bb + c->bl.err());
         if (e == cudaSuccess) e = launch_rmsnorm(c->b_x, L.norm_post, c->b_xn, B, H, C.rms_norm_eps, st);
         if (e == cudaSuccess) e = proj_b(c, 4, c->b_xn, L.wg, nullptr, c->b_g, B, I, st);
         if (e == cudaSuccess) e = proj_b(c, 4, c->b_xn, L.wu, nullptr, c->b_u, B, I, st, true);
         if (e == cudaSuccess) e = launch_silu_mul(c->b_g, c->b_u, c->b_g, B * I, st);
-        if (e == cudaSuccess) e = proj_b(c, 4, c->b_g, L.wd, nullptr, c->b_t, B, H, st);
-        if (e == cudaSuccess) e = launch_add(c->b_x, c->b_t, c->b_x, B * H, st);
+        if (e == cudaSuccess) e = proj_add(c, c->b_g, L.wd, c->b_x, c->b_t, B, H, st, tc, c->b_ws, c->d_bb + c->bl.err());
     }
     if (e == cudaSuccess) e = launch_rmsnorm(c->b_x, c->head.norm, c->normed, B, H, C.rms_norm_eps, st);
     if (e == cudaSuccess) e = proj_b(c, c->head.bits, c->normed, c->head.embed, nullptr, c->logits, B, C.vocab, st);
@@ -1254,8 +1261,8 @@ static enx_status batch_profile(enx_ctx* c, uint32_t B, float* ms, uint32_t coun
             }
         }
         if (e == cudaSuccess) e = section(5, [&] {
-            cudaError_t r = proj_b(c, 4, c->b_att, L.wo, nullptr, c->b_t, B, H, st);
-            return r == cudaSuccess ? launch_add(c->b_x, c->b_t, c->b_x, B * H, st) : r;
+            return proj_add(c, c->b_att, L.wo, c->b_x, c->b_t, B, H, st, B >= kTcMinTokens && codes_of(c, L.wo), c->b_ws,
+                            c->d_bb + c->bl.err());
         });
         if (e == cudaSuccess) e = section(1, [&] { return launch_rmsnorm(c->b_x, L.norm_post, c->b_xn, B, H, C.rms_norm_eps, st); });
         if (e == cudaSuccess) e = section(6, [&] {
@@ -1264,8 +1271,8 @@ static enx_status batch_profile(enx_ctx* c, uint32_t B, float* ms, uint32_t coun
             return r == cudaSuccess ? launch_silu_mul(c->b_g, c->b_u, c->b_g, B * I, st) : r;
         });
         if (e == cudaSuccess) e = section(7, [&] {
-            cudaError_t r = proj_b(c, 4, c->b_g, L.wd, nullptr, c->b_t, B, H, st);
-            return r == cudaSuccess ? launch_add(c->b_x, c->b_t, c->b_x, B * H, st) : r;
+            return proj_add(c, c->b_g, L.wd, c->b_x, c->b_t, B, H, st, B >= kTcMinTokens && codes_of(c, L.wd), c->b_ws,
+                            c->d_bb + c->bl.err());
         });
     }
     if (e == cudaSuccess) e = section(1, [&] { return launch_rmsnorm(c->b_x, c->head.norm, c->normed, B, H, C.rms_norm_eps, st); });

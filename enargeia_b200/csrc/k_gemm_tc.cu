@@ -239,8 +239,8 @@ __global__ void k_codes_i8(QW w, uint8_t* __restrict__ out) {
 template <int BITS>
 __global__ void __launch_bounds__(kTcWsThreads, 1)
     k_gemm_tc(const __grid_constant__ CUtensorMap cmap, const uint8_t* __restrict__ limbs, QW w,
-              const float* __restrict__ bias, float* __restrict__ out, double* __restrict__ partial, uint32_t M,
-              uint32_t out_stride, uint32_t out_offset, uint32_t blocks_per_split, uint32_t* err) {
+              const float* __restrict__ bias, float* out, double* __restrict__ partial, uint32_t M,
+              uint32_t out_stride, uint32_t out_offset, uint32_t blocks_per_split, uint32_t* err, const float* residual) {
     extern __shared__ __align__(1024) uint8_t smem[];
     uint8_t* sA = smem;                                // [stages][kTcATile]
     uint8_t* sB = smem + kTcStages * kTcATile;         // [stages][kTcLimbTileBytes]
@@ -402,7 +402,13 @@ __global__ void __launch_bounds__(kTcWsThreads, 1)
 #pragma unroll
                 for (int tt = 0; tt < kTcEpiTok; ++tt) {
                     const uint32_t m = g * kTcTokens + wg * kTcEpiTok + tt;
-                    if (m < M) out[(size_t)m * out_stride + out_offset + grow] = (float)(acc[tt] + bv);
+                    if (m < M) {
+                        // with a residual: the projection rounded to float, then the float add of the
+                        // reference's separate add kernel (test/reference/ops.ts:219-225)
+                        const size_t o = (size_t)m * out_stride + out_offset + grow;
+                        const float v = (float)(acc[tt] + bv);
+                        out[o] = residual ? residual[o] + v : v;
+                    }
                 }
             }
         }
@@ -421,15 +427,16 @@ cudaError_t tc_set_spin(uint32_t spins) {
 
 // Split-K: out = float(sum of the splits' partials in split order + bias).
 __global__ void k_gemm_tc_combine(const double* __restrict__ partial, uint32_t splits, uint32_t M, uint32_t N,
-                                  const float* __restrict__ bias, float* __restrict__ out, uint32_t out_stride,
-                                  uint32_t out_offset) {
+                                  const float* __restrict__ bias, float* out, uint32_t out_stride,
+                                  uint32_t out_offset, const float* residual) {
     const size_t i = (size_t)blockIdx.x * blockDim.x + threadIdx.x;
     if (i >= (size_t)M * N) return;
     const uint32_t m = (uint32_t)(i / N), n = (uint32_t)(i % N);
     double acc = 0.0;
     for (uint32_t s = 0; s < splits; ++s) acc += partial[(size_t)s * M * N + i];
     if (bias) acc += (double)__ldg(bias + n);
-    out[(size_t)m * out_stride + out_offset + n] = (float)acc;
+    const size_t o = (size_t)m * out_stride + out_offset + n;
+    out[o] = residual ? residual[o] + (float)acc : (float)acc;
 }
 
 // Splits of the reduction axis: the count that minimises the modelled time waves(s) * (blocks
@@ -496,7 +503,7 @@ static EncodeTiledFn encode_tiled() {
 
 cudaError_t launch_gemm_tc(int bits, const float* x, uint32_t ld, const QW& w, const uint8_t* codes8, const float* bias,
                            float* out, uint32_t m, uint32_t out_stride, uint32_t out_offset, uint8_t* workspace,
-                           uint32_t* err, cudaStream_t st, bool limbs_ready) {
+                           uint32_t* err, cudaStream_t st, bool limbs_ready, const float* residual) {
     const uint32_t groups = (m + kTcTokens - 1) / kTcTokens, nb = w.cols / kBlock;
     cudaError_t e;
     if (bits == 8) {
@@ -548,18 +555,18 @@ cudaError_t launch_gemm_tc(int bits, const float* x, uint32_t ld, const QW& w, c
         e = cudaFuncSetAttribute(k_gemm_tc<4>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
         if (e == cudaSuccess)
             e = cudaLaunchKernelEx(&cfg, k_gemm_tc<4>, cmap, (const uint8_t*)workspace, w, bias, out, partial, m,
-                                   out_stride, out_offset, per, err);
+                                   out_stride, out_offset, per, err, residual);
     } else {
         e = cudaFuncSetAttribute(k_gemm_tc<8>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
         if (e == cudaSuccess)
             e = cudaLaunchKernelEx(&cfg, k_gemm_tc<8>, cmap, (const uint8_t*)workspace, w, bias, out, partial, m,
-                                   out_stride, out_offset, per, err);
+                                   out_stride, out_offset, per, err, residual);
     }
     if (e == cudaSuccess) e = cudaGetLastError();
     if (e != cudaSuccess || splits == 1) return e;
     const size_t total = (size_t)m * w.rows;
     k_gemm_tc_combine<<<(unsigned)((total + 255) / 256), 256, 0, st>>>(partial, splits, m, w.rows, bias, out, out_stride,
-                                                                       out_offset);
+                                                                       out_offset, residual);
     return cudaGetLastError();
 }
 

@@ -25,9 +25,10 @@ cudaError_t launch_codes_i8(const QW& w, uint8_t* out, cudaStream_t st);
 // matrix, or null to convert into the workspace (which then needs gemm_tc_codes_bytes more).
 // *err is raised to 3 if a bounded wait inside the kernel gives up.  limbs_ready: the previous
 // call on this workspace had the same x, ld, m and w.cols, so its activation limbs are reused.
+// residual: added in float to each rounded output (same layout as out; may be out itself).
 cudaError_t launch_gemm_tc(int bits, const float* x, uint32_t ld, const QW& w, const uint8_t* codes8, const float* bias,
                            float* out, uint32_t m, uint32_t out_stride, uint32_t out_offset, uint8_t* workspace,
-                           uint32_t* err, cudaStream_t st, bool limbs_ready = false);
+                           uint32_t* err, cudaStream_t st, bool limbs_ready = false, const float* residual = nullptr);
 
 // The tied int8 head for 1-4 tokens on the tensor cores (exact limbs, like launch_gemm_tc):
 // out[t * out_stride + row] = float(x_t . W[row]) for row < w.rows, t < ntok; with `gain`, x is
