@@ -56,19 +56,6 @@ __device__ __forceinline__ void csync() {
 // 2^52 + v as a double (0 <= v < 2^32): (2^52 + q) - (2^52 + z) is exactly q - z.
 __device__ __forceinline__ double magic_d(uint32_t v) { return __hiloint2double(0x43300000, (int)v); }
 
-// Exact f16 -> double by bit manipulation (the conversion instructions are a slow path): the half
-// exponent is rebiased into the double one and the 10 mantissa bits move to the top of the double
-// mantissa; zero/subnormal halves are m * 2^-24.
-__device__ __forceinline__ double half_bits_to_double(uint32_t b) {
-    const uint32_t sgn = (b & 0x8000u) << 16, e = (b >> 10) & 0x1Fu, m = b & 0x3FFu;
-    if (e == 0) {
-        const double v = (magic_d(m) - 4503599627370496.0) * 0x1p-24;
-        return sgn ? -v : v;
-    }
-    const uint32_t ed = e == 31 ? 0x7FFu : e + 1008u;
-    return __hiloint2double((int)(sgn | (ed << 20) | (m << 10)), 0);
-}
-
 // Chunk-transposed index of element k of token t.
 template <int BITS>
 __device__ __forceinline__ uint32_t xd_index(uint32_t t, uint32_t k, uint32_t nchunk) {

@@ -432,6 +432,9 @@ __device__ void attend(const MegaArgs& A, uint32_t l, uint32_t t, uint32_t g, ui
     const uint16_t* Kc = A.S.kcache + base;
     const uint16_t* Vc = A.S.vcache + base;
     const double scale = 1.0 / sqrt((double)hd);
+    // f16 -> f32 -> double through the conversion units: exact, and in this loop (few
+    // conversions per loaded byte, integer pipe busy with addressing) faster than bit moves
+    auto h2d = [](uint16_t v) { return (double)__half2float(__ushort_as_half(v)); };
     const uint32_t lr8 = hd == 64 ? 3 : 2;  // row8 = 1 << lr8 (head_dim 32 or 64)
     auto stage_rows = [&](uint16_t* st, const uint16_t* src, const uint16_t* cur, uint32_t j0, uint32_t n) {
         for (uint32_t i = tid; i < (n << lr8); i += kMConsumers) {
@@ -455,7 +458,7 @@ __device__ void attend(const MegaArgs& A, uint32_t l, uint32_t t, uint32_t g, ui
             double acc = 0.0;
             if (j < n) {
                 const uint16_t* kr = kst + (size_t)j * hd + sub * row8;
-                for (uint32_t d = 0; d < row8; ++d) acc = fma(hs.qd[sub * row8 + d], half_bits_to_double(kr[d]), acc);
+                for (uint32_t d = 0; d < row8; ++d) acc = fma(hs.qd[sub * row8 + d], h2d(kr[d]), acc);
             }
             acc += __shfl_xor_sync(0xffffffffu, acc, 1);
             acc += __shfl_xor_sync(0xffffffffu, acc, 2);
@@ -500,10 +503,10 @@ __device__ void attend(const MegaArgs& A, uint32_t l, uint32_t t, uint32_t g, ui
         if (slice < S) {
             uint32_t j = slice;
             for (; j + S < n; j += 2 * S) {
-                a0 = fma(pw[j0 + j], half_bits_to_double(vst[(size_t)j * hd + d]), a0);
-                a1 = fma(pw[j0 + j + S], half_bits_to_double(vst[(size_t)(j + S) * hd + d]), a1);
+                a0 = fma(pw[j0 + j], h2d(vst[(size_t)j * hd + d]), a0);
+                a1 = fma(pw[j0 + j + S], h2d(vst[(size_t)(j + S) * hd + d]), a1);
             }
-            if (j < n) a0 = fma(pw[j0 + j], half_bits_to_double(vst[(size_t)j * hd + d]), a0);
+            if (j < n) a0 = fma(pw[j0 + j], h2d(vst[(size_t)j * hd + d]), a0);
         }
     }
     cbar();
