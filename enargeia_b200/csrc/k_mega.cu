@@ -832,16 +832,55 @@ __global__ void __launch_bounds__(kMThreads, 1) k_mega(const __grid_constant__ M
             if (D.nrange) {
                 const MegaRange& Rg = D.range[0];
                 const MegaRange& Ru = D.range[1];
-                const uint32_t nr = Rg.r1 - Rg.r0;
-                for (uint32_t i = warp; i < nr; i += kMWarps) {  // gate row i with up row i
-                    double acc[2][MT];
-                    row_dot2<4, MT>(slot, Rg, Rg.r0 + i, Ru, Ru.r0 + i, H, XD, xsum, H / 32, lane, acc);
-                    if (lane == 0)
+                const uint32_t nr = Rg.r1 - Rg.r0, nchunk = H / 32;
+                if (MT == 1 && 2 * nr * nchunk * MT <= kKvHalfs / 4) {
+                    // (row pair, chunk) units spread over every consumer thread: 33 rows of 28
+                    // chunks take 2 rounds instead of 3 warp-per-row rounds with 28 of 32 lanes.
+                    // Partials land in the K/V staging area (free in this stage) and are summed
+                    // per row in chunk order.
+                    double* part = reinterpret_cast<double*>(kst);  // [2][nr][nchunk][MT]
+                    const uint32_t bpr = H / kBlock;
+                    const uint32_t* zg = reinterpret_cast<const uint32_t*>(slot + Rg.off_z);
+                    const uint32_t* zu = reinterpret_cast<const uint32_t*>(slot + Ru.off_z);
+                    for (uint32_t u = tid; u < nr * nchunk; u += kMConsumers) {
+                        const uint32_t i = u / nchunk, c = u % nchunk;
+                        const uint32_t bg = (Rg.r0 + i) * bpr + c / Geom<4>::CPB, bu = (Ru.r0 + i) * bpr + c / Geom<4>::CPB;
+                        const uint4 q[2] = {(reinterpret_cast<const uint4*>(slot + Rg.off_p) + (size_t)i * nchunk)[c],
+                                            (reinterpret_cast<const uint4*>(slot + Ru.off_p) + (size_t)i * nchunk)[c]};
+                        const float sv[2] = {reinterpret_cast<const float*>(slot + Rg.off_s)[bg - Rg.s_base],
+                                             reinterpret_cast<const float*>(slot + Ru.off_s)[bu - Ru.s_base]};
+                        const uint32_t zc[2] = {(zg[(bg >> 3) - Rg.z_base] >> ((bg & 7u) * 4u)) & 0xFu,
+                                                (zu[(bu >> 3) - Ru.z_base] >> ((bu & 7u) * 4u)) & 0xFu};
+                        double a[2][MT];
 #pragma unroll
-                        for (int t = 0; t < MT; ++t) {
-                            res[i * MT + t] = acc[0][t];
-                            res[(nr + i) * MT + t] = acc[1][t];
-                        }
+                        for (int r = 0; r < 2; ++r)
+#pragma unroll
+                            for (int t = 0; t < MT; ++t) a[r][t] = 0.0;
+                        chunk_dot_b<4, MT, 2>(q, sv, zc, XD, xsum, nchunk, c, a);
+#pragma unroll
+                        for (int r = 0; r < 2; ++r)
+#pragma unroll
+                            for (int t = 0; t < MT; ++t) part[(((size_t)r * nr + i) * nchunk + c) * MT + t] = a[r][t];
+                    }
+                    cbar();
+                    for (uint32_t e = tid; e < 2 * nr * MT; e += kMConsumers) {
+                        const uint32_t ri = e / MT, t = e % MT;  // ri = r * nr + i
+                        const double* pp = part + (size_t)ri * nchunk * MT + t;
+                        double v = 0.0;
+                        for (uint32_t c = 0; c < nchunk; ++c) v += pp[(size_t)c * MT];  // chunk order
+                        res[ri * MT + t] = v;
+                    }
+                } else {
+                    for (uint32_t i = warp; i < nr; i += kMWarps) {  // gate row i with up row i
+                        double acc[2][MT];
+                        row_dot2<4, MT>(slot, Rg, Rg.r0 + i, Ru, Ru.r0 + i, H, XD, xsum, nchunk, lane, acc);
+                        if (lane == 0)
+#pragma unroll
+                            for (int t = 0; t < MT; ++t) {
+                                res[i * MT + t] = acc[0][t];
+                                res[(nr + i) * MT + t] = acc[1][t];
+                            }
+                    }
                 }
                 cbar();
                 stamp_a(A, l, 12);
