@@ -631,17 +631,16 @@ __global__ void __launch_bounds__(kMThreads, 1) k_mega(const __grid_constant__ M
 
     // ---------------- consumers ---------------------------------------------------------------
     uint32_t slice = 0;
-    // Thread 0 alone waits (bounded) so that every consumer takes the same branch; the others
-    // then observe the completed phase themselves, which orders the copied bytes before their reads.
+    // Thread 0 alone waits (bounded) so that every consumer takes the same branch.  Its wait
+    // acquires the completed phase (the copied bytes); the barrier after it carries that order to
+    // every other consumer, so they read the slot without polling the mbarrier themselves.
     auto wait_slice = [&]() -> bool {
         if (tid == 0 && !mbar_wait_bounded(full + slice % NS, (slice / NS) & 1u, spin)) {
             atomicMax(A.err, 2u);
             s_fail = 1;
         }
         cbar();
-        if (s_fail) return false;
-        if (tid != 0) mbar_wait_bounded(full + slice % NS, (slice / NS) & 1u, spin);
-        return true;
+        return !s_fail;
     };
     auto release_slice = [&]() {
         cbar();  // every consumer is done with this slot
@@ -901,6 +900,7 @@ __global__ void __launch_bounds__(kMThreads, 1) k_mega(const __grid_constant__ M
             const bool ok = ll_read(V.gated(l), MT * I, tag, spin, A.err,
                                     [&](uint32_t i, uint32_t v) { Xd[xd_index<4>(i / I, i % I, nchunk)] = (double)__uint_as_float(v); });
             if (!ll_done(ok)) BAIL();
+            stamp_a(A, l, 13);
             stage_xsum<4, MT>(Xd, xsum, nchunk);
         }
         if (!wait_slice()) BAIL();
