@@ -328,7 +328,7 @@ class OracleModel:
 
     def __del__(self):
         h = getattr(self, "_h", None)
-        if h:
+        if h and lib is not None:  # at interpreter shutdown the module's globals may already be gone
             lib().orc_model_destroy(h)
             self._h = None
 
