@@ -498,7 +498,14 @@ struct enx_ctx {
     uint32_t* b_ids = nullptr;
     uint8_t* b_ws = nullptr;
     // int4 projection weights as the byte matrices (q - z) the tensor-core GEMM reads, by packed pointer
-    std::map<const uint32_t*, uint8_t*> codes8;
+    std::map<const uint32_t*, uint8_t*> codes8;  // int8 code matrix of each int4 projection (may alias a stack)
+    std::vector<void*> codes8_bufs;                // the allocations behind codes8 and the stacks' scales
+    struct Stacked {
+        QW qkv, gu;               // q|k|v and gate|up rows one after another (stacked scales)
+        const uint8_t* qkv_codes;
+        const uint8_t* gu_codes;
+    };
+    std::vector<Stacked> stacked;  // per layer, with codes8
     std::map<uint32_t, cudaGraphExec_t> b_graph, b_loop_graph;
     std::map<uint32_t, uint32_t> b_launches;
     bool loop_batched = false;  // the last enx_decode_loop ran the batched path
@@ -692,7 +699,7 @@ extern "C" enx_status enx_destroy(enx_ctx* c) {
         if (c->stream) cudaStreamSynchronize(c->stream);
         free_kv(c);
         dfree(c->d_trace);
-        for (auto& kv : c->codes8) cudaFree(kv.second);
+        for (void* b : c->codes8_bufs) cudaFree(b);
         if (c->arena) cudaFree(c->arena);
         if (c->stream) cudaStreamDestroy(c->stream);
     }
@@ -769,8 +776,10 @@ extern "C" enx_status enx_load_enargeia_memory(enx_ctx* c, const void* data, siz
     }
     DeviceGuard g(c->device);
     if (c->arena) { cudaFree(c->arena); c->arena = nullptr; }
-    for (auto& kv : c->codes8) cudaFree(kv.second);
+    for (void* b : c->codes8_bufs) cudaFree(b);
+    c->codes8_bufs.clear();
     c->codes8.clear();
+    c->stacked.clear();
     c->tensors.clear();
     c->loaded = false;
     free_graphs(c);
@@ -944,20 +953,78 @@ static StepArgs step_args(enx_ctx* c) {
 }
 
 // The byte matrices of every int4 projection weight for the tensor-core GEMM, prepared once
-// (before any graph capture) and reused by prefill and batched decode.
+// (before any graph capture) and reused by prefill and batched decode.  q|k|v and gate|up share
+// their input, so their matrices are laid out one after another (with a stacked copy of their
+// scales) and each runs as one GEMM over the stack; the single weights' code pointers point into
+// the stack.
 static enx_status ensure_codes8(enx_ctx* c) {
     if (!c->codes8.empty()) return ENX_OK;
-    for (const LayerArgs& L : c->layers) {
-        for (const QW* w : {&L.wq, &L.wk, &L.wv, &L.wo, &L.wg, &L.wu, &L.wd}) {
+    auto stack = [&](std::initializer_list<const QW*> ws, QW& sw, const uint8_t*& codes) -> enx_status {
+        uint32_t rows = 0;
+        const uint32_t K = (*ws.begin())->cols, bpr = K / kBlock;
+        for (const QW* w : ws) rows += w->rows;
+        uint8_t* buf = nullptr;
+        float* sc = nullptr;
+        ENX_TRY(dalloc(&buf, gemm_tc_codes_bytes(rows, K), "GEMM code matrix"));
+        c->codes8_bufs.push_back(buf);
+        ENX_TRY(dalloc(&sc, (size_t)rows * bpr, "GEMM stacked scales"));
+        c->codes8_bufs.push_back(sc);
+        uint32_t r = 0;
+        for (const QW* w : ws) {
+            c->codes8[w->packed] = buf + (size_t)r * K;
+            ENX_CUDA(launch_codes_i8(*w, buf + (size_t)r * K, c->stream));
+            ENX_CUDA(cudaMemcpyAsync(sc + (size_t)r * bpr, w->scales, (size_t)w->rows * bpr * 4, cudaMemcpyDeviceToDevice,
+                                     c->stream));
+            r += w->rows;
+        }
+        sw = QW{nullptr, sc, nullptr, rows, K};
+        codes = buf;
+        return ENX_OK;
+    };
+    c->stacked.assign(c->layers.size(), enx_ctx::Stacked{});
+    for (size_t l = 0; l < c->layers.size(); ++l) {
+        const LayerArgs& L = c->layers[l];
+        enx_ctx::Stacked& S = c->stacked[l];
+        ENX_TRY(stack({&L.wq, &L.wk, &L.wv}, S.qkv, S.qkv_codes));
+        ENX_TRY(stack({&L.wg, &L.wu}, S.gu, S.gu_codes));
+        for (const QW* w : {&L.wo, &L.wd}) {
             if (c->codes8.count(w->packed)) continue;
             uint8_t* buf = nullptr;
             ENX_TRY(dalloc(&buf, gemm_tc_codes_bytes(w->rows, w->cols), "GEMM code matrix"));
+            c->codes8_bufs.push_back(buf);
             c->codes8[w->packed] = buf;
             ENX_CUDA(launch_codes_i8(*w, buf, c->stream));
         }
     }
     ENX_CUDA(cudaStreamSynchronize(c->stream));
     return ENX_OK;
+}
+
+// One tensor-core GEMM over layer l's q|k|v stack (outputs q, k, v with their biases) or its
+// gate|up stack (outputs g, u): the stacked rows' input is normalised x, m rows.
+static cudaError_t proj_qkv(enx_ctx* c, uint32_t l, const float* x, float* q, float* k, float* v, uint32_t m,
+                            uint8_t* ws, uint32_t* err, cudaStream_t st) {
+    const LayerArgs& L = c->layers[l];
+    const uint32_t H = L.wq.rows, kv = L.wk.rows;
+    TcSeg seg{};
+    seg.out[0] = q, seg.out[1] = k, seg.out[2] = v;
+    seg.bias[0] = L.bq, seg.bias[1] = L.bk, seg.bias[2] = L.bv;
+    seg.stride[0] = H, seg.stride[1] = kv, seg.stride[2] = kv;
+    seg.end[0] = H, seg.end[1] = H + kv, seg.end[2] = H + 2 * kv;
+    seg.n = 3;
+    const enx_ctx::Stacked& S = c->stacked[l];
+    return launch_gemm_tc(4, x, S.qkv.cols, S.qkv, S.qkv_codes, nullptr, nullptr, m, 0, 0, ws, err, st, false, nullptr, &seg);
+}
+static cudaError_t proj_gu(enx_ctx* c, uint32_t l, const float* x, float* g, float* u, uint32_t m, uint8_t* ws,
+                           uint32_t* err, cudaStream_t st) {
+    const uint32_t I = c->layers[l].wg.rows;
+    TcSeg seg{};
+    seg.out[0] = g, seg.out[1] = u;
+    seg.stride[0] = I, seg.stride[1] = I;
+    seg.end[0] = I, seg.end[1] = 2 * I;
+    seg.n = 2;
+    const enx_ctx::Stacked& S = c->stacked[l];
+    return launch_gemm_tc(4, x, S.gu.cols, S.gu, S.gu_codes, nullptr, nullptr, m, 0, 0, ws, err, st, false, nullptr, &seg);
 }
 
 static const uint8_t* codes_of(const enx_ctx* c, const QW& w) {
@@ -1049,9 +1116,14 @@ extern "C" enx_status enx_prefill(enx_ctx* c, uint32_t seq, const uint32_t* ids,
         for (uint32_t l = 0; l < C.layers; ++l) {
             const LayerArgs& L = c->layers[l];
             ENX_CUDA(launch_rmsnorm(c->pf_x, L.norm_in, c->pf_n, m, H, C.rms_norm_eps, st));
-            ENX_CUDA(proj(c, 4, c->pf_n, L.wq, L.bq, c->pf_q, m, H, 0, st));
-            ENX_CUDA(proj(c, 4, c->pf_n, L.wk, L.bk, c->pf_k, m, kv, 0, st, true));  // limbs of pf_n reused
-            ENX_CUDA(proj(c, 4, c->pf_n, L.wv, L.bv, c->pf_v, m, kv, 0, st, true));
+            const bool stk = m >= kTcMinTokens && c->pf_ws && l < c->stacked.size();  // one GEMM over q|k|v
+            if (stk) {
+                ENX_CUDA(proj_qkv(c, l, c->pf_n, c->pf_q, c->pf_k, c->pf_v, m, c->pf_ws, &c->d_step->err, st));
+            } else {
+                ENX_CUDA(proj(c, 4, c->pf_n, L.wq, L.bq, c->pf_q, m, H, 0, st));
+                ENX_CUDA(proj(c, 4, c->pf_n, L.wk, L.bk, c->pf_k, m, kv, 0, st, true));  // limbs of pf_n reused
+                ENX_CUDA(proj(c, 4, c->pf_n, L.wv, L.bv, c->pf_v, m, kv, 0, st, true));
+            }
             ENX_CUDA(launch_rope_d(c->pf_q, c->pf_q2, c->rope_cos, c->rope_sin, m, C.heads, C.head_dim, begin, 0, st));
             ENX_CUDA(launch_rope_d(c->pf_k, c->pf_k2, c->rope_cos, c->rope_sin, m, C.kv_heads, C.head_dim, begin, 0, st));
             ENX_CUDA(launch_cache_pack(c->pf_k2, c->kcache + S.cache_offset(seq, l, begin), m * kv, 0, st));
@@ -1060,8 +1132,12 @@ extern "C" enx_status enx_prefill(enx_ctx* c, uint32_t seq, const uint32_t* ids,
             const bool tc = m >= kTcMinTokens && c->pf_ws && codes_of(c, L.wo);
             ENX_CUDA(proj_add(c, c->pf_att, L.wo, c->pf_x, c->pf_t, m, H, st, tc, c->pf_ws, &c->d_step->err));
             ENX_CUDA(launch_rmsnorm(c->pf_x, L.norm_post, c->pf_n, m, H, C.rms_norm_eps, st));
-            ENX_CUDA(proj(c, 4, c->pf_n, L.wg, nullptr, c->pf_g, m, I, 0, st));
-            ENX_CUDA(proj(c, 4, c->pf_n, L.wu, nullptr, c->pf_u, m, I, 0, st, true));
+            if (stk) {
+                ENX_CUDA(proj_gu(c, l, c->pf_n, c->pf_g, c->pf_u, m, c->pf_ws, &c->d_step->err, st));
+            } else {
+                ENX_CUDA(proj(c, 4, c->pf_n, L.wg, nullptr, c->pf_g, m, I, 0, st));
+                ENX_CUDA(proj(c, 4, c->pf_n, L.wu, nullptr, c->pf_u, m, I, 0, st, true));
+            }
             ENX_CUDA(launch_silu_mul(c->pf_g, c->pf_u, c->pf_g, m * I, st));
             ENX_CUDA(proj_add(c, c->pf_g, L.wd, c->pf_x, c->pf_t, m, H, st, tc, c->pf_ws, &c->d_step->err));
         }
@@ -1191,16 +1267,19 @@ static cudaError_t batch_body(enx_ctx* c, uint32_t B, cudaStream_t st) {
     for (uint32_t l = 0; l < C.layers && e == cudaSuccess; ++l) {
         const LayerArgs& L = c->layers[l];
         e = launch_rmsnorm(c->b_x, L.norm_in, c->b_xn, B, H, C.rms_norm_eps, st);
-        if (e == cudaSuccess) e = proj_b(c, 4, c->b_xn, L.wq, L.bq, c->b_q, B, H, st);
-        if (e == cudaSuccess) e = proj_b(c, 4, c->b_xn, L.wk, L.bk, c->b_k, B, kvd, st, true);  // limbs of b_xn reused
-        if (e == cudaSuccess) e = proj_b(c, 4, c->b_xn, L.wv, L.bv, c->b_v, B, kvd, st, true);
+        const bool stk = B >= kTcMinTokens && l < c->stacked.size();  // one GEMM over q|k|v, one over gate|up
+        if (e == cudaSuccess && stk) e = proj_qkv(c, l, c->b_xn, c->b_q, c->b_k, c->b_v, B, c->b_ws, c->d_bb + c->bl.err(), st);
+        if (e == cudaSuccess && !stk) e = proj_b(c, 4, c->b_xn, L.wq, L.bq, c->b_q, B, H, st);
+        if (e == cudaSuccess && !stk) e = proj_b(c, 4, c->b_xn, L.wk, L.bk, c->b_k, B, kvd, st, true);  // limbs of b_xn reused
+        if (e == cudaSuccess && !stk) e = proj_b(c, 4, c->b_xn, L.wv, L.bv, c->b_v, B, kvd, st, true);
         if (e == cudaSuccess) e = launch_rope_cache_batch(S, l, c->b_q, c->b_k, c->b_v, B, st);
         if (e == cudaSuccess) e = launch_attn(S, l, B, c->b_att, st, false);
         const bool tc = B >= kTcMinTokens && codes_of(c, L.wo);
         if (e == cudaSuccess) e = proj_add(c, c->b_att, L.wo, c->b_x, c->b_t, B, H, st, tc, c->b_ws, c->d_bb + c->bl.err());
         if (e == cudaSuccess) e = launch_rmsnorm(c->b_x, L.norm_post, c->b_xn, B, H, C.rms_norm_eps, st);
-        if (e == cudaSuccess) e = proj_b(c, 4, c->b_xn, L.wg, nullptr, c->b_g, B, I, st);
-        if (e == cudaSuccess) e = proj_b(c, 4, c->b_xn, L.wu, nullptr, c->b_u, B, I, st, true);
+        if (e == cudaSuccess && stk) e = proj_gu(c, l, c->b_xn, c->b_g, c->b_u, B, c->b_ws, c->d_bb + c->bl.err(), st);
+        if (e == cudaSuccess && !stk) e = proj_b(c, 4, c->b_xn, L.wg, nullptr, c->b_g, B, I, st);
+        if (e == cudaSuccess && !stk) e = proj_b(c, 4, c->b_xn, L.wu, nullptr, c->b_u, B, I, st, true);
         if (e == cudaSuccess) e = launch_silu_mul(c->b_g, c->b_u, c->b_g, B * I, st);
         if (e == cudaSuccess) e = proj_add(c, c->b_g, L.wd, c->b_x, c->b_t, B, H, st, tc, c->b_ws, c->d_bb + c->bl.err());
     }
@@ -1246,6 +1325,8 @@ static enx_status batch_profile(enx_ctx* c, uint32_t B, float* ms, uint32_t coun
         const LayerArgs& L = c->layers[l];
         e = section(1, [&] { return launch_rmsnorm(c->b_x, L.norm_in, c->b_xn, B, H, C.rms_norm_eps, st); });
         if (e == cudaSuccess) e = section(2, [&] {
+            if (B >= kTcMinTokens && l < c->stacked.size())
+                return proj_qkv(c, l, c->b_xn, c->b_q, c->b_k, c->b_v, B, c->b_ws, c->d_bb + c->bl.err(), st);
             cudaError_t r = proj_b(c, 4, c->b_xn, L.wq, L.bq, c->b_q, B, H, st);
             if (r == cudaSuccess) r = proj_b(c, 4, c->b_xn, L.wk, L.bk, c->b_k, B, kvd, st, true);
             return r == cudaSuccess ? proj_b(c, 4, c->b_xn, L.wv, L.bv, c->b_v, B, kvd, st, true) : r;
@@ -1266,8 +1347,13 @@ static enx_status batch_profile(enx_ctx* c, uint32_t B, float* ms, uint32_t coun
         });
         if (e == cudaSuccess) e = section(1, [&] { return launch_rmsnorm(c->b_x, L.norm_post, c->b_xn, B, H, C.rms_norm_eps, st); });
         if (e == cudaSuccess) e = section(6, [&] {
-            cudaError_t r = proj_b(c, 4, c->b_xn, L.wg, nullptr, c->b_g, B, I, st);
-            if (r == cudaSuccess) r = proj_b(c, 4, c->b_xn, L.wu, nullptr, c->b_u, B, I, st, true);
+            cudaError_t r = cudaSuccess;
+            if (B >= kTcMinTokens && l < c->stacked.size()) {
+                r = proj_gu(c, l, c->b_xn, c->b_g, c->b_u, B, c->b_ws, c->d_bb + c->bl.err(), st);
+            } else {
+                r = proj_b(c, 4, c->b_xn, L.wg, nullptr, c->b_g, B, I, st);
+                if (r == cudaSuccess) r = proj_b(c, 4, c->b_xn, L.wu, nullptr, c->b_u, B, I, st, true);
+            }
             return r == cudaSuccess ? launch_silu_mul(c->b_g, c->b_u, c->b_g, B * I, st) : r;
         });
         if (e == cudaSuccess) e = section(7, [&] {

@@ -240,7 +240,8 @@ template <int BITS>
 __global__ void __launch_bounds__(kTcWsThreads, 1)
     k_gemm_tc(const __grid_constant__ CUtensorMap cmap, const uint8_t* __restrict__ limbs, QW w,
               const float* __restrict__ bias, float* out, double* __restrict__ partial, uint32_t M,
-              uint32_t out_stride, uint32_t out_offset, uint32_t blocks_per_split, uint32_t* err, const float* residual) {
+              uint32_t out_stride, uint32_t out_offset, uint32_t blocks_per_split, uint32_t* err, const float* residual,
+              TcSeg seg) {
     extern __shared__ __align__(1024) uint8_t smem[];
     uint8_t* sA = smem;                                // [stages][kTcATile]
     uint8_t* sB = smem + kTcStages * kTcATile;         // [stages][kTcLimbTileBytes]
@@ -398,16 +399,28 @@ __global__ void __launch_bounds__(kTcWsThreads, 1)
                     if (m < M) pp[(size_t)m * w.rows + grow] = acc[tt];
                 }
             } else {
-                const double bv = bias ? (double)__ldg(bias + grow) : 0.0;
+                // this row's output: the single one, or its segment of a stacked weight
+                float* o_ptr = out;
+                const float* b_ptr = bias;
+                uint32_t o_stride = out_stride, o_col = out_offset + grow, b_row = grow;
+                if (BITS == 4 && seg.n) {  // stacked weights are int4 projections
+                    const bool s0 = grow < seg.end[0], s1 = !s0 && grow < seg.end[1];  // static picks: no local copy
+                    const uint32_t sb = s0 ? 0 : (s1 ? seg.end[0] : seg.end[1]);
+                    o_ptr = s0 ? seg.out[0] : (s1 ? seg.out[1] : seg.out[2]);
+                    b_ptr = s0 ? seg.bias[0] : (s1 ? seg.bias[1] : seg.bias[2]);
+                    o_stride = s0 ? seg.stride[0] : (s1 ? seg.stride[1] : seg.stride[2]);
+                    o_col = b_row = grow - sb;
+                }
+                const double bv = b_ptr ? (double)__ldg(b_ptr + b_row) : 0.0;
 #pragma unroll
                 for (int tt = 0; tt < kTcEpiTok; ++tt) {
                     const uint32_t m = g * kTcTokens + wg * kTcEpiTok + tt;
                     if (m < M) {
                         // with a residual: the projection rounded to float, then the float add of the
                         // reference's separate add kernel (test/reference/ops.ts:219-225)
-                        const size_t o = (size_t)m * out_stride + out_offset + grow;
+                        const size_t o = (size_t)m * o_stride + o_col;
                         const float v = (float)(acc[tt] + bv);
-                        out[o] = residual ? residual[o] + v : v;
+                        o_ptr[o] = residual ? residual[o] + v : v;
                     }
                 }
             }
@@ -428,15 +441,26 @@ cudaError_t tc_set_spin(uint32_t spins) {
 // Split-K: out = float(sum of the splits' partials in split order + bias).
 __global__ void k_gemm_tc_combine(const double* __restrict__ partial, uint32_t splits, uint32_t M, uint32_t N,
                                   const float* __restrict__ bias, float* out, uint32_t out_stride,
-                                  uint32_t out_offset, const float* residual) {
+                                  uint32_t out_offset, const float* residual, TcSeg seg) {
     const size_t i = (size_t)blockIdx.x * blockDim.x + threadIdx.x;
     if (i >= (size_t)M * N) return;
     const uint32_t m = (uint32_t)(i / N), n = (uint32_t)(i % N);
     double acc = 0.0;
     for (uint32_t s = 0; s < splits; ++s) acc += partial[(size_t)s * M * N + i];
-    if (bias) acc += (double)__ldg(bias + n);
-    const size_t o = (size_t)m * out_stride + out_offset + n;
-    out[o] = residual ? residual[o] + (float)acc : (float)acc;
+    float* o_ptr = out;
+    const float* b_ptr = bias;
+    uint32_t o_stride = out_stride, o_col = out_offset + n, b_row = n;
+    if (seg.n) {  // the row's segment of a stacked weight
+        const bool s0 = n < seg.end[0], s1 = !s0 && n < seg.end[1];
+        const uint32_t sb = s0 ? 0 : (s1 ? seg.end[0] : seg.end[1]);
+        o_ptr = s0 ? seg.out[0] : (s1 ? seg.out[1] : seg.out[2]);
+        b_ptr = s0 ? seg.bias[0] : (s1 ? seg.bias[1] : seg.bias[2]);
+        o_stride = s0 ? seg.stride[0] : (s1 ? seg.stride[1] : seg.stride[2]);
+        o_col = b_row = n - sb;
+    }
+    if (b_ptr) acc += (double)__ldg(b_ptr + b_row);
+    const size_t o = (size_t)m * o_stride + o_col;
+    o_ptr[o] = residual ? residual[o] + (float)acc : (float)acc;
 }
 
 // Splits of the reduction axis: the count that minimises the modelled time waves(s) * (blocks
@@ -503,8 +527,14 @@ static EncodeTiledFn encode_tiled() {
 
 cudaError_t launch_gemm_tc(int bits, const float* x, uint32_t ld, const QW& w, const uint8_t* codes8, const float* bias,
                            float* out, uint32_t m, uint32_t out_stride, uint32_t out_offset, uint8_t* workspace,
-                           uint32_t* err, cudaStream_t st, bool limbs_ready, const float* residual) {
+                           uint32_t* err, cudaStream_t st, bool limbs_ready, const float* residual, const TcSeg* segp) {
     const uint32_t groups = (m + kTcTokens - 1) / kTcTokens, nb = w.cols / kBlock;
+    TcSeg seg{};
+    if (segp) {
+        if (residual || segp->n == 0 || segp->n > 3 || segp->end[segp->n - 1] != w.rows) return cudaErrorInvalidValue;
+        seg = *segp;
+        for (uint32_t s2 = seg.n; s2 < 3; ++s2) seg.end[s2] = w.rows;
+    }
     cudaError_t e;
     if (bits == 8) {
         codes8 = reinterpret_cast<const uint8_t*>(w.packed);  // int8 codes are the byte matrix already
@@ -555,18 +585,18 @@ cudaError_t launch_gemm_tc(int bits, const float* x, uint32_t ld, const QW& w, c
         e = cudaFuncSetAttribute(k_gemm_tc<4>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
         if (e == cudaSuccess)
             e = cudaLaunchKernelEx(&cfg, k_gemm_tc<4>, cmap, (const uint8_t*)workspace, w, bias, out, partial, m,
-                                   out_stride, out_offset, per, err, residual);
+                                   out_stride, out_offset, per, err, residual, seg);
     } else {
         e = cudaFuncSetAttribute(k_gemm_tc<8>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
         if (e == cudaSuccess)
             e = cudaLaunchKernelEx(&cfg, k_gemm_tc<8>, cmap, (const uint8_t*)workspace, w, bias, out, partial, m,
-                                   out_stride, out_offset, per, err, residual);
+                                   out_stride, out_offset, per, err, residual, seg);
     }
     if (e == cudaSuccess) e = cudaGetLastError();
     if (e != cudaSuccess || splits == 1) return e;
     const size_t total = (size_t)m * w.rows;
     k_gemm_tc_combine<<<(unsigned)((total + 255) / 256), 256, 0, st>>>(partial, splits, m, w.rows, bias, out, out_stride,
-                                                                       out_offset, residual);
+                                                                       out_offset, residual, seg);
     return cudaGetLastError();
 }
 

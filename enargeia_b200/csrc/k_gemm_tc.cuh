@@ -20,6 +20,16 @@ size_t gemm_tc_codes_bytes(uint32_t rows, uint32_t k);
 // reuse it.
 cudaError_t launch_codes_i8(const QW& w, uint8_t* out, cudaStream_t st);
 
+// Output segments of a GEMM over stacked int4 weights (q|k|v, gate|up): rows [end[s-1], end[s]) of w
+// (end[-1] = 0) go to out[s][t * stride[s] + row - end[s-1]] with bias[s] (may be null).
+struct TcSeg {
+    float* out[3];
+    const float* bias[3];
+    uint32_t stride[3];
+    uint32_t end[3];
+    uint32_t n;  // 0: the single output of launch_gemm_tc's out / bias / out_stride / out_offset
+};
+
 // out[t * out_stride + out_offset + n] = float(x[t] . W[n] (+ bias[n])) for t < m, n < w.rows;
 // x rows ld floats apart.  bits 4 or 8; w.cols a multiple of 64.  codes8: the prepared int4 byte
 // matrix, or null to convert into the workspace (which then needs gemm_tc_codes_bytes more).
@@ -28,7 +38,8 @@ cudaError_t launch_codes_i8(const QW& w, uint8_t* out, cudaStream_t st);
 // residual: added in float to each rounded output (same layout as out; may be out itself).
 cudaError_t launch_gemm_tc(int bits, const float* x, uint32_t ld, const QW& w, const uint8_t* codes8, const float* bias,
                            float* out, uint32_t m, uint32_t out_stride, uint32_t out_offset, uint8_t* workspace,
-                           uint32_t* err, cudaStream_t st, bool limbs_ready = false, const float* residual = nullptr);
+                           uint32_t* err, cudaStream_t st, bool limbs_ready = false, const float* residual = nullptr,
+                           const TcSeg* seg = nullptr);
 
 // The tied int8 head for 1-4 tokens on the tensor cores (exact limbs, like launch_gemm_tc):
 // out[t * out_stride + row] = float(x_t . W[row]) for row < w.rows, t < ntok; with `gain`, x is
