@@ -531,7 +531,9 @@ cudaError_t launch_gemm_tc(int bits, const float* x, uint32_t ld, const QW& w, c
     const uint32_t groups = (m + kTcTokens - 1) / kTcTokens, nb = w.cols / kBlock;
     TcSeg seg{};
     if (segp) {
-        if (residual || segp->n == 0 || segp->n > 3 || segp->end[segp->n - 1] != w.rows) return cudaErrorInvalidValue;
+        // segments: int4 stacks only (the int8 kernel writes the single output), no residual
+        if (bits != 4 || residual || segp->n == 0 || segp->n > 3 || segp->end[segp->n - 1] != w.rows)
+            return cudaErrorInvalidValue;
         seg = *segp;
         for (uint32_t s2 = seg.n; s2 < 3; ++s2) seg.end[s2] = w.rows;
     }
