@@ -188,43 +188,15 @@ class Model:
     def stage_times(self) -> dict:
         """Per-stage device times (us) of the last traced step, summed over layers: how long each
         stage waited for its barrier+weights and how long it computed (kernel-group telemetry of
-        src/runtime/telemetry.ts, at stage granularity)."""
+        src/runtime/telemetry.ts, at stage granularity; telemetry.parse_stage_trace)."""
+        from .telemetry import parse_stage_trace, trace_words
+
         L = self.config.layers
-        n = 3 * (3 * L + 1) + 14 * L + 2
+        n = trace_words(L)
         buf = np.zeros(n, dtype=np.uint64)
         cnt = C.c_uint32()
         call("enx_trace", self._h, buf.ctypes.data, n, C.byref(cnt))
-        t = buf[: 3 * (3 * L + 1)].astype(np.float64).reshape(-1, 3) / 1e3
-        names = ["attn", "gate_up", "down"]
-        out = {f"{k}_{p}": 0.0 for k in names for p in ("wait", "weights", "compute")}
-        for i in range(3 * L):
-            k = names[i % 3]
-            prev_done = t[i - 1, 2] if i > 0 else t[i, 0]
-            out[f"{k}_wait"] += t[i, 0] - prev_done          # barrier after the previous stage
-            out[f"{k}_weights"] += max(t[i, 1] - t[i, 0], 0.0)  # includes the activation loads/norm
-            out[f"{k}_compute"] += t[i, 2] - t[i, 1]
-        out["head_wait"] = t[3 * L, 0] - t[3 * L - 1, 2]
-        out["head"] = t[3 * L, 2] - t[3 * L, 0]
-        out["total"] = t[3 * L, 2] - t[0, 0]
-        # inside the attention stage (first CTA): weights + norm, q|k|v units, wait for the kv
-        # head's units, q and current k/v loads, attention, wait for every head, o rows
-        d = buf[3 * (3 * L + 1):3 * (3 * L + 1) + 14 * L].astype(np.float64).reshape(L, 14) / 1e3
-        if d.any():
-            marks = ["norm", "units", "ready_wait", "q_load", "attention", "done_wait", "o_rows+end"]
-            d = d[:, :6]
-            starts = t[0:3 * L:3, 0]
-            ends = t[0:3 * L:3, 2]
-            seq = np.concatenate([starts[:, None], d, ends[:, None]], axis=1)
-            for j, m in enumerate(marks):
-                out[f"attn.{m}"] = float(np.sum(seq[:, j + 1] - seq[:, j]))
-            full = buf[3 * (3 * L + 1):3 * (3 * L + 1) + 14 * L].astype(np.float64).reshape(L, 14)[1:] / 1e3
-            t1 = t[3:3 * L:3, 1]
-            out["norm.loads"] = float(np.sum(full[:, 6] - t1))
-            out["norm.rs"] = float(np.sum(full[:, 7] - full[:, 6]))
-            out["norm.stage"] = float(np.sum(full[:, 0] - full[:, 7]))
-            out["head.wait"] = float(buf[-2]) / 1e3
-            out["head.compute"] = float(buf[-1]) / 1e3
-        return out
+        return parse_stage_trace(buf, L)
 
     def stream_handle(self) -> int:
         s = C.c_void_p()
