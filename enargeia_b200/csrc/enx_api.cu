@@ -462,6 +462,7 @@ struct enx_ctx {
     cudaGraphExec_t graph[kMaxStepBatch + 1] = {};
     uint32_t graph_launches[kMaxStepBatch + 1] = {};
     cudaGraphExec_t loop_graph[kMaxStepBatch + 1] = {};
+    cudaGraphExec_t loop_graph_n[kMaxStepBatch + 1] = {};  // kLoopGraphSteps loop steps in one graph
     uint32_t loop_launches[kMaxStepBatch + 1] = {};
     LoopState* d_loop = nullptr;
     LoopState* h_loop = nullptr;
@@ -555,6 +556,10 @@ void free_graphs(enx_ctx* c) {
         g = nullptr;
     }
     for (auto& g : c->loop_graph) {
+        if (g) cudaGraphExecDestroy(g);
+        g = nullptr;
+    }
+    for (auto& g : c->loop_graph_n) {
         if (g) cudaGraphExecDestroy(g);
         g = nullptr;
     }
@@ -1512,7 +1517,13 @@ static cudaError_t launch_step_head(enx_ctx* c, uint32_t B, const StepArgs& S, c
     return launch_head(B, c->head.bits, c->head, S, st);
 }
 
-static enx_status capture_step(enx_ctx* c, uint32_t B, bool loop) {
+// Decode-loop steps per graph launch (the rest of a loop runs one-step graphs): consecutive steps
+// inside one graph start without a graph launch between them.
+constexpr uint32_t kLoopGraphSteps = 8;
+
+// Captures the decode step of B sequences (loop: the device-fed loop step) as a CUDA graph; reps
+// loop steps one after another in one graph when reps > 1.
+static enx_status capture_step(enx_ctx* c, uint32_t B, bool loop, uint32_t reps = 1) {
     cudaStream_t st = c->stream;
     StepArgs S = step_args(c);
     S.pos = c->d_step->pos;
@@ -1523,40 +1534,42 @@ static enx_status capture_step(enx_ctx* c, uint32_t B, bool loop) {
     const bool mega = mega_eligible(c, B, S, A, geo);
     ENX_CUDA(cudaStreamBeginCapture(st, cudaStreamCaptureModeThreadLocal));
     cudaError_t e = cudaSuccess;
-    if (loop) {
-        k_loop_prep<<<1, 32, 0, st>>>(c->d_loop, c->d_step, c->d_loop_rand, c->d_loop_ids, c->history, c->max_ctx, B,
-                                      c->d_bar);
-        e = cudaGetLastError();
-    } else {
-        e = cudaMemcpyAsync(c->d_step, c->h_step, in_bytes, cudaMemcpyHostToDevice, st);
-        if (e == cudaSuccess) {
-            k_step_prep<<<1, 32, 0, st>>>(c->d_step, c->history, c->max_ctx, B, c->d_bar);
-            e = cudaGetLastError();
-        }
-    }
-    if (e == cudaSuccess) {
-        if (mega) {
-            e = launch_mega(B, A, geo, st);  // the prep kernel above bumped the tag epoch
-            if (e == cudaSuccess) e = launch_step_head(c, B, S, st);
-        } else {
-            e = launch_embed(c->d_step->tokens, c->head.embed, c->head.bits, c->x, B, 0, c->cfg.vocab, c->cfg.hidden,
-                             st, true);
-            for (uint32_t l = 0; l < c->cfg.layers && e == cudaSuccess; ++l) e = launch_layer(B, c->layers[l], S, st);
-            if (e == cudaSuccess) e = launch_head(B, c->head.bits, c->head, S, st);
-        }
-    }
-    (loop ? c->loop_mega : c->graph_mega)[B] = mega;
-    if (e == cudaSuccess)
-        e = launch_sample(c->logits, c->cfg.vocab, B, c->history, c->max_ctx, c->d_step->hist_len, c->d_step->rows,
-                          false, SampleRow{}, c->d_step->out, st, true);
-    if (e == cudaSuccess) {
+    for (uint32_t rep = 0; rep < (loop ? reps : 1u) && e == cudaSuccess; ++rep) {
         if (loop) {
-            k_loop_post<<<1, 32, 0, st>>>(c->d_loop, c->d_step, c->d_loop_ids, B);
+            k_loop_prep<<<1, 32, 0, st>>>(c->d_loop, c->d_step, c->d_loop_rand, c->d_loop_ids, c->history, c->max_ctx, B,
+                                          c->d_bar);
             e = cudaGetLastError();
         } else {
-            // the ids and the sticky error word travel back together
-            e = cudaMemcpyAsync(c->h_step->out, c->d_step->out, sizeof(StepBlock) - offsetof(StepBlock, out),
-                                cudaMemcpyDeviceToHost, st);
+            e = cudaMemcpyAsync(c->d_step, c->h_step, in_bytes, cudaMemcpyHostToDevice, st);
+            if (e == cudaSuccess) {
+                k_step_prep<<<1, 32, 0, st>>>(c->d_step, c->history, c->max_ctx, B, c->d_bar);
+                e = cudaGetLastError();
+            }
+        }
+        if (e == cudaSuccess) {
+            if (mega) {
+                e = launch_mega(B, A, geo, st);  // the prep kernel above bumped the tag epoch
+                if (e == cudaSuccess) e = launch_step_head(c, B, S, st);
+            } else {
+                e = launch_embed(c->d_step->tokens, c->head.embed, c->head.bits, c->x, B, 0, c->cfg.vocab, c->cfg.hidden,
+                                 st, true);
+                for (uint32_t l = 0; l < c->cfg.layers && e == cudaSuccess; ++l) e = launch_layer(B, c->layers[l], S, st);
+                if (e == cudaSuccess) e = launch_head(B, c->head.bits, c->head, S, st);
+            }
+        }
+        (loop ? c->loop_mega : c->graph_mega)[B] = mega;
+        if (e == cudaSuccess)
+            e = launch_sample(c->logits, c->cfg.vocab, B, c->history, c->max_ctx, c->d_step->hist_len, c->d_step->rows,
+                              false, SampleRow{}, c->d_step->out, st, true);
+        if (e == cudaSuccess) {
+            if (loop) {
+                k_loop_post<<<1, 32, 0, st>>>(c->d_loop, c->d_step, c->d_loop_ids, B);
+                e = cudaGetLastError();
+            } else {
+                // the ids and the sticky error word travel back together
+                e = cudaMemcpyAsync(c->h_step->out, c->d_step->out, sizeof(StepBlock) - offsetof(StepBlock, out),
+                                    cudaMemcpyDeviceToHost, st);
+            }
         }
     }
     cudaGraph_t graph = nullptr;
@@ -1580,6 +1593,10 @@ static enx_status capture_step(enx_ctx* c, uint32_t B, bool loop) {
     e = cudaGraphInstantiate(&exec, graph, 0);
     cudaGraphDestroy(graph);
     if (e != cudaSuccess) return cuda_fail(e, "cudaGraphInstantiate(decode step)");
+    if (loop && reps > 1) {
+        c->loop_graph_n[B] = exec;
+        return ENX_OK;
+    }
     (loop ? c->loop_graph : c->graph)[B] = exec;
     (loop ? c->loop_launches : c->graph_launches)[B] = kernels;
     return ENX_OK;
@@ -1650,6 +1667,7 @@ extern "C" enx_status enx_decode_loop(enx_ctx* c, uint32_t batch, const uint32_t
     if (batch > kMaxStepBatch)
         return decode_batch_loop(c, batch, first_tokens, params, params_count, steps, randoms, out_ids, sync);
     if (!c->loop_graph[batch]) ENX_TRY(capture_step(c, batch, true));
+    if (steps >= kLoopGraphSteps && !c->loop_graph_n[batch]) ENX_TRY(capture_step(c, batch, true, kLoopGraphSteps));
     ENX_CUDA(cudaStreamSynchronize(c->stream));  // the pinned loop state may still be in flight
     LoopState* L = c->h_loop;
     L->i = 0;
@@ -1661,7 +1679,10 @@ extern "C" enx_status enx_decode_loop(enx_ctx* c, uint32_t batch, const uint32_t
     }
     ENX_CUDA(cudaMemcpyAsync(c->d_loop, L, sizeof(LoopState), cudaMemcpyHostToDevice, c->stream));
     ENX_CUDA(cudaMemcpyAsync(c->d_loop_rand, randoms, (size_t)steps * batch * 4, cudaMemcpyHostToDevice, c->stream));
-    for (uint32_t i = 0; i < steps; ++i) ENX_CUDA(cudaGraphLaunch(c->loop_graph[batch], c->stream));
+    uint32_t i = 0;
+    for (; i + kLoopGraphSteps <= steps && c->loop_graph_n[batch]; i += kLoopGraphSteps)
+        ENX_CUDA(cudaGraphLaunch(c->loop_graph_n[batch], c->stream));
+    for (; i < steps; ++i) ENX_CUDA(cudaGraphLaunch(c->loop_graph[batch], c->stream));
     ENX_CUDA(cudaMemcpyAsync(c->h_loop_ids, c->d_loop_ids, (size_t)steps * batch * 4, cudaMemcpyDeviceToHost,
                              c->stream));
     for (uint32_t b = 0; b < batch; ++b) c->filled[b] += steps;
